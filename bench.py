@@ -1,0 +1,451 @@
+#!/usr/bin/env python3
+"""Decode throughput of WEX4 expert records into HBM on B200 (decoded GB/s and experts/s).
+
+Workload (default "mid"): MoE experts of hidden 2048 and expert FFN 768 (gate/up [768 x 2048], down
+[2048 x 768] in MXFP4: E2M1 nibbles packed two per byte, one E8M0 scale per 32), 48 layers x 128
+experts, per-layer sigma drawn from U(0.01, 0.04), encoded as WNR3 byte-exact records (chunks
+2048:512) under one WNM2 model. A step is one token of routed decode: for each of the 48 layers a
+batch of 8 distinct experts drawn from a Zipf(1.1) popularity over that layer's experts (seeded),
+i.e. 384 expert records and 962 MB of decoded slabs. Inputs are seeded synthetic data (no dataset is
+involved) and larger than L2 between steps.
+
+  value  records resident in HBM (wexb_resident_*), the step's 384 records decoded by one queued
+         decode (3 kernel launches), timed with CUDA events on the launching stream
+  e2e    the reference-facing drop-in: per layer one wex_cuda_decode_batch_to_device call of 8
+         records from pinned host memory (H2D inside the timed region, statuses read back), 48 calls
+         a step, timed by the host clock around the synchronous calls (max over ranks)
+
+N GPUs (torchrun): expert-parallel placement, rank r decodes the experts whose id = r mod N (weak
+scaling: 384 records per rank per step); the only collectives are the max-over-ranks timing and a
+final gather of per-rank outcome counters.
+
+--impl reference: the reference's own CPU decoder (wex_nr2_decode via its wex_nr3_decode tool,
+compiled from its sources into oracle/_ref) on all host cores, one record per core, on a bounded
+sample of the same records.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, 'wex-wrn2_b200'))
+
+CONFIGS = {
+    'tiny': dict(hidden=1024, ffn=512, layers=1, experts=8, batch=8, cz=False, sigma=(0.02, 0.02), neg_zero=0.0),
+    'mid': dict(hidden=2048, ffn=768, layers=48, experts=128, batch=8, cz=False, sigma=(0.01, 0.04), neg_zero=0.0),
+    'large': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03),
+}
+SEED = 20261201
+MEASURED_PEAKS = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---- workload -------------------------------------------------------------------------------------
+def layer_sigmas(cfg):
+    rng = np.random.default_rng(SEED)
+    lo, hi = cfg['sigma']
+    return rng.uniform(lo, hi, cfg['layers'])
+
+
+def routing_trace(cfg, steps, rank, world, layers):
+    """[step][layer] -> 8 distinct expert ids of this rank's shard (id % world == rank), Zipf(1.1)."""
+    shard = np.arange(rank, cfg['experts'], world)
+    trace = []
+    for layer in range(layers):
+        rng = np.random.default_rng([SEED, layer, rank])
+        order = rng.permutation(shard)                         # popularity rank of each expert
+        p = 1.0 / np.arange(1, len(order) + 1) ** 1.1
+        p /= p.sum()
+        k = min(cfg['batch'], len(order))
+        trace.append([list(rng.choice(order, size=k, replace=False, p=p)) for _ in range(steps)])
+    return [[trace[l][s] for l in range(layers)] for s in range(steps)]
+
+
+def build_pool(cfg, owners, threads):
+    """WNM2 model (trained on one fixed expert per layer, the same on every rank) and the records."""
+    import synth
+    sig = layer_sigmas(cfg)
+    train = [(l, l % cfg['experts']) for l in range(cfg['layers'])]
+    blob, _ = synth.make_experts(cfg['hidden'], cfg['ffn'], train, seed=SEED, sigma=lambda l: sig[l], cz=cfg['cz'],
+                                 neg_zero=cfg['neg_zero'], train_every=1, threads=threads)
+    _, experts = synth.make_experts(cfg['hidden'], cfg['ffn'], owners, seed=SEED, sigma=lambda l: sig[l], cz=cfg['cz'],
+                                    neg_zero=cfg['neg_zero'], threads=threads, blob=blob)
+    return blob, experts
+
+
+def pinned_records(experts):
+    """All records in one page-locked host buffer; returns (buffer, views)."""
+    import wexcuda
+    total = sum(len(e.record) for e in experts)
+    buf = np.empty(total, np.uint8)
+    views, at = [], 0
+    for e in experts:
+        n = len(e.record)
+        buf[at:at + n] = np.frombuffer(e.record, np.uint8)
+        views.append(buf[at:at + n])
+        at += n
+    assert wexcuda.host_register(buf) == 0
+    return buf, views
+
+
+# ---- clocks -------------------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi samples (200 ms) of this rank's GPU during the timed regions."""
+    FIELDS = 'index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,' \
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,' \
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap'
+
+    def __init__(self, gpu):
+        self.gpu, self.proc, self.lines = gpu, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.gpu), f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=lambda: self.lines.extend(self.proc.stdout), daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.reader.join(timeout=5)
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.lines:
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(n)
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ---- distributed plumbing ----------------------------------------------------------------------------
+def dist_init():
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=600))
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(vals, world):
+    if world == 1:
+        return vals
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(v) for v in t.tolist()]
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---- CPU decoder of the reference (the baseline / the reference arm) -------------------------------
+def reference_decode_rate(experts, blob, cores, min_seconds=10.0, max_records=None):
+    """Decode records with the reference's CPU decoder (oracle/_ref/wex_nr3_tools.so: wex_nr3_decode ->
+    wex_decode_nr2_record -> wex_nr2_decode), one record per host thread, until min_seconds of work.
+    Returns (seconds, records decoded, decoded bytes, kind, sample description)."""
+    sys.path.insert(0, os.path.join(ROOT, 'oracle'))
+    import ctypes
+    import oracle
+    L = oracle.ref_lib('wex_nr3_tools')
+    if L is None:
+        raise RuntimeError('oracle/_ref/wex_nr3_tools.so is missing: build it with `make -C oracle ref`')
+    sample = [e for e in experts if e.codec == 5][: (max_records or len(experts))]
+    outs = [ctypes.create_string_buffer(len(e.source)) for e in sample]
+
+    def one(i):
+        e = sample[i % len(sample)]
+        st = L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, outs[i % len(sample)])
+        if st != 0:
+            raise RuntimeError('reference decoder refused a record')
+        return len(e.source)
+    with ThreadPoolExecutor(cores) as pool:
+        t0 = time.perf_counter()
+        done, nbytes, n = 0, 0, 0
+        while True:
+            batch = list(pool.map(one, range(n, n + cores)))
+            n += cores
+            nbytes += sum(batch)
+            done = n
+            if time.perf_counter() - t0 >= min_seconds:
+                break
+        dt = time.perf_counter() - t0
+    return dt, done, nbytes
+
+
+# ---- the two arms ---------------------------------------------------------------------------------
+def run_reference(args, cfg):
+    world, rank, local = int(os.environ.get('WORLD_SIZE', '1')), int(os.environ.get('RANK', '0')), 0
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    layers = args.layers or cfg['layers']
+    trace = routing_trace(cfg, args.warmup + args.steps, 0, 1, layers)
+    # one step of the reference arm: ceil(cores / 8) layer batches of the trace (bounded sample)
+    per_step = max(1, min(layers, -(-cores // cfg['batch'])))
+    owners = []
+    for s in range(args.warmup + args.steps):
+        for l in range(per_step):
+            for e in trace[s][(s * per_step + l) % layers]:
+                if ((s * per_step + l) % layers, int(e)) not in owners:
+                    owners.append(((s * per_step + l) % layers, int(e)))
+    blob, experts = build_pool(cfg, owners, threads=cores)
+    by_owner = {(e.layer, e.index): e for e in experts}
+    sys.path.insert(0, os.path.join(ROOT, 'oracle'))
+    import ctypes
+    import oracle
+    L = oracle.ref_lib('wex_nr3_tools')
+    if L is None:
+        print(json.dumps({'impl': 'reference', 'unavailable': 'oracle/_ref/wex_nr3_tools.so was not built'}))
+        return 0
+
+    def one(e):
+        out = ctypes.create_string_buffer(len(e.source))
+        if L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, out) != 0:
+            raise RuntimeError('reference decoder refused a record')
+        return len(e.source)
+    times, nbytes, nrec = [], 0, 0
+    with ThreadPoolExecutor(cores) as pool:
+        for s in range(args.warmup + args.steps):
+            recs = [by_owner[((s * per_step + l) % layers, int(e))] for l in range(per_step)
+                    for e in trace[s][(s * per_step + l) % layers]]
+            t0 = time.perf_counter()
+            b = sum(pool.map(one, recs))
+            dt = time.perf_counter() - t0
+            if s >= args.warmup:
+                times.append(dt); nbytes += b; nrec += len(recs)
+    total = sum(times)
+    value = nbytes / total / 1e9
+    line = {
+        'impl': 'reference', 'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 4), 'unit': 'GB/s',
+        'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(1e3 * total / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'experts_per_s': round(nrec / total, 2),
+        'config': config_desc(args, cfg),
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
+                         'sample': f'{per_step} layer batch(es) of {cfg["batch"]} records per step, one record per '
+                                   f'host thread, reference wex_nr2_decode'},
+        'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def config_desc(args, cfg):
+    return {'workload': f'{args.config}: routed decode of WNR3 MXFP4 experts, hidden {cfg["hidden"]}, expert FFN '
+                        f'{cfg["ffn"]}, {args.layers or cfg["layers"]} layers x {cfg["experts"]} experts, top-'
+                        f'{cfg["batch"]} Zipf(1.1) per layer per step' + (', canonical zero' if cfg['cz'] else ''),
+            'records_per_step_per_gpu': (args.layers or cfg['layers']) * cfg['batch'],
+            'chunks': '2048:512', 'placement': 'expert id mod world size',
+            'l2': 'inputs larger than L2 (126 MB) between steps'}
+
+
+def run_gpu(args, cfg):
+    import torch
+    import wexcuda
+    world, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    dev = local
+    layers = args.layers or cfg['layers']
+    steps_total = args.warmup + args.steps
+    trace = routing_trace(cfg, steps_total, rank, world, layers)
+    owners = sorted({(l, int(e)) for s in range(steps_total) for l in range(layers) for e in trace[s][l]})
+    threads = max(1, (os.cpu_count() or 8) // max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world))))
+    t0 = time.time()
+    blob, experts = build_pool(cfg, owners, threads)
+    log(f'[rank {rank}] {len(experts)} experts generated and encoded in {time.time() - t0:.1f} s')
+    assert all(e.codec == 5 for e in experts), 'every synthetic expert compresses'
+    index = {(e.layer, e.index): i for i, e in enumerate(experts)}
+    assert wexcuda.register_model(blob) == 0
+    hostbuf, views = pinned_records(experts)
+    raw = len(experts[0].source)
+    k = layers * cfg['batch']
+    # destinations of one step: 384 experts' six regions
+    sizes = [r * c // 32 for r, c in [(cfg['ffn'], cfg['hidden']), (cfg['hidden'], cfg['ffn']), (cfg['ffn'], cfg['hidden'])]]
+    dst = torch.empty((k, raw), dtype=torch.uint8, device='cuda')
+    base = dst.data_ptr()
+    soffs = [0, sizes[0], sizes[0] + sizes[1]]
+    woffs = [sum(sizes) + 16 * x for x in soffs]
+    dscale = [base + j * raw + soffs[m] for j in range(k) for m in range(3)]
+    dweight = [base + j * raw + woffs[m] for j in range(k) for m in range(3)]
+    step_idx = [[index[(l, int(e))] for l in range(layers) for e in trace[s][l]] for s in range(steps_total)]
+
+    # ---- value: resident records, one decode per step --------------------------------------------
+    res = wexcuda.Resident([e.entry for e in experts], views, dev)
+    assert res.failures == 0
+    res.profile(True)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    kernel_ms, launches = [], 0
+    for s in range(args.warmup):
+        assert res.decode(step_idx[s], dscale, dweight, sh) == 0
+        bad, st = res.wait()
+        assert bad == 0, st
+    clocks = Clocks(dev)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for s in range(args.warmup, steps_total):
+        assert res.decode(step_idx[s], dscale, dweight, sh) == 0
+        bad, st = res.wait()
+        assert bad == 0, st
+        kernel_ms.append(res.kernel_ms())
+        launches += res.launches()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    value_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    # bit-exact check of the last step's slabs (8 sampled records)
+    last = step_idx[steps_total - 1]
+    check = list(range(0, k, max(1, k // 8)))[:8]
+    got = dst[check].cpu().numpy()
+    verified = sum(int(got[i].tobytes() == experts[last[j]].expected) for i, j in enumerate(check))
+    assert verified == len(check), 'decoded bytes differ from the source'
+
+    # ---- e2e: the drop-in batch call, 8 records per layer, from pinned host memory ----------------
+    def e2e_step(s):
+        ids = step_idx[s]
+        bad_total = 0
+        for l in range(layers):
+            sel = ids[l * cfg['batch']:(l + 1) * cfg['batch']]
+            bad, st = wexcuda.decode_batch_to_device([experts[i].entry for i in sel], [views[i] for i in sel], dev,
+                                                     dscale[3 * l * cfg['batch']:3 * (l + 1) * cfg['batch']],
+                                                     dweight[3 * l * cfg['batch']:3 * (l + 1) * cfg['batch']])
+            bad_total += bad
+        return bad_total
+    for s in range(args.warmup):
+        assert e2e_step(s) == 0
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s in range(args.warmup, steps_total):
+        assert e2e_step(s) == 0
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    barrier(world)
+    clk = clocks.stop()
+    got = dst[check].cpu().numpy()
+    assert all(got[i].tobytes() == experts[last[j]].expected for i, j in enumerate(check))
+
+    # ---- bytes ----------------------------------------------------------------------------------
+    dec_bytes = sum(len(experts[i].source) for s in range(args.warmup, steps_total) for i in step_idx[s])
+    stored = sum(len(experts[i].record) for s in range(args.warmup, steps_total) for i in step_idx[s])
+    wpay = sum(int.from_bytes(experts[i].record[12:16], 'little') for s in range(args.warmup, steps_total)
+               for i in step_idx[s])
+    wbytes = sum(int.from_bytes(experts[i].entry[16:20], 'little') + int.from_bytes(experts[i].entry[12:16], 'little')
+                 for s in range(args.warmup, steps_total) for i in step_idx[s])
+    totals = sum_over_ranks([dec_bytes, stored, k * args.steps], world)
+    dec_all, stored_all, recs_all = totals
+    value = dec_all / (value_ms / 1e3) / 1e9
+    e2e = dec_all / e2e_s / 1e9
+    # roofline of the dominant kernel (weights): algorithmic bytes = weight payload read + packed
+    # weights written + scales read for the contexts, per launch, over its event-timed duration
+    wk = [m[1] for m in kernel_ms if m]
+    wk_ms = statistics.mean(wk) if wk else None
+    alg = (wpay + wbytes) / args.steps
+    peaks = json.load(open(MEASURED_PEAKS)) if os.path.exists(MEASURED_PEAKS) else {}
+    hbm_peak = peaks.get('hbm_gbs', 6650.0)
+    achieved = alg / (wk_ms / 1e3) / 1e9 if wk_ms else None
+    h2d_per_step = stored // args.steps + 0
+    line = {
+        'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 3), 'unit': 'GB/s', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(value_ms / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'experts_per_s': round(recs_all / (value_ms / 1e3), 1),
+        'config': config_desc(args, cfg),
+        'e2e': {'value': round(e2e, 3), 'unit': 'GB/s', 'experts_per_s': round(recs_all / e2e_s, 1),
+                'h2d_bytes_per_step': int(h2d_per_step), 'd2h_bytes_per_step': 4 * k,
+                'api': 'wex_cuda_decode_batch_to_device, 8 records per call, 48 calls per step',
+                'ms_per_step': round(1e3 * e2e_s / args.steps, 3)},
+        'roofline': {'bound': 'hbm', 'kernel': 'nr3_weights', 'achieved': round(achieved, 2) if achieved else None,
+                     'peak': hbm_peak, 'unit': 'GB/s', 'frac': round(achieved / hbm_peak, 5) if achieved else None,
+                     'peak_source': 'measured' if peaks else 'fallback', 'traffic': None,
+                     'kernel_ms': round(wk_ms, 4) if wk_ms else None,
+                     'alg_bytes_per_launch': int(alg),
+                     'step_kernel_ms': [round(statistics.mean(m[i] for m in kernel_ms if m), 4) for i in range(3)]},
+        'gpu_launches': launches,
+        'clocks': clk,
+        'verified_records': verified,
+        'stored_over_decoded': round(stored / dec_bytes, 4),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        dt, n, nb = reference_decode_rate(experts, blob, cores, min_seconds=args.cpu_seconds)
+        line['cpu_baseline'] = {'value': round(nb / dt / 1e9, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
+                                'experts_per_s': round(n / dt, 2),
+                                'sample': f'{n} records of the same pool, one per host thread, reference '
+                                          f'wex_nr2_decode, {dt:.1f} s'}
+    res.close()
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=5)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', choices=['wexb', 'reference'], default='wexb')
+    ap.add_argument('--config', choices=sorted(CONFIGS), default='mid')
+    ap.add_argument('--layers', type=int, default=0, help='layers per step (default: all of the config)')
+    ap.add_argument('--cpu-seconds', type=float, default=12.0)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    assert args.warmup >= 1
+    cfg = CONFIGS[args.config]
+    if args.impl == 'reference':
+        return run_reference(args, cfg)
+    return run_gpu(args, cfg)
+
+
+if __name__ == '__main__':
+    sys.exit(main())

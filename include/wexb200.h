@@ -1,0 +1,56 @@
+/* B200 additions to the helper ABI. None of these has a counterpart in the reference; they sit beside
+ * the drop-in entry points of wex_cuda_helper.h and use the same status codes (0 ok, 1 unavailable,
+ * -1 invalid) and the same fail-closed destinations.
+ *
+ * Resident records: an engine that keeps compressed experts in HBM uploads and validates them once
+ * (wexb_resident_create) and then decodes any subset straight from device memory into its own
+ * device buffers, asynchronously on its own stream (wexb_resident_decode + wexb_resident_wait).
+ * One decode of a resident set is in flight at a time. */
+#ifndef WEXB_WEXB200_H
+#define WEXB_WEXB200_H
+#include "wex_entry.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library ABI of these additions. */
+unsigned int wexb_abi(void);
+
+typedef struct WexbResident WexbResident;
+
+/* Validate n WNR2/WNR3 records (host memory) and copy them, with their stream offset tables, to
+ * `device`. status[i]: 0 resident, -1 invalid, 1 unavailable (model not registered, CUDA error).
+ * Resident record j is the j-th record whose status is 0. Returns the number of non-zero statuses;
+ * *out is NULL only when no record could be kept. */
+int wexb_resident_create(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
+                         WexbResident **out, int *status);
+/* Device bytes held by a resident set (records, offset tables). */
+size_t wexb_resident_bytes(const WexbResident *r);
+/* Queue the decode of resident records index[0 .. k) on `stream` (a cudaStream_t, NULL = the set's own
+ * stream): record index[j]'s matrix m goes to dst_scale[3j + m] / dst_weight[3j + m] (device), each
+ * written only if that record decoded cleanly. Returns 0 queued, -1 bad arguments (nothing queued),
+ * 1 CUDA error. */
+int wexb_resident_decode(WexbResident *r, int k, const int *index, unsigned char *const *dst_scale,
+                         unsigned char *const *dst_weight, void *stream);
+/* Wait for the queued decode; status[j] of record index[j]: 0 written, -1 failed its checks
+ * (destination untouched), 1 CUDA error. Returns the number of non-zero statuses. */
+int wexb_resident_wait(WexbResident *r, int *status);
+/* 1: bracket each kernel of the following decodes with CUDA events on its stream; 0: stop. Returns 0,
+ * or 1 when the events cannot be created. */
+int wexb_resident_profile(WexbResident *r, int on);
+/* Milliseconds of the scale, weight and commit kernels of the last waited decode (profiling on):
+ * 0, or -1 when there is nothing to report. */
+int wexb_resident_kernel_ms(const WexbResident *r, float *ms3);
+/* Kernel launches of the last queued decode (3: scales, weights, commit). */
+int wexb_resident_launches(const WexbResident *r);
+void wexb_resident_destroy(WexbResident *r);
+
+/* Error bits of the last failed record seen by this process (1 structure, 2 stream hash, 4 ceil form
+ * at scale 0, 8 canonical zero, 16 bounded wait expired); 0 if none failed. */
+unsigned int wexb_last_error_bits(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -41,7 +41,7 @@ def build_tools(verbose=False):
     src = [os.path.join(CSRC, 'tools', 'wexb_tools.c')]
     if _stale(TOOLS_LIB, src):
         os.makedirs(LIB, exist_ok=True)
-        cmd = ['gcc', '-O2', '-Wall', '-Wextra', '-shared', '-fPIC', '-o', TOOLS_LIB] + src + ['-lm']
+        cmd = ['gcc', '-O2', '-Wall', '-Wextra', '-shared', '-fPIC', '-o', TOOLS_LIB] + src + ['-lm', '-lpthread']
         if verbose:
             print(' '.join(cmd))
         subprocess.run(cmd, check=True)

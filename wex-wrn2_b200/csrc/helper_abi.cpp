@@ -1,0 +1,522 @@
+// The CUDA helper C ABI (include/wex_cuda_helper.h) and the resident-record additions
+// (include/wexb200.h), over the sm_100a WNR2/WNR3 kernels.
+//
+// One call = one pipeline on a pooled workspace of the target device: all launch metadata of the
+// call (record descriptors, CTA tasks, commit jobs, error words, stream offsets) goes up in one
+// copy, then every record is uploaded on the copy stream in order; record j's kernels run on lane
+// j % 4 as soon as its upload event fires, so decode overlaps the uploads of the later records.
+// A record's destinations are written by the error-gated commit kernel (device destinations), or
+// copied back after its kernels (host destinations).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "nr3_host.h"
+#include "wex_cuda_helper.h"
+#include "wexb200.h"
+
+#define WEXB_API extern "C" __attribute__((visibility("default")))
+
+namespace wexb {
+namespace {
+
+struct DevBuf {
+    uint8_t *p = nullptr;
+    size_t cap = 0;
+    bool grow(size_t n) {
+        if (n <= cap) return true;
+        if (p) cudaFree(p);
+        p = nullptr; cap = 0;
+        if (cudaMalloc(&p, std::max<size_t>(n, 256)) != cudaSuccess) { (void)cudaGetLastError(); return false; }
+        cap = n;
+        return true;
+    }
+    void release() { if (p) cudaFree(p); p = nullptr; cap = 0; }
+};
+struct PinBuf {
+    uint8_t *p = nullptr;
+    size_t cap = 0;
+    bool grow(size_t n) {
+        if (n <= cap) return true;
+        if (p) cudaFreeHost(p);
+        p = nullptr; cap = 0;
+        if (cudaMallocHost(&p, std::max<size_t>(n, 256)) != cudaSuccess) { (void)cudaGetLastError(); return false; }
+        cap = n;
+        return true;
+    }
+    void release() { if (p) cudaFreeHost(p); p = nullptr; cap = 0; }
+};
+
+constexpr int kLanes = 4;
+
+// A call's device workspace: a copy stream, kLanes kernel streams, grown buffers. Pooled per device and
+// never freed (the reference's pools, c/tools/wex_cuda_bridge.cu:111-153, for the same reason: CUDA
+// cannot be called while the process unloads).
+struct Workspace {
+    int device = -1;
+    cudaStream_t copy = nullptr, lane[kLanes] = {};
+    cudaEvent_t lane_done[kLanes] = {};
+    std::vector<cudaEvent_t> uploaded;
+    DevBuf drec, dscratch, dmeta;
+    PinBuf hmeta;
+    bool init(int dev) {
+        if (cudaStreamCreateWithFlags(&copy, cudaStreamNonBlocking) != cudaSuccess) return false;
+        for (int l = 0; l < kLanes; ++l)
+            if (cudaStreamCreateWithFlags(&lane[l], cudaStreamNonBlocking) != cudaSuccess ||
+                cudaEventCreateWithFlags(&lane_done[l], cudaEventDisableTiming) != cudaSuccess) return false;
+        device = dev;
+        return true;
+    }
+    bool events(size_t n) {
+        while (uploaded.size() < n) {
+            cudaEvent_t e;
+            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
+            uploaded.push_back(e);
+        }
+        return true;
+    }
+};
+
+std::mutex g_pool_mu;
+std::vector<Workspace *> g_idle[kMaxDevices];
+
+Workspace *take(int device) {
+    {
+        std::lock_guard<std::mutex> lock(g_pool_mu);
+        if (!g_idle[device].empty()) { Workspace *w = g_idle[device].back(); g_idle[device].pop_back(); return w; }
+    }
+    Workspace *w = new (std::nothrow) Workspace();
+    if (w && !w->init(device)) { (void)cudaGetLastError(); delete w; w = nullptr; }   // streams leak only on CUDA failure
+    return w;
+}
+void give(Workspace *w) {
+    if (!w) return;
+    std::lock_guard<std::mutex> lock(g_pool_mu);
+    g_idle[w->device].push_back(w);
+}
+struct Lease {
+    Workspace *w;
+    explicit Lease(int device) : w(take(device)) {}
+    ~Lease() { give(w); }
+    Lease(const Lease &) = delete;
+    Lease &operator=(const Lease &) = delete;
+};
+
+// Byte layout of a call's metadata block (host pinned, copied to the device in one piece).
+struct MetaLayout {
+    size_t recs = 0, stasks = 0, wtasks = 0, jobs = 0, errs = 0, offs = 0, total = 0;
+    void compute(size_t k, size_t ns, size_t nw, size_t njobs, size_t noffs) {
+        size_t at = 0;
+        recs = at; at = align_up(at + k * sizeof(Nr3Record), 256);
+        stasks = at; at = align_up(at + ns * sizeof(Nr3Task), 256);
+        wtasks = at; at = align_up(at + nw * sizeof(Nr3Task), 256);
+        jobs = at; at = align_up(at + njobs * sizeof(CommitJob), 256);
+        errs = at; at = align_up(at + k * 4, 256);
+        offs = at; at = align_up(at + noffs * 4, 256);
+        total = at;
+    }
+};
+
+enum class Dest { Device, Host, HostChecked };
+
+// n records (host memory) through the pipeline. dst_scale / dst_weight (Device) or dst_host (Host:
+// copied back after the kernels; HostChecked: copied back only after a clean decode). Follows the
+// reference batch's argument and status rules (c/tools/wex_cuda_bridge.cu:388-487).
+int run_batch(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
+              unsigned char *const *dst_scale, unsigned char *const *dst_weight, unsigned char *const *dst_host,
+              Dest mode, int *status) {
+    if (n <= 0) return 0;
+    const bool host_dst = mode != Dest::Device;
+    if (!entries || !records || !(host_dst ? dst_host != nullptr : (dst_scale && dst_weight)) || !status) return n;
+    const int PENDING = 2;
+    std::vector<Plan> plans((size_t)n);
+    std::vector<int> pend;
+    for (int i = 0; i < n; ++i) {
+        status[i] = -1;
+        const WexEntry *e = entries[i];
+        if (!e || !records[i]) continue;
+        bool targets = host_dst ? dst_host[i] != nullptr : true;
+        if (!host_dst) for (int m = 0; m < 3; ++m) if (!dst_scale[3 * i + m] || !dst_weight[3 * i + m]) targets = false;
+        if (!targets || plan_record(e, records[i], &plans[(size_t)i])) continue;
+        if (!model_registered(plans[(size_t)i].model_id)) { status[i] = 1; continue; }
+        status[i] = PENDING;
+        pend.push_back(i);
+    }
+    auto failures = [&] { int bad = 0; for (int i = 0; i < n; ++i) bad += status[i] != 0; return bad; };
+    auto finish = [&](int v) { for (int i = 0; i < n; ++i) if (status[i] == PENDING) status[i] = v; };
+    if (pend.empty()) return failures();
+    if (device < 0 || device >= kMaxDevices || cudaSetDevice(device) != cudaSuccess) {
+        (void)cudaGetLastError(); finish(1); return failures();
+    }
+    Lease lease(device);
+    Workspace *w = lease.w;
+    if (!w) { finish(1); return failures(); }
+    // device tables of every record's model
+    std::vector<Nr3Tables> tabs(pend.size());
+    {
+        std::vector<int> keep;
+        std::vector<Nr3Tables> kt;
+        for (size_t j = 0; j < pend.size(); ++j) {
+            if (model_tables(plans[(size_t)pend[j]].model_id, device, &tabs[j])) { status[pend[j]] = 1; continue; }
+            keep.push_back(pend[j]); kt.push_back(tabs[j]);
+        }
+        pend.swap(keep); tabs.swap(kt);
+    }
+    const size_t k = pend.size();
+    if (!k) return failures();
+    // layout
+    const int wthreads = weight_threads();
+    std::vector<size_t> rec_off(k), scr_off(k), off_off(k), s0(k + 1), w0(k + 1);
+    std::vector<Nr3Task> stasks, wtasks;
+    size_t rec_bytes = 0, scr_bytes = 0, noffs = 0;
+    for (size_t j = 0; j < k; ++j) {
+        const Plan &p = plans[(size_t)pend[j]];
+        rec_off[j] = rec_bytes; rec_bytes += align_up(p.total, 256);
+        scr_off[j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
+        off_off[j] = noffs; noffs += p.streams() + 1;
+        s0[j] = stasks.size(); w0[j] = wtasks.size();
+        plan_tasks(p, (uint32_t)j, wthreads, stasks, wtasks);
+    }
+    s0[k] = stasks.size(); w0[k] = wtasks.size();
+    MetaLayout L;
+    L.compute(k, stasks.size(), wtasks.size(), host_dst ? 0 : k, noffs);
+    if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total) ||
+        !w->events(k)) {
+        finish(1); return failures();
+    }
+    uint8_t *hm = w->hmeta.p, *dm = w->dmeta.p;
+    Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + L.recs);
+    CommitJob *hjobs = reinterpret_cast<CommitJob *>(hm + L.jobs);
+    uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + L.errs);
+    uint32_t *hoffs = reinterpret_cast<uint32_t *>(hm + L.offs);
+    const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + L.recs);
+    const Nr3Task *dst_tasks = reinterpret_cast<const Nr3Task *>(dm + L.stasks);
+    const Nr3Task *dwt_tasks = reinterpret_cast<const Nr3Task *>(dm + L.wtasks);
+    const CommitJob *djobs = reinterpret_cast<const CommitJob *>(dm + L.jobs);
+    uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + L.errs);
+    std::memcpy(hm + L.stasks, stasks.data(), stasks.size() * sizeof(Nr3Task));
+    std::memcpy(hm + L.wtasks, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
+    for (size_t j = 0; j < k; ++j) {
+        const int i = pend[j];
+        const Plan &p = plans[(size_t)i];
+        uint8_t *scr = w->dscratch.p + scr_off[j];
+        plan_offsets(p, hoffs + off_off[j]);
+        plan_descriptor(p, tabs[j], w->drec.p + rec_off[j], reinterpret_cast<const uint32_t *>(dm + L.offs) + off_off[j],
+                        scr, derrs + j, &hrecs[j]);
+        herrs[j] = 0;
+        if (!host_dst) {
+            CommitJob &J = hjobs[j];
+            for (int m = 0; m < 3; ++m) {
+                J.src[m] = scr + p.soff[m]; J.dst[m] = dst_scale[3 * i + m]; J.bytes[m] = p.dst_bytes[m];
+                J.src[3 + m] = scr + p.wout[m]; J.dst[3 + m] = dst_weight[3 * i + m]; J.bytes[3 + m] = p.dst_bytes[3 + m];
+            }
+            J.error = derrs + j;
+        }
+    }
+    // enqueue
+    size_t broken_at = k;
+    bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, w->copy) == cudaSuccess;
+    for (size_t j = 0; ok && j < k; ++j)
+        ok = cudaMemcpyAsync(w->drec.p + rec_off[j], records[pend[j]], plans[(size_t)pend[j]].total, cudaMemcpyHostToDevice,
+                             w->copy) == cudaSuccess &&
+             cudaEventRecord(w->uploaded[j], w->copy) == cudaSuccess;
+    if (!ok) broken_at = 0;
+    const int lanes = (int)std::min<size_t>(k, kLanes);
+    for (size_t j = 0; j < broken_at; ++j) {
+        const int i = pend[j];
+        const Plan &p = plans[(size_t)i];
+        cudaStream_t st = w->lane[j % kLanes];
+        const uint8_t *scr = w->dscratch.p + scr_off[j];
+        ok = cudaStreamWaitEvent(st, w->uploaded[j], 0) == cudaSuccess &&
+             launch_nr3_scales(drecs, dst_tasks + s0[j], (uint32_t)(s0[j + 1] - s0[j]), st) == cudaSuccess &&
+             launch_nr3_weights(drecs, dwt_tasks + w0[j], (uint32_t)(w0[j + 1] - w0[j]), wthreads, st) == cudaSuccess;
+        if (ok && mode == Dest::Device) ok = launch_commit(djobs + j, 1, st) == cudaSuccess;
+        if (ok && mode == Dest::Host) {
+            ok = cudaMemcpyAsync(dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                 cudaMemcpyAsync(dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost,
+                                 st) == cudaSuccess;
+        }
+        if (!ok) { (void)cudaGetLastError(); broken_at = j; }
+    }
+    bool synced = true;
+    for (int l = 0; l < lanes; ++l)
+        if (cudaEventRecord(w->lane_done[l], w->lane[l]) != cudaSuccess ||
+            cudaStreamWaitEvent(w->copy, w->lane_done[l], 0) != cudaSuccess) synced = false;
+    if (synced && cudaMemcpyAsync(herrs, derrs, k * 4, cudaMemcpyDeviceToHost, w->copy) != cudaSuccess) synced = false;
+    for (int l = 0; l < lanes; ++l) if (cudaStreamSynchronize(w->lane[l]) != cudaSuccess) synced = false;
+    if (cudaStreamSynchronize(w->copy) != cudaSuccess) synced = false;
+    if (!synced) (void)cudaGetLastError();
+    for (size_t j = 0; j < k; ++j) {
+        const int i = pend[j];
+        status[i] = (j >= broken_at || !synced) ? 1 : herrs[j] ? -1 : 0;
+        if (status[i] == -1) report_error_bits(herrs[j]);
+    }
+    if (mode == Dest::HostChecked && synced) {   // the single to-host call: copy back only a clean decode
+        for (size_t j = 0; j < k; ++j) {
+            const int i = pend[j];
+            if (status[i]) continue;
+            const Plan &p = plans[(size_t)i];
+            const uint8_t *scr = w->dscratch.p + scr_off[j];
+            if (cudaMemcpy(dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
+                cudaMemcpy(dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost) != cudaSuccess) {
+                (void)cudaGetLastError();
+                status[i] = 1;   // the slab may now be partly written: the caller treats 1 as "decode again"
+            }
+        }
+    }
+    return failures();
+}
+
+}  // namespace
+}  // namespace wexb
+
+using namespace wexb;
+
+// ---- the helper ABI ----------------------------------------------------------------------------
+WEXB_API unsigned int wex_cuda_helper_abi(void) { return 1u; }
+
+WEXB_API unsigned int wex_cuda_helper_features(void) {
+    return WEX_CUDA_FEATURE_DEVICE | WEX_CUDA_FEATURE_REGISTER | WEX_CUDA_FEATURE_NR2 | WEX_CUDA_FEATURE_BATCH |
+           WEX_CUDA_FEATURE_NR3 | WEX_CUDA_FEATURE_BATCH_HOST;
+}
+
+WEXB_API int wex_cuda_register_model(const unsigned char *blob, size_t bytes) { return model_register(blob, bytes); }
+
+WEXB_API int wex_cuda_decode_to_host(const WexEntry *entry, unsigned char *slab, size_t slab_capacity) {
+    uint64_t raw, aligned;
+    if (!entry || !slab) return -1;
+    if (entry->flags == WEX_ENTRY_NEURAL_RANS) return 1;   // WNR1: legacy codec, not built here
+    if (entry->flags != WEX_ENTRY_NEURAL_RANS2 && entry->flags != WEX_ENTRY_NEURAL_RANS3) return -1;
+    if (entry_raw_sizes(entry, &raw, &aligned) || aligned > slab_capacity || entry->total_bytes >= aligned) return -1;
+    const size_t offset = (size_t)(aligned - entry->total_bytes);   // wex_record_read_offset (c/wex_format.h:161-176)
+    if (offset > slab_capacity || entry->total_bytes > slab_capacity - offset) return -1;
+    const unsigned char *rec = slab + offset;
+    unsigned char *dst = slab;
+    int status = -1, device = 0;   // the caller's current device (c/tools/wex_cuda_bridge.cu:141-142)
+    if (cudaGetDevice(&device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    run_batch(1, &entry, &rec, device, nullptr, nullptr, &dst, Dest::HostChecked, &status);
+    return status;
+}
+
+WEXB_API int wex_cuda_decode_to_device(const WexEntry *entry, const unsigned char *record, int device,
+                                       unsigned char *const *dst_scale, unsigned char *const *dst_weight) {
+    if (!entry || !record || !dst_scale || !dst_weight) return -1;
+    if (entry->flags == WEX_ENTRY_NEURAL_RANS) return 1;
+    int status = -1;
+    run_batch(1, &entry, &record, device, dst_scale, dst_weight, nullptr, Dest::Device, &status);
+    return status;
+}
+
+WEXB_API int wex_cuda_decode_batch_to_device(int n, const WexEntry *const *entries, const unsigned char *const *records,
+                                             int device, unsigned char *const *dst_scale, unsigned char *const *dst_weight,
+                                             int *status) {
+    if (!dst_scale || !dst_weight) return n > 0 ? n : 0;
+    return run_batch(n, entries, records, device, dst_scale, dst_weight, nullptr, Dest::Device, status);
+}
+
+WEXB_API int wex_cuda_decode_batch_to_host(int n, const WexEntry *const *entries, const unsigned char *const *records,
+                                           int device, unsigned char *const *dst, int *status) {
+    if (!dst) return n > 0 ? n : 0;
+    return run_batch(n, entries, records, device, nullptr, nullptr, dst, Dest::Host, status);
+}
+
+WEXB_API int wex_cuda_host_register(void *pointer, size_t bytes) {
+    if (!pointer || !bytes) return -1;
+    if (cudaHostRegister(pointer, bytes, cudaHostRegisterPortable) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    return 0;
+}
+
+WEXB_API int wex_cuda_host_unregister(void *pointer) {
+    if (!pointer) return -1;
+    if (cudaHostUnregister(pointer) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    return 0;
+}
+
+// ---- resident records --------------------------------------------------------------------------
+struct WexbResident {
+    int device = -1;
+    cudaStream_t own = nullptr;
+    cudaEvent_t done = nullptr;
+    std::vector<Plan> plans;          // lengths pointers cleared: the records live on the device
+    std::vector<Nr3Tables> tabs;
+    std::vector<size_t> rec_off, off_off;
+    DevBuf store, dscratch, dmeta;    // store: records, then offset tables
+    PinBuf hmeta;
+    size_t offs_at = 0, bytes = 0;
+    bool queued = false, profiling = false, timed = false;
+    int last_k = 0, launches = 0;
+    cudaEvent_t marks[4] = {};
+    MetaLayout L;
+};
+
+WEXB_API unsigned int wexb_abi(void) { return 1u; }
+
+WEXB_API unsigned int wexb_last_error_bits(void) { return last_error_bits(); }
+
+WEXB_API int wexb_resident_create(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
+                                  WexbResident **out, int *status) {
+    if (!out) return n > 0 ? n : 0;
+    *out = nullptr;
+    if (n <= 0 || !entries || !records || !status) return n > 0 ? n : 0;
+    auto *r = new (std::nothrow) WexbResident();
+    if (!r) { for (int i = 0; i < n; ++i) status[i] = 1; return n; }
+    int bad = 0;
+    const bool dev_ok = device >= 0 && device < kMaxDevices && cudaSetDevice(device) == cudaSuccess;
+    if (!dev_ok) (void)cudaGetLastError();
+    size_t rec_bytes = 0, noffs = 0;
+    std::vector<std::vector<uint32_t>> offs;
+    for (int i = 0; i < n; ++i) {
+        Plan p{};
+        Nr3Tables t{};
+        status[i] = -1;
+        if (!entries[i] || !records[i] || plan_record(entries[i], records[i], &p)) { ++bad; continue; }
+        if (!dev_ok || !model_registered(p.model_id) || model_tables(p.model_id, device, &t)) { status[i] = 1; ++bad; continue; }
+        status[i] = 0;
+        std::vector<uint32_t> o(p.streams() + 1);
+        plan_offsets(p, o.data());
+        offs.push_back(std::move(o));
+        r->rec_off.push_back(rec_bytes); rec_bytes += align_up(p.total, 256);
+        r->off_off.push_back(noffs); noffs += p.streams() + 1;
+        p.lengths = nullptr;
+        r->plans.push_back(p);
+        r->tabs.push_back(t);
+    }
+    if (r->plans.empty()) { delete r; return bad; }
+    r->device = device;
+    r->offs_at = align_up(rec_bytes, 256);
+    r->bytes = r->offs_at + noffs * 4;
+    bool ok = cudaStreamCreateWithFlags(&r->own, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming) == cudaSuccess && r->store.grow(r->bytes);
+    for (int i = 0, j = 0; ok && i < n; ++i) {
+        if (status[i]) continue;
+        ok = cudaMemcpy(r->store.p + r->rec_off[(size_t)j], records[i], r->plans[(size_t)j].total, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(r->store.p + r->offs_at + 4 * r->off_off[(size_t)j], offs[(size_t)j].data(), 4 * offs[(size_t)j].size(),
+                        cudaMemcpyHostToDevice) == cudaSuccess;
+        ++j;
+    }
+    if (!ok) {
+        (void)cudaGetLastError();
+        for (int i = 0; i < n; ++i) if (!status[i]) { status[i] = 1; ++bad; }
+        wexb_resident_destroy(r);
+        return bad;
+    }
+    // resident index j <-> caller index: the j-th record with status 0
+    *out = r;
+    return bad;
+}
+
+WEXB_API size_t wexb_resident_bytes(const WexbResident *r) { return r ? r->bytes : 0; }
+
+WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsigned char *const *dst_scale,
+                                  unsigned char *const *dst_weight, void *stream) {
+    if (!r || k <= 0 || !index || !dst_scale || !dst_weight) return -1;
+    for (int j = 0; j < k; ++j) {
+        if (index[j] < 0 || (size_t)index[j] >= r->plans.size()) return -1;
+        for (int m = 0; m < 3; ++m) if (!dst_scale[3 * j + m] || !dst_weight[3 * j + m]) return -1;
+    }
+    if (cudaSetDevice(r->device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    if (r->queued && cudaEventSynchronize(r->done) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    r->queued = false;
+    cudaStream_t st = stream ? (cudaStream_t)stream : r->own;
+    const int wthreads = weight_threads();
+    std::vector<Nr3Task> stasks, wtasks;
+    size_t scr_bytes = 0;
+    std::vector<size_t> scr_off((size_t)k);
+    for (int j = 0; j < k; ++j) {
+        const Plan &p = r->plans[(size_t)index[j]];
+        scr_off[(size_t)j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
+        plan_tasks(p, (uint32_t)j, wthreads, stasks, wtasks);
+    }
+    r->L.compute((size_t)k, stasks.size(), wtasks.size(), (size_t)k, 0);
+    if (!r->dscratch.grow(scr_bytes) || !r->dmeta.grow(r->L.total) || !r->hmeta.grow(r->L.total)) return 1;
+    uint8_t *hm = r->hmeta.p, *dm = r->dmeta.p;
+    Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + r->L.recs);
+    CommitJob *hjobs = reinterpret_cast<CommitJob *>(hm + r->L.jobs);
+    uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + r->L.errs);
+    uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + r->L.errs);
+    std::memcpy(hm + r->L.stasks, stasks.data(), stasks.size() * sizeof(Nr3Task));
+    std::memcpy(hm + r->L.wtasks, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
+    for (int j = 0; j < k; ++j) {
+        const size_t x = (size_t)index[j];
+        const Plan &p = r->plans[x];
+        uint8_t *scr = r->dscratch.p + scr_off[(size_t)j];
+        plan_descriptor(p, r->tabs[x], r->store.p + r->rec_off[x],
+                        reinterpret_cast<const uint32_t *>(r->store.p + r->offs_at) + r->off_off[x], scr, derrs + j, &hrecs[j]);
+        herrs[j] = 0;
+        CommitJob &J = hjobs[j];
+        for (int m = 0; m < 3; ++m) {
+            J.src[m] = scr + p.soff[m]; J.dst[m] = dst_scale[3 * j + m]; J.bytes[m] = p.dst_bytes[m];
+            J.src[3 + m] = scr + p.wout[m]; J.dst[3 + m] = dst_weight[3 * j + m]; J.bytes[3 + m] = p.dst_bytes[3 + m];
+        }
+        J.error = derrs + j;
+    }
+    const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + r->L.recs);
+    auto mark = [&](int i) { return !r->profiling || cudaEventRecord(r->marks[i], st) == cudaSuccess; };
+    bool ok = cudaMemcpyAsync(dm, hm, r->L.total, cudaMemcpyHostToDevice, st) == cudaSuccess && mark(0) &&
+              launch_nr3_scales(drecs, reinterpret_cast<const Nr3Task *>(dm + r->L.stasks), (uint32_t)stasks.size(), st) == cudaSuccess &&
+              mark(1) &&
+              launch_nr3_weights(drecs, reinterpret_cast<const Nr3Task *>(dm + r->L.wtasks), (uint32_t)wtasks.size(), wthreads, st) == cudaSuccess &&
+              mark(2) && launch_commit(reinterpret_cast<const CommitJob *>(dm + r->L.jobs), (uint32_t)k, st) == cudaSuccess &&
+              mark(3) && cudaMemcpyAsync(herrs, derrs, 4 * (size_t)k, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+              cudaEventRecord(r->done, st) == cudaSuccess;
+    if (!ok) { (void)cudaGetLastError(); return 1; }
+    r->timed = r->profiling;
+    r->queued = true;
+    r->last_k = k;
+    r->launches = 3;
+    return 0;
+}
+
+WEXB_API int wexb_resident_wait(WexbResident *r, int *status) {
+    if (!r || !r->queued) return -1;
+    const bool ok = cudaSetDevice(r->device) == cudaSuccess && cudaEventSynchronize(r->done) == cudaSuccess;
+    if (!ok) (void)cudaGetLastError();
+    r->queued = false;
+    const uint32_t *herrs = reinterpret_cast<const uint32_t *>(r->hmeta.p + r->L.errs);
+    int bad = 0;
+    for (int j = 0; j < r->last_k; ++j) {
+        const int v = !ok ? 1 : herrs[j] ? -1 : 0;
+        if (v == -1) report_error_bits(herrs[j]);
+        if (status) status[j] = v;
+        bad += v != 0;
+    }
+    return bad;
+}
+
+WEXB_API int wexb_resident_launches(const WexbResident *r) { return r ? r->launches : 0; }
+
+WEXB_API int wexb_resident_profile(WexbResident *r, int on) {
+    if (!r) return -1;
+    if (on && !r->marks[0]) {
+        if (cudaSetDevice(r->device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+        for (auto &e : r->marks)
+            if (cudaEventCreate(&e) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    }
+    r->profiling = on != 0;
+    return 0;
+}
+
+WEXB_API int wexb_resident_kernel_ms(const WexbResident *r, float *ms3) {
+    if (!r || !ms3 || !r->timed || r->queued) return -1;
+    for (int i = 0; i < 3; ++i)
+        if (cudaEventElapsedTime(&ms3[i], r->marks[i], r->marks[i + 1]) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
+    return 0;
+}
+
+WEXB_API void wexb_resident_destroy(WexbResident *r) {
+    if (!r) return;
+    if (r->device >= 0 && cudaSetDevice(r->device) == cudaSuccess) {
+        if (r->own) cudaStreamSynchronize(r->own);
+        if (r->done) { cudaEventSynchronize(r->done); cudaEventDestroy(r->done); }
+        if (r->own) cudaStreamDestroy(r->own);
+        for (auto &e : r->marks) if (e) cudaEventDestroy(e);
+        r->store.release(); r->dscratch.release(); r->dmeta.release(); r->hmeta.release();
+    }
+    (void)cudaGetLastError();
+    delete r;
+}

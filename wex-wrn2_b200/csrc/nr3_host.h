@@ -1,0 +1,66 @@
+// Host side of the WNR2/WNR3 decoder: model registry with per-device lookup tables, record
+// validation and launch planning. Shared by the helper ABI (helper_abi.cpp) and the WEX4 entry
+// points (wex4_api.cpp).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "wex_entry.h"
+#include "wnr3.cuh"
+
+namespace wexb {
+
+inline uint32_t rd32(const uint8_t *p) { return p[0] | (uint32_t)p[1] << 8 | (uint32_t)p[2] << 16 | (uint32_t)p[3] << 24; }
+inline uint32_t rd16(const uint8_t *p) { return p[0] | (uint32_t)p[1] << 8; }
+inline uint64_t rd64(const uint8_t *p) { return rd32(p) | (uint64_t)rd32(p + 4) << 32; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) & ~(a - 1); }
+
+constexpr uint32_t kMagicWnr2 = 0x32524e57u, kMagicWnr3 = 0x33524e57u, kMagicWnm2 = 0x324d4e57u;
+constexpr int kMaxModels = 16, kMaxDevices = 64;
+
+// ---- WNM2 model registry (process-wide, never freed; c/tools/wex_cuda_bridge.cu:161-202) -------
+// 0 and *id when blob is a valid WNM2 model (c/wex_neural_rans.h:258-274), else -1.
+int model_validate(const uint8_t *blob, size_t bytes, uint32_t *id);
+// 0 registered (or already, same bytes), -1 invalid or id collision, 1 registry full.
+int model_register(const uint8_t *blob, size_t bytes);
+bool model_registered(uint32_t id);
+// Device tables of model `id` on `device` (the current device), built on first use: 0, or 1 when the
+// model is not registered or CUDA failed.
+int model_tables(uint32_t id, int device, Nr3Tables *out);
+
+// ---- one validated record ---------------------------------------------------------------------
+struct Plan {
+    uint32_t nr3, flags, model_id, owner, word24, schunk, wchunk;
+    uint32_t scount[3], wcount[3], soff[3], wout[3], sbase[3], wbase[3];
+    uint32_t sstreams, wstreams, meta, total;
+    uint32_t scale_bytes, weight_bytes, weight_at;   // weights at weight_at (16-aligned) in the decode layout
+    uint64_t raw, scratch;                           // canonical slab bytes, decode-layout bytes
+    uint32_t dst_bytes[6];                           // bytes of the six regions (scales m, weights m)
+    const uint8_t *lengths;
+    uint32_t streams() const { return sstreams + wstreams; }
+};
+
+// wex_entry_raw_sizes (c/wex_format.h:130-159): 0 and the raw / 4096-aligned sizes, else -1.
+int entry_raw_sizes(const WexEntry *e, uint64_t *raw, uint64_t *aligned);
+// Validates a codec-4/5 record of entry e (e->total_bytes at rec, host memory) and plans it; any model
+// id is accepted (the caller resolves it). The checks are the reference's parse (c/wex_neural_rans.h:
+// 287-337) behind its entry checks (c/wex_cuda.cuh:421-459). 0 or -1.
+int plan_record(const WexEntry *e, const uint8_t *rec, Plan *p);
+// Absolute record offsets of every stream, then the end: streams() + 1 words.
+void plan_offsets(const Plan &p, uint32_t *off);
+// Fills the device descriptor of a planned record.
+void plan_descriptor(const Plan &p, const Nr3Tables &t, const uint8_t *drec, const uint32_t *doff, uint8_t *dout,
+                     uint32_t *derr, Nr3Record *out);
+// Appends the CTA tasks of record `rec`: scale tasks of kScaleThreads streams, weight tasks of
+// `wthreads` streams.
+void plan_tasks(const Plan &p, uint32_t rec, int wthreads, std::vector<Nr3Task> &stasks, std::vector<Nr3Task> &wtasks);
+
+// Weight CTA size: WEXB_WEIGHT_THREADS (32..256, multiple of 32), default 128.
+int weight_threads();
+// Reports an integrity failure once per process (c/tools/wex_cuda_bridge.cu:117-122).
+void report_error_bits(uint32_t bits);
+uint32_t last_error_bits();
+
+}  // namespace wexb

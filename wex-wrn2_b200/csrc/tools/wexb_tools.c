@@ -7,6 +7,7 @@
  * Expert slab layout (the legacy 72-byte entry, c/wex_format.h:57-67): scales of w1, w2, w3, then
  * the packed E2M1 nibbles of w1, w2, w3 (even element in the low nibble). */
 #include <math.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -40,35 +41,50 @@ static uint64_t rng_u64(Rng *r) {
     return z ^ (z >> 31);
 }
 static double rng_unit(Rng *r) { return ((rng_u64(r) >> 11) + 0.5) * (1.0 / 9007199254740992.0); }
+/* Standard normal by inverse CDF: quantiles of 65536 equal-probability buckets (bisection on erfc,
+ * built once), linear inside a bucket; the two outermost buckets draw an exact Box-Muller tail. */
+#define QBUCKETS 65536
+static double g_quantile[QBUCKETS + 1];   /* [1 .. QBUCKETS - 1] used */
+static pthread_once_t g_quantile_once = PTHREAD_ONCE_INIT;
+static void quantile_init(void) {
+    for (int i = 1; i < QBUCKETS; i++) {
+        double p = (double)i / QBUCKETS, lo = -10, hi = 10;
+        for (int it = 0; it < 80; it++) {
+            double mid = 0.5 * (lo + hi);
+            if (0.5 * erfc(-mid / 1.4142135623730951) < p) lo = mid; else hi = mid;
+        }
+        g_quantile[i] = 0.5 * (lo + hi);
+    }
+}
 static double rng_normal(Rng *r) {
-    if (r->have) { r->have = 0; return r->spare; }
-    double u = rng_unit(r), v = rng_unit(r), m = sqrt(-2.0 * log(u));
-    r->spare = m * sin(6.283185307179586 * v); r->have = 1;
-    return m * cos(6.283185307179586 * v);
+    const uint32_t u = (uint32_t)(rng_u64(r) >> 32), i = u >> 16;
+    if (i == 0 || i == QBUCKETS - 1) {   /* tails beyond the first / last quantile: Marsaglia's tail method */
+        const double a = g_quantile[QBUCKETS - 1];
+        double x, y;
+        do { x = -log(rng_unit(r)) / a; y = -log(rng_unit(r)); } while (2.0 * y < x * x);
+        return i ? a + x : -(a + x);
+    }
+    const double f = (u & 0xffffu) * (1.0 / 65536.0);
+    return g_quantile[i] + f * (g_quantile[i + 1] - g_quantile[i]);
 }
 
 /* OCP MXFP4 of one 32-element block: E8M0 exponent floor(log2(amax)) - 2 (amax 0: -127), E2M1
  * magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6} rounded to nearest with ties to the even code, the sign
  * bit only on non-zero codes (the rule of the reference's c/tools/make_qwen38_tiny_mxfp4.py:44-64). */
-static uint8_t e2m1_code(double mag) {
-    if (mag <= 0.25) return 0;
-    if (mag < 0.75) return 1;
-    if (mag <= 1.25) return 2;
-    if (mag < 1.75) return 3;
-    if (mag <= 2.5) return 4;
-    if (mag < 3.5) return 5;
-    if (mag <= 5.0) return 6;
-    return 7;
+static uint8_t e2m1_code(double mag) {   /* midpoints; a tie goes to the even code */
+    return (uint8_t)((mag > 0.25) + (mag >= 0.75) + (mag > 1.25) + (mag >= 1.75) + (mag > 2.5) + (mag >= 3.5) +
+                     (mag > 5.0));
 }
 static uint8_t quantize_block(const double *g, uint8_t nib[32]) {
     double amax = 0;
     for (int i = 0; i < 32; i++) amax = fmax(amax, fabs(g[i]));
     int e = -127;
-    if (amax > 0) { int k; frexp(amax, &k); e = k - 1 - 2; }
+    if (amax > 0) e = ilogb(amax) - 2;   /* floor(log2 amax) - 2, exact */
     if (e < -127) e = -127;
     if (e > 127) e = 127;
+    const double inv = ldexp(1.0, -e);   /* a power of two: the products below are exact */
     for (int i = 0; i < 32; i++) {
-        double x = ldexp(g[i], -e), mag = fmin(fabs(x), 6.0);
+        double x = g[i] * inv, mag = fmin(fabs(x), 6.0);
         uint8_t c = e2m1_code(mag);
         nib[i] = (x < 0 && c) ? (uint8_t)(c | 8u) : c;
     }
@@ -77,10 +93,15 @@ static uint8_t quantize_block(const double *g, uint8_t nib[32]) {
 
 /* One matrix of rows x cols FP4 elements (cols a multiple of 32): packed[rows * cols / 2] and
  * scales[rows * cols / 32]. mode 0: N(0, sigma) quantized; mode 1: uniform random nibbles and
- * scales in 118..126 (incompressible). neg_zero: the fraction of zero nibbles written as -0 (0x8). */
+ * scales in 118..126 (incompressible); mode 2: mode 0 with every WNR3 block case mixed in (a quarter
+ * of the blocks "even": maximum magnitude 7 and no magnitude 1 or 3, some of them at scale 254 or
+ * 255; blocks of maximum 0..4; all-zero blocks with random signs), like the reference's test fill
+ * (c/tests/test_wex_format.c:694-730); mode 3: mode 2 plus one block of maximum 5, which keeps the
+ * ceil form off for the matrix. neg_zero: the fraction of zero nibbles written as -0 (0x8). */
 EXPORT int wexb_synth_matrix(uint64_t seed, uint32_t rows, uint32_t cols, double sigma, int mode, double neg_zero,
                              uint8_t *packed, uint8_t *scales) {
     if (!rows || !cols || cols % 32u || !packed || !scales) return -1;
+    pthread_once(&g_quantile_once, quantile_init);
     Rng r = {seed * 0x9e3779b97f4a7c15ull + 0x632be59bd9b4e019ull, 0, 0};
     double g[32];
     uint8_t nib[32];
@@ -95,6 +116,23 @@ EXPORT int wexb_synth_matrix(uint64_t seed, uint32_t rows, uint32_t cols, double
         } else {
             for (int i = 0; i < 32; i++) g[i] = sigma * rng_normal(&r);
             scales[b] = quantize_block(g, nib);
+            if (mode >= 2) {
+                static const uint8_t even[6] = {0, 2, 4, 5, 6, 7};
+                const uint32_t pick = (uint32_t)(rng_u64(&r) % 16u);
+                if (pick < 4) {            /* even block, maximum 7 */
+                    for (int i = 0; i < 32; i++) nib[i] = even[rng_u64(&r) % 6u];
+                    nib[rng_u64(&r) % 32u] = 7;
+                    if (pick == 0) scales[b] = (uint8_t)(254u + rng_u64(&r) % 2u);
+                } else if (pick == 4) {    /* maximum 0..4 */
+                    const uint32_t top = (uint32_t)(rng_u64(&r) % 5u);
+                    for (int i = 0; i < 32; i++) nib[i] = (uint8_t)(rng_u64(&r) % (top + 1u));
+                } else if (pick == 5) {    /* all zero, random signs */
+                    for (int i = 0; i < 32; i++) nib[i] = (uint8_t)((rng_u64(&r) & 1u) << 3);
+                }
+                if (pick < 5)
+                    for (int i = 0; i < 32; i++) if (nib[i] && (rng_u64(&r) & 1u)) nib[i] |= 8u;
+                if (mode == 3 && b == 0) { for (int i = 0; i < 32; i++) nib[i] &= 0xbu; nib[5] = 5; }
+            }
             if (nz)
                 for (int i = 0; i < 32; i++)
                     if (nib[i] == 0 && (rng_u64(&r) >> 11) < nz) nib[i] = 8;

@@ -1,0 +1,360 @@
+// WNR2/WNR3 decode kernels for sm_100a (see wnr3.cuh for the structures).
+//
+// Layout per CTA: the CTA serves one matrix of one record; its lookup tables are staged into shared
+// memory by TMA bulk copies (cp.async.bulk, completion on an mbarrier), and every lane owns a
+// 32-word ring of its stream's payload in shared memory, refilled every 16 symbols by 4-byte
+// cp.async copies kept 24 words ahead of the read position (ring word w of lane l at
+// ring[(w % 32) * blockDim + l]: conflict-free whatever position each lane is at).
+//
+// Weight symbol lookup: the 16 cumulative frequencies of the context are compared with the slot
+// all at once (packed 16-bit subtraction, sign bits gathered with PRMT, one POPC), then one shared
+// load fetches the symbol's start and frequency. Renormalisation is branch-free: from a valid
+// state a symbol leaves at least 2^9, so it takes 0, 1 or 2 bytes, read as one big-endian pair.
+#include "wnr3.cuh"
+
+namespace wexb {
+namespace {
+
+constexpr uint32_t kRingWords = 32;
+constexpr uint32_t kAhead = 24;
+constexpr uint32_t kSpinLimit = 1u << 24;   // bounded waits: never spin forever on a barrier
+
+__device__ __forceinline__ uint32_t rotl32(uint32_t x, int r) { return __funnelshift_l(x, x, r); }
+__device__ __forceinline__ uint32_t mm3_mix(uint32_t k) { return rotl32(k * 0xcc9e2d51u, 15) * 0x1b873593u; }
+__device__ __forceinline__ uint32_t mm3_block(uint32_t h, uint32_t k) { return rotl32(h ^ mm3_mix(k), 13) * 5u + 0xe6546b64u; }
+__device__ __forceinline__ uint32_t mm3_final(uint32_t h, uint32_t len) {
+    h ^= len;
+    h ^= h >> 16; h *= 0x85ebca6bu; h ^= h >> 13; h *= 0xc2b2ae35u; h ^= h >> 16;
+    return h;
+}
+// MurmurHash3 state after the stream's ident words {model, owner, g, word24}, seed "WNR3"
+// (c/wex_neural_rans.h:225-233).
+__device__ __forceinline__ uint32_t ident_hash(uint32_t model, uint32_t owner, uint32_t g, uint32_t word24) {
+    uint32_t h = 0x33524e57u;
+    h = mm3_block(h, model); h = mm3_block(h, owner); h = mm3_block(h, g);
+    return mm3_block(h, word24);
+}
+
+// ---- async copies ----------------------------------------------------------------------------
+__device__ __forceinline__ void cp4(uint32_t *dst, const uint32_t *src, bool pred) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p cp.async.ca.shared.global [%0], [%1], 4;\n}\n"
+                 :: "r"(d), "l"(src), "r"((int)pred) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" :: "r"((unsigned)__cvta_generic_to_shared(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n"
+                 :: "r"((unsigned)__cvta_generic_to_shared(bar)), "r"(bytes) : "memory");
+}
+// TMA bulk copy global -> this CTA's shared memory, completing `bytes` on the mbarrier. Both
+// addresses 16-byte aligned, bytes a multiple of 16 (every table block here is).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                 :: "r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src), "r"(bytes),
+                    "r"((unsigned)__cvta_generic_to_shared(bar)) : "memory");
+}
+// Waits for phase `parity` of the mbarrier, at most kSpinLimit polls; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        uint32_t done;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Stages `n` blocks of table bytes into shared memory with TMA; every thread returns once they
+// landed (or, after a bounded wait, with false).
+__device__ __forceinline__ bool stage_tables(uint64_t *bar, void *const *dst, const void *const *src,
+                                             const uint32_t *bytes, int n) {
+    if (threadIdx.x == 0) mbar_init(bar, 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t total = 0;
+        for (int i = 0; i < n; ++i) total += bytes[i];
+        mbar_expect(bar, total);
+        for (int i = 0; i < n; ++i) bulk_g2s(dst[i], src[i], bytes[i], bar);
+    }
+    return mbar_wait(bar, 0);
+}
+
+// ---- one stream's payload: a per-lane ring in shared memory ------------------------------------
+struct Reader {
+    uint32_t *lane;          // this lane's ring base; word w lives at lane[(w % kRingWords) * stride]
+    uint32_t stride;
+    const uint32_t *src;     // the record as 32-bit words (4-byte aligned)
+    uint32_t pos;            // record offset of the next payload byte
+    uint32_t req;            // next word to request
+    uint32_t last;           // the stream's last word
+
+    __device__ __forceinline__ uint32_t *slot(uint32_t w) const { return lane + (w & (kRingWords - 1)) * stride; }
+
+    // Opens [begin, end) (length >= 4, checked on the host) and returns its initial state.
+    __device__ __forceinline__ uint32_t open(uint32_t begin, uint32_t end) {
+        const uint32_t first = begin >> 2;
+        last = (end - 1) >> 2;
+        const uint32_t target = min(first + kAhead, last + 1);
+        for (uint32_t w = first; w < target; ++w) cp4(slot(w), src + w, true);
+        req = target;
+        cp_commit();
+        cp_wait<0>();
+        const uint32_t v = __funnelshift_r(*slot(first), *slot(first + 1), (begin & 3u) * 8u);
+        pos = begin + 4;
+        return __byte_perm(v, 0, 0x0123);   // big-endian bytes begin .. begin + 3
+    }
+    // Every 16 symbols (at most 32 bytes): keep kAhead words requested, then wait for the words of
+    // the previous request, which cover every byte the next 16 symbols can read.
+    __device__ __forceinline__ void refill() {
+        const uint32_t target = min((pos >> 2) + kAhead, last + 1);
+#pragma unroll
+        for (uint32_t k = 0; k < 8; ++k) {
+            const uint32_t w = req + k;
+            cp4(slot(w), src + w, w < target);
+        }
+        req = max(req, min(req + 8, target));
+        cp_commit();
+        cp_wait<1>();
+    }
+    // The next two payload bytes as a big-endian pair in bits 16..31 (read before the lookup, so
+    // the shared loads overlap it). Past the stream's end the ring holds stale words: consuming
+    // them is caught by the final pos == end check.
+    __device__ __forceinline__ uint32_t peek() const {
+        const uint32_t w = pos >> 2;
+        return __byte_perm(__funnelshift_r(*slot(w), *slot(w + 1), (pos & 3u) * 8u), 0, 0x0144);
+    }
+    // Waits for every copy this lane still has in flight (before the lane returns).
+    __device__ __forceinline__ void drain() const { cp_wait<0>(); }
+    // while (x < L) x = x << 8 | next byte, as one funnel shift of 0, 8 or 16 bits.
+    __device__ __forceinline__ uint32_t renorm(uint32_t x, uint32_t two) {
+        const uint32_t bits = x < (1u << 15) ? 16u : (x < kRansL ? 8u : 0u);
+        pos += bits >> 3;
+        return __funnelshift_l(two, x, bits);
+    }
+};
+
+// Symbol of `slot` in a 16-entry cumulative row (cdf[0] = 0 < cdf[1] < ... < cdf[15] < 2^14), i.e.
+// the number of entries <= slot, minus one. Per 16-bit half, (slot | 0x8000) - cdf keeps bit 15
+// set exactly when cdf <= slot and never borrows from the other half.
+__device__ __forceinline__ uint32_t row_symbol(const uint4 a, const uint4 b, uint32_t slot) {
+    const uint32_t g = slot * 0x10001u | 0x80008000u;
+    const uint32_t p0 = __byte_perm(g - a.x, g - a.y, 0x7531), p1 = __byte_perm(g - a.z, g - a.w, 0x7531);
+    const uint32_t p2 = __byte_perm(g - b.x, g - b.y, 0x7531), p3 = __byte_perm(g - b.z, g - b.w, 0x7531);
+    const uint32_t m = 0x80808080u;
+    return (uint32_t)__popc((p0 & m) | ((p1 & m) >> 1) | ((p2 & m) >> 2) | ((p3 & m) >> 3)) - 1u;
+}
+
+// Non-zero iff one of the eight nibbles of w is 8 (-0).
+__device__ __forceinline__ uint32_t has_neg_zero(uint32_t w) {
+    const uint32_t t = w ^ 0x88888888u;
+    return (t - 0x11111111u) & ~t & 0x88888888u;
+}
+// Ceil-form inverse of eight nibbles: magnitude a -> a + min(a, 2), signs kept.
+__device__ __forceinline__ uint32_t ceil_double(uint32_t w) {
+    const uint32_t mag = w & 0x77777777u;
+    const uint32_t two_or_more = ((mag >> 1) | (mag >> 2)) & 0x11111111u;
+    const uint32_t least = (two_or_more << 1) | (mag & 0x11111111u & ~two_or_more);
+    return (w & 0x88888888u) | (mag + least);
+}
+
+// ---- kernel A: scale streams ------------------------------------------------------------------
+__global__ void __launch_bounds__(kScaleThreads) nr3_scales(const Nr3Record *__restrict__ recs,
+                                                            const Nr3Task *__restrict__ tasks) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bar;
+    uint32_t *sdir = reinterpret_cast<uint32_t *>(smem);
+    uint8_t *ssym = smem + kTotal * 4u;
+    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kTotal * 5u);
+    const Nr3Task task = tasks[blockIdx.x];
+    const Nr3Record &R = recs[task.rec];
+    const uint32_t m = task.matrix;
+    {
+        void *dst[2] = {sdir, ssym};
+        const void *src[2] = {R.t.sdir + (size_t)m * kTotal, R.t.ssym + (size_t)m * kTotal};
+        const uint32_t bytes[2] = {kTotal * 4u, kTotal};
+        if (!stage_tables(&bar, dst, src, bytes, 2)) {
+            if (threadIdx.x == 0) atomicOr(R.error, kErrTimeout);
+            return;
+        }
+    }
+    if (threadIdx.x >= task.count) return;
+    const uint32_t j = task.first + threadIdx.x, g = R.sbase[m] + j;
+    const uint32_t begin = R.offsets[g], end = R.offsets[g + 1];
+    const uint32_t first = j * R.schunk, count = min(R.schunk, R.scount[m] - first);
+    uint8_t *out = R.out + R.soff[m] + first;
+    Reader rd{ring + threadIdx.x, blockDim.x, reinterpret_cast<const uint32_t *>(R.rec), 0, 0, 0};
+    uint32_t x = rd.open(begin, end);
+    if (x < kRansL || x >= (kRansL << 8)) { atomicOr(R.error, kErrStruct); rd.drain(); return; }
+    const bool nr3 = R.flags & 256u, aligned = !(reinterpret_cast<uintptr_t>(out) & 3u);
+    uint32_t h = nr3 ? ident_hash(R.model_id, R.owner, g, R.word24) : 0u;
+    const uint32_t full = count & ~15u;
+    for (uint32_t i = 0; i < full; i += 16) {
+        rd.refill();
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) {
+            uint32_t word = 0;
+#pragma unroll
+            for (uint32_t k = 0; k < 4; ++k) {
+                const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), e = sdir[slot];
+                word |= (uint32_t)ssym[slot] << (8u * k);
+                x = (e >> 14) * (x >> kPrec) + (e & 0x3fffu);
+                x = rd.renorm(x, two);
+            }
+            if (nr3) h = mm3_block(h, word);
+            if (aligned) *reinterpret_cast<uint32_t *>(out + i + 4u * q) = word;
+            else for (uint32_t k = 0; k < 4; ++k) out[i + 4u * q + k] = (uint8_t)(word >> (8u * k));
+        }
+    }
+    if (full < count) {   // the last stream of a matrix: a partial group of 16
+        rd.refill();
+        uint32_t word = 0, held = 0;
+        for (uint32_t i = full; i < count; ++i) {
+            const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), e = sdir[slot], s = ssym[slot];
+            out[i] = (uint8_t)s;
+            word |= s << (8u * held);
+            x = (e >> 14) * (x >> kPrec) + (e & 0x3fffu);
+            x = rd.renorm(x, two);
+            if (++held == 4) { if (nr3) h = mm3_block(h, word); word = 0; held = 0; }
+        }
+        if (nr3 && held) h ^= mm3_mix(word);
+    }
+    rd.drain();
+    const uint32_t expect = nr3 ? kRansL + (mm3_final(h, 16u + count) & 0x7fffffu) : kRansL;
+    if (rd.pos != end) atomicOr(R.error, kErrStruct);
+    else if (x != expect) atomicOr(R.error, nr3 ? kErrHash : kErrStruct);
+}
+
+// ---- kernel B: weight streams -----------------------------------------------------------------
+constexpr uint32_t kRowBytes = kContexts * 32u, kSfBytes = kContexts * 64u;
+
+__global__ void __launch_bounds__(kWeightThreadsMax, 2) nr3_weights(const Nr3Record *__restrict__ recs,
+                                                                    const Nr3Task *__restrict__ tasks) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bar;
+    const uint4 *rows = reinterpret_cast<const uint4 *>(smem);
+    const uint32_t *sf = reinterpret_cast<const uint32_t *>(smem + kRowBytes);
+    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kRowBytes + kSfBytes);
+    const Nr3Task task = tasks[blockIdx.x];
+    const Nr3Record &R = recs[task.rec];
+    const uint32_t m = task.matrix;
+    {
+        void *dst[2] = {smem, smem + kRowBytes};
+        const void *src[2] = {R.t.wrows + (size_t)m * kContexts * 2u, R.t.wsf + (size_t)m * kContexts * 16u};
+        const uint32_t bytes[2] = {kRowBytes, kSfBytes};
+        if (!stage_tables(&bar, dst, src, bytes, 2)) {
+            if (threadIdx.x == 0) atomicOr(R.error, kErrTimeout);
+            return;
+        }
+    }
+    if (threadIdx.x >= task.count) return;
+    const uint32_t j = task.first + threadIdx.x, g = R.wbase[m] + j;
+    const uint32_t begin = R.offsets[g], end = R.offsets[g + 1];
+    const uint32_t first = j * R.wchunk, blocks = min(R.wchunk, R.wcount[m] - first) / 32u;
+    uint8_t *scales = R.out + R.soff[m] + first / 32u;   // coded scales; the ceil inverse edits them
+    uint4 *out = reinterpret_cast<uint4 *>(R.out + R.wout[m] + first / 2u);
+    Reader rd{ring + threadIdx.x, blockDim.x, reinterpret_cast<const uint32_t *>(R.rec), 0, 0, 0};
+    uint32_t x = rd.open(begin, end);
+    if (x < kRansL || x >= (kRansL << 8)) { atomicOr(R.error, kErrStruct); rd.drain(); return; }
+    const bool nr3 = R.flags & 256u, cz = nr3 && (R.flags & 8u), ceil = nr3 && ((R.flags >> m) & 1u);
+    const int anchor = (int)((R.word24 >> (8u * m)) & 0xffu);
+    uint32_t h = nr3 ? ident_hash(R.model_id, R.owner, g, R.word24) : 0u;
+    uint32_t scale = scales[0];
+#pragma unroll 1
+    for (uint32_t b = 0; b < blocks; ++b) {
+        const uint32_t next_scale = b + 1 < blocks ? scales[b + 1] : 0u;
+        const int d = (int)scale - anchor;
+        const uint32_t base = (uint32_t)(min(max(d, -3), 3) + 3) * 81u;
+        uint32_t ctx = base + 80u, top = 0, w[4] = {0, 0, 0, 0};   // context of "no previous, no maximum"
+#pragma unroll
+        for (uint32_t k = 0; k < 32; ++k) {
+            if (k == 0 || k == 16) rd.refill();
+            const uint32_t two = rd.peek(), slot = x & (kTotal - 1u);
+            const uint32_t sym = row_symbol(rows[2u * ctx], rows[2u * ctx + 1u], slot);
+            const uint32_t e = sf[ctx * 16u + sym];
+            x = (e >> 16) * (x >> kPrec) + slot - (e & 0xffffu);
+            x = rd.renorm(x, two);
+            w[k / 8u] |= sym << (4u * (k % 8u));
+            const uint32_t mag = sym & 7u;
+            top = max(top, mag);
+            ctx = base + mag * 9u + top;
+        }
+        if (nr3) {   // hash and checks on the coded nibbles, then the ceil inverse
+            h = mm3_block(mm3_block(mm3_block(mm3_block(h, w[0]), w[1]), w[2]), w[3]);
+            if (cz && (has_neg_zero(w[0]) | has_neg_zero(w[1]) | has_neg_zero(w[2]) | has_neg_zero(w[3]))) {
+                atomicOr(R.error, kErrCz);
+                rd.drain();
+                return;
+            }
+            if (ceil && top == 5u) {
+                if (!scale) { atomicOr(R.error, kErrCeil); rd.drain(); return; }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) w[q] = ceil_double(w[q]);
+                scales[b] = (uint8_t)(scale - 1u);
+            }
+        }
+        out[b] = make_uint4(w[0], w[1], w[2], w[3]);
+        scale = next_scale;
+    }
+    rd.drain();
+    const uint32_t expect = nr3 ? kRansL + (mm3_final(h, 16u + blocks * 16u) & 0x7fffffu) : kRansL;
+    if (rd.pos != end) atomicOr(R.error, kErrStruct);
+    else if (x != expect) atomicOr(R.error, nr3 ? kErrHash : kErrStruct);
+}
+
+// ---- commit -----------------------------------------------------------------------------------
+__global__ void commit_regions(const CommitJob *__restrict__ jobs) {
+    const CommitJob &J = jobs[blockIdx.z];
+    if (*reinterpret_cast<const volatile uint32_t *>(J.error)) return;
+    const uint32_t r = blockIdx.y;
+    const uint8_t *from = J.src[r];
+    uint8_t *to = J.dst[r];
+    const size_t bytes = J.bytes[r], stride = (size_t)gridDim.x * blockDim.x;
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (!((reinterpret_cast<uintptr_t>(from) | reinterpret_cast<uintptr_t>(to)) & 15u)) {
+        const size_t n16 = bytes / 16u;
+        for (size_t k = i; k < n16; k += stride) reinterpret_cast<uint4 *>(to)[k] = reinterpret_cast<const uint4 *>(from)[k];
+        for (size_t k = n16 * 16u + i; k < bytes; k += stride) to[k] = from[k];
+    } else {
+        for (size_t k = i; k < bytes; k += stride) to[k] = from[k];
+    }
+}
+
+constexpr size_t scale_smem(int threads) { return kTotal * 5u + (size_t)kRingWords * 4u * threads; }
+constexpr size_t weight_smem(int threads) { return kRowBytes + kSfBytes + (size_t)kRingWords * 4u * threads; }
+
+}  // namespace
+
+cudaError_t prepare_nr3_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(nr3_scales, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scale_smem(kScaleThreads));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(nr3_weights, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)weight_smem(kWeightThreadsMax));
+    return e;
+}
+
+cudaError_t launch_nr3_scales(const Nr3Record *recs, const Nr3Task *tasks, uint32_t ntasks, cudaStream_t st) {
+    if (!ntasks) return cudaSuccess;
+    nr3_scales<<<ntasks, kScaleThreads, scale_smem(kScaleThreads), st>>>(recs, tasks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_nr3_weights(const Nr3Record *recs, const Nr3Task *tasks, uint32_t ntasks, int threads, cudaStream_t st) {
+    if (!ntasks) return cudaSuccess;
+    if (threads < 32 || threads > kWeightThreadsMax || threads % 32) return cudaErrorInvalidValue;
+    nr3_weights<<<ntasks, threads, weight_smem(threads), st>>>(recs, tasks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_commit(const CommitJob *jobs, uint32_t njobs, cudaStream_t st) {
+    if (!njobs) return cudaSuccess;
+    commit_regions<<<dim3(32, 6, njobs), 256, 0, st>>>(jobs);
+    return cudaGetLastError();
+}
+
+}  // namespace wexb

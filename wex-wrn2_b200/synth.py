@@ -76,8 +76,10 @@ def raw_bytes(hidden, ffn):
 
 
 def synth_expert(hidden, ffn, seed, sigma=0.02, mode=0, neg_zero=0.0):
-    """Decoded slab of one expert: seeded N(0, sigma) quantized to MXFP4 (mode 0) or uniform random
-    nibbles (mode 1, incompressible); neg_zero = fraction of zero nibbles written as -0."""
+    """Decoded slab of one expert: seeded N(0, sigma) quantized to MXFP4 (mode 0), uniform random
+    nibbles (mode 1, incompressible), Gaussian with every WNR3 block case mixed in (mode 2), or mode 2
+    with a block of maximum 5 in w2 that keeps the ceil form off there (mode 3); neg_zero = fraction
+    of zero nibbles written as -0."""
     mats = matrices(hidden, ffn)
     out = np.zeros(raw_bytes(hidden, ffn), np.uint8)
     scale_at = 0
@@ -86,7 +88,8 @@ def synth_expert(hidden, ffn, seed, sigma=0.02, mode=0, neg_zero=0.0):
         ns, nw = r * c // 32, r * c // 2
         sc = out[scale_at:scale_at + ns]
         wt = out[weight_at:weight_at + nw]
-        assert tools().wexb_synth_matrix(seed * 3 + m, r, c, sigma, mode, neg_zero,
+        md = 2 if (mode == 3 and m != 1) else mode   # mode 3: the maximum-5 block in w2 only
+        assert tools().wexb_synth_matrix(seed * 3 + m, r, c, sigma, md, neg_zero,
                                          wt.ctypes.data, sc.ctypes.data) == 0
         scale_at += ns
         weight_at += nw

@@ -1,0 +1,178 @@
+"""ctypes binding of libwexb200.so: the CUDA helper ABI (include/wex_cuda_helper.h), the engine API
+(include/wex_decode.h), the WEX4 tools ABI (include/wex4_tools.h), the WNR4 ABI (include/wnr4_cuda.h)
+and the resident-record additions (include/wexb200.h).
+
+Device buffers are plain integers (device pointers: torch tensors' data_ptr() work, any runtime of
+the process shares the device's primary context). Host buffers are numpy uint8 arrays or bytes.
+The library must be present: this module never falls back to anything else.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+import build as _build
+
+P, U32, U64, SZ, I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_int
+_lib = None
+
+
+def lib_path():
+    return _build.CUDA_LIB
+
+
+def lib():
+    """The loaded library (built in-tree first if it is missing and nvcc is available)."""
+    global _lib
+    if _lib is None:
+        path = lib_path()
+        if not os.path.exists(path):
+            _build.build_cuda()
+        if not os.path.exists(path):
+            raise RuntimeError(f'{path} is missing: run `python wex-wrn2_b200/build.py`')
+        L = ctypes.CDLL(path)
+        L.wex_cuda_helper_abi.restype = U32
+        L.wex_cuda_helper_features.restype = U32
+        L.wex_cuda_register_model.argtypes = [P, SZ]
+        L.wex_cuda_decode_to_host.argtypes = [P, P, SZ]
+        L.wex_cuda_decode_to_device.argtypes = [P, P, I, P, P]
+        L.wex_cuda_decode_batch_to_device.argtypes = [I, P, P, I, P, P, P]
+        L.wex_cuda_decode_batch_to_host.argtypes = [I, P, P, I, P, P]
+        L.wex_cuda_host_register.argtypes = [P, SZ]
+        L.wex_cuda_host_unregister.argtypes = [P]
+        L.wexb_abi.restype = U32
+        L.wexb_last_error_bits.restype = U32
+        L.wexb_resident_create.argtypes = [I, P, P, I, P, P]
+        L.wexb_resident_bytes.argtypes = [P]; L.wexb_resident_bytes.restype = SZ
+        L.wexb_resident_decode.argtypes = [P, I, P, P, P, P]
+        L.wexb_resident_wait.argtypes = [P, P]
+        L.wexb_resident_launches.argtypes = [P]
+        L.wexb_resident_profile.argtypes = [P, I]
+        L.wexb_resident_kernel_ms.argtypes = [P, P]
+        L.wexb_resident_destroy.argtypes = [P]; L.wexb_resident_destroy.restype = None
+        _lib = L
+    return _lib
+
+
+def _buf(x):
+    """(address, keep-alive) of a host buffer: numpy array, bytearray or bytes."""
+    if isinstance(x, np.ndarray):
+        assert x.flags['C_CONTIGUOUS']
+        return x.ctypes.data, x
+    if isinstance(x, bytearray):
+        a = (ctypes.c_char * len(x)).from_buffer(x)
+        return ctypes.addressof(a), a
+    if isinstance(x, (bytes, memoryview)):
+        a = np.frombuffer(bytes(x), np.uint8)
+        return a.ctypes.data, a
+    raise TypeError(type(x))
+
+
+def _ptrs(values):
+    return (ctypes.c_void_p * len(values))(*[v or None for v in values])
+
+
+def _entries(entries):
+    """Array of WexEntry pointers from 72-byte entries (keeps the storage alive in the result)."""
+    store = [np.frombuffer(bytes(e), np.uint8).copy() for e in entries]
+    return _ptrs([a.ctypes.data for a in store]), store
+
+
+def register_model(blob):
+    return lib().wex_cuda_register_model(bytes(blob), len(blob))
+
+
+def decode_to_host(entry, slab):
+    """slab: bytearray / numpy array holding the record at its read offset; returns the status."""
+    a, keep = _buf(slab)
+    e = np.frombuffer(bytes(entry), np.uint8).copy()
+    return lib().wex_cuda_decode_to_host(e.ctypes.data, a, len(slab))
+
+
+def decode_to_device(entry, record, device, dst_scale, dst_weight):
+    a, keep = _buf(record)
+    e = np.frombuffer(bytes(entry), np.uint8).copy()
+    return lib().wex_cuda_decode_to_device(e.ctypes.data, a, device, _ptrs(dst_scale), _ptrs(dst_weight))
+
+
+def decode_batch_to_device(entries, records, device, dst_scale, dst_weight):
+    """(failures, statuses). dst_scale / dst_weight: 3 * n device pointers."""
+    n = len(entries)
+    ep, keep_e = _entries(entries)
+    bufs = [_buf(r) for r in records]
+    status = (ctypes.c_int * max(n, 1))()
+    bad = lib().wex_cuda_decode_batch_to_device(n, ep, _ptrs([b[0] for b in bufs]), device, _ptrs(dst_scale),
+                                                _ptrs(dst_weight), status)
+    return bad, list(status)[:n]
+
+
+def decode_batch_to_host(entries, records, device, dsts):
+    n = len(entries)
+    ep, keep_e = _entries(entries)
+    bufs = [_buf(r) for r in records]
+    outs = [_buf(d) for d in dsts]
+    status = (ctypes.c_int * max(n, 1))()
+    bad = lib().wex_cuda_decode_batch_to_host(n, ep, _ptrs([b[0] for b in bufs]), device, _ptrs([o[0] for o in outs]),
+                                              status)
+    return bad, list(status)[:n]
+
+
+def host_register(array):
+    return lib().wex_cuda_host_register(array.ctypes.data, array.nbytes)
+
+
+def host_unregister(array):
+    return lib().wex_cuda_host_unregister(array.ctypes.data)
+
+
+class Resident:
+    """Records kept in device memory (wexb_resident_*): decode any subset into device buffers."""
+
+    def __init__(self, entries, records, device=0):
+        n = len(entries)
+        ep, keep_e = _entries(entries)
+        bufs = [_buf(r) for r in records]
+        self.status = (ctypes.c_int * n)()
+        h = ctypes.c_void_p()
+        self.failures = lib().wexb_resident_create(n, ep, _ptrs([b[0] for b in bufs]), device, ctypes.byref(h),
+                                                   self.status)
+        self.handle = h.value
+        self._k = 0
+
+    @property
+    def bytes(self):
+        return lib().wexb_resident_bytes(self.handle)
+
+    def decode(self, index, dst_scale, dst_weight, stream=None):
+        """Queue the decode of resident records `index` (0 queued)."""
+        self._k = len(index)
+        idx = (ctypes.c_int * len(index))(*index)
+        self._keep = (idx, _ptrs(dst_scale), _ptrs(dst_weight))
+        return lib().wexb_resident_decode(self.handle, len(index), idx, self._keep[1], self._keep[2], stream)
+
+    def wait(self):
+        status = (ctypes.c_int * max(self._k, 1))()
+        bad = lib().wexb_resident_wait(self.handle, status)
+        return bad, list(status)[:self._k]
+
+    def launches(self):
+        return lib().wexb_resident_launches(self.handle)
+
+    def profile(self, on=True):
+        return lib().wexb_resident_profile(self.handle, 1 if on else 0)
+
+    def kernel_ms(self):
+        """(scales, weights, commit) milliseconds of the last waited decode, or None."""
+        ms = (ctypes.c_float * 3)()
+        return tuple(ms) if lib().wexb_resident_kernel_ms(self.handle, ms) == 0 else None
+
+    def close(self):
+        if self.handle:
+            lib().wexb_resident_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
