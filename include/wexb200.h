@@ -46,6 +46,19 @@ int wexb_resident_kernel_ms(const WexbResident *r, float *ms3);
 int wexb_resident_launches(const WexbResident *r);
 void wexb_resident_destroy(WexbResident *r);
 
+/* No counterpart in the reference. wex_cuda_decode_to_device for callers that may not allocate device
+ * memory at run time (an engine that reserves all of HBM in its own pool at start-up, or whose serving
+ * streams must not stall on the device synchronisation cudaMalloc / cudaFree can cause): it calls no
+ * cudaMalloc, cudaFree or other allocating routine and works in a fixed ~50 MiB device array defined
+ * in the library, held by every device that loads the library until the process exits. Limits:
+ * records of at most 24 MiB stored and 24 MiB decoded and 32,768 streams (larger ones return -2 with
+ * a message on stderr), at most 4 models per device (a fifth returns 1). The first call on a device
+ * sets that device up (looks up the array's address) and should come before any stream capture there.
+ * Calls are synchronous and serialised by a process-wide lock; calls that overlapped on the GPU would
+ * race on the shared array. Returns 0, -1 invalid (destination untouched), 1 unavailable, -2 too large. */
+int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned char *record, int device,
+                                  unsigned char *const *dst_scale, unsigned char *const *dst_weight);
+
 /* Error bits of the last failed record seen by this process (1 structure, 2 stream hash, 4 ceil form
  * at scale 0, 8 canonical zero, 16 bounded wait expired); 0 if none failed. */
 unsigned int wexb_last_error_bits(void);

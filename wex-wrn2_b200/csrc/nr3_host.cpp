@@ -116,6 +116,12 @@ int model_tables(uint32_t id, int device, Nr3Tables *out) {
     return 0;
 }
 
+const uint8_t *model_image(uint32_t id) {
+    std::lock_guard<std::mutex> lock(g_models_mu);
+    Model *m = find_locked(id);
+    return m ? m->image.data() : nullptr;
+}
+
 // ---- records ----------------------------------------------------------------------------------
 int entry_raw_sizes(const WexEntry *e, uint64_t *raw, uint64_t *aligned) {
     uint64_t s = 0, w = 0;

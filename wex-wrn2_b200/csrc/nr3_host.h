@@ -29,6 +29,9 @@ bool model_registered(uint32_t id);
 // Device tables of model `id` on `device` (the current device), built on first use: 0, or 1 when the
 // model is not registered or CUDA failed.
 int model_tables(uint32_t id, int device, Nr3Tables *out);
+// Host image (kTableBytes, the device table layout) of registered model `id`, or nullptr. Registered
+// models are never freed, so the pointer stays valid.
+const uint8_t *model_image(uint32_t id);
 
 // ---- one validated record ---------------------------------------------------------------------
 struct Plan {
