@@ -29,7 +29,7 @@ unsigned int wex_cuda_helper_abi(void);
 unsigned int wex_cuda_helper_features(void);
 /* Register a WNM2 model blob (59,408 B; process-wide, kept until exit): 0 registered or already
  * registered with the same bytes, -1 invalid or another blob with the same id, 1 registry full
- * (16 models) (c/tools/wex_cuda_bridge.cu:94-107). */
+ * (64 models here; the reference holds 16) (c/tools/wex_cuda_bridge.cu:94-107). */
 int wex_cuda_register_model(const unsigned char *blob, size_t bytes);
 /* Decode the record at slab + read offset (entry->total_bytes, in the tail of the slab) into the
  * canonical slab at slab[0 .. scale_bytes + weight_bytes); the slab is untouched unless it returns

@@ -1,0 +1,18 @@
+// Kernels of the WEX4 container layer besides SHA-256 (container_kernels.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace wexb {
+
+// A RAW record's padding [begin, end) must be zero (c/wex4.h:678-682); any non-zero byte ORs `bit`
+// into *error.
+struct ZeroJob {
+    const uint8_t *base;
+    uint64_t begin, end;
+    uint32_t *error;
+    uint32_t bit;
+};
+cudaError_t launch_zero_check(const ZeroJob *jobs, uint32_t n, cudaStream_t st);
+
+}  // namespace wexb

@@ -16,6 +16,7 @@
 #include <new>
 #include <vector>
 
+#include "bufs.h"
 #include "nr3_host.h"
 #include "wex_cuda_helper.h"
 #include "wexb200.h"
@@ -24,33 +25,6 @@
 
 namespace wexb {
 namespace {
-
-struct DevBuf {
-    uint8_t *p = nullptr;
-    size_t cap = 0;
-    bool grow(size_t n) {
-        if (n <= cap) return true;
-        if (p) cudaFree(p);
-        p = nullptr; cap = 0;
-        if (cudaMalloc(&p, std::max<size_t>(n, 256)) != cudaSuccess) { (void)cudaGetLastError(); return false; }
-        cap = n;
-        return true;
-    }
-    void release() { if (p) cudaFree(p); p = nullptr; cap = 0; }
-};
-struct PinBuf {
-    uint8_t *p = nullptr;
-    size_t cap = 0;
-    bool grow(size_t n) {
-        if (n <= cap) return true;
-        if (p) cudaFreeHost(p);
-        p = nullptr; cap = 0;
-        if (cudaMallocHost(&p, std::max<size_t>(n, 256)) != cudaSuccess) { (void)cudaGetLastError(); return false; }
-        cap = n;
-        return true;
-    }
-    void release() { if (p) cudaFreeHost(p); p = nullptr; cap = 0; }
-};
 
 constexpr int kLanes = 4;
 

@@ -18,7 +18,7 @@ inline uint64_t rd64(const uint8_t *p) { return rd32(p) | (uint64_t)rd32(p + 4) 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) & ~(a - 1); }
 
 constexpr uint32_t kMagicWnr2 = 0x32524e57u, kMagicWnr3 = 0x33524e57u, kMagicWnm2 = 0x324d4e57u;
-constexpr int kMaxModels = 16, kMaxDevices = 64;
+constexpr int kMaxModels = 64, kMaxDevices = 64;   // the reference registry holds 16 models
 
 // ---- WNM2 model registry (process-wide, never freed; c/tools/wex_cuda_bridge.cu:161-202) -------
 // 0 and *id when blob is a valid WNM2 model (c/wex_neural_rans.h:258-274), else -1.

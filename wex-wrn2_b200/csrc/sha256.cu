@@ -1,0 +1,135 @@
+// SHA-256 (FIPS 180-4) on the GPU: the per-record hash of stored bytes checked against a WEX4 index
+// (c/wex4.h:673-677) and the content digest of a container (wex4/wex4_tools.c:125-158).
+//
+// A SHA-256 chain is serial, so one thread hashes one message; records hash concurrently, one thread
+// each. The content digest is one message over many segments (tensor metadata from the host,
+// decoded bytes on the device), hashed by a single thread in order.
+#include "sha256.cuh"
+
+namespace wexb {
+namespace {
+
+__constant__ uint32_t kSha[64] = {
+    0x428a2f98, 0x71374491, 0xb5c0fbcf, 0xe9b5dba5, 0x3956c25b, 0x59f111f1, 0x923f82a4, 0xab1c5ed5,
+    0xd807aa98, 0x12835b01, 0x243185be, 0x550c7dc3, 0x72be5d74, 0x80deb1fe, 0x9bdc06a7, 0xc19bf174,
+    0xe49b69c1, 0xefbe4786, 0x0fc19dc6, 0x240ca1cc, 0x2de92c6f, 0x4a7484aa, 0x5cb0a9dc, 0x76f988da,
+    0x983e5152, 0xa831c66d, 0xb00327c8, 0xbf597fc7, 0xc6e00bf3, 0xd5a79147, 0x06ca6351, 0x14292967,
+    0x27b70a85, 0x2e1b2138, 0x4d2c6dfc, 0x53380d13, 0x650a7354, 0x766a0abb, 0x81c2c92e, 0x92722c85,
+    0xa2bfe8a1, 0xa81a664b, 0xc24b8b70, 0xc76c51a3, 0xd192e819, 0xd6990624, 0xf40e3585, 0x106aa070,
+    0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f, 0x682e6ff3,
+    0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
+
+__device__ __forceinline__ uint32_t ror(uint32_t x, int r) { return __funnelshift_r(x, x, r); }
+__device__ __forceinline__ uint32_t bswap(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
+
+// One compression of the big-endian message words w[0..15] into st.
+__device__ __forceinline__ void compress(uint32_t st[8], uint32_t w[16]) {
+    uint32_t a = st[0], b = st[1], c = st[2], d = st[3], e = st[4], f = st[5], g = st[6], h = st[7];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+        uint32_t wi;
+        if (i < 16) {
+            wi = w[i];
+        } else {   // the schedule kept in a 16-word circular window
+            const uint32_t w15 = w[(i - 15) & 15], w2 = w[(i - 2) & 15];
+            wi = w[i & 15] + (ror(w15, 7) ^ ror(w15, 18) ^ (w15 >> 3)) + w[(i - 7) & 15] +
+                 (ror(w2, 17) ^ ror(w2, 19) ^ (w2 >> 10));
+            w[i & 15] = wi;
+        }
+        const uint32_t t1 = h + (ror(e, 6) ^ ror(e, 11) ^ ror(e, 25)) + ((e & f) ^ (~e & g)) + kSha[i] + wi;
+        const uint32_t t2 = (ror(a, 2) ^ ror(a, 13) ^ ror(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
+        h = g; g = f; f = e; e = d + t1; d = c; c = b; b = a; a = t1 + t2;
+    }
+    st[0] += a; st[1] += b; st[2] += c; st[3] += d; st[4] += e; st[5] += f; st[6] += g; st[7] += h;
+}
+
+__device__ __forceinline__ void init(uint32_t st[8]) {
+    st[0] = 0x6a09e667; st[1] = 0xbb67ae85; st[2] = 0x3c6ef372; st[3] = 0xa54ff53a;
+    st[4] = 0x510e527f; st[5] = 0x9b05688c; st[6] = 0x1f83d9ab; st[7] = 0x5be0cd19;
+}
+
+// Streaming state of one thread: the chaining value, a partial block of `fill` bytes, the length. The
+// partial block lives in a byte buffer; the message words handed to compress() are always a fresh
+// statically indexed array, so they stay in registers.
+struct Sha {
+    uint32_t st[8];
+    uint8_t buf[64];
+    uint32_t fill;
+    uint64_t len;
+    __device__ void start() { init(st); fill = 0; len = 0; }
+    __device__ __forceinline__ void flush_buf() {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            w[i] = (uint32_t)buf[4 * i] << 24 | (uint32_t)buf[4 * i + 1] << 16 | (uint32_t)buf[4 * i + 2] << 8 | buf[4 * i + 3];
+        compress(st, w);
+    }
+    __device__ __forceinline__ void byte(uint32_t v) {
+        buf[fill] = (uint8_t)v;
+        if (++fill == 64) { flush_buf(); fill = 0; }
+    }
+    __device__ void update(const uint8_t *p, uint64_t n) {
+        len += n;
+        while (n && fill) { byte(*p++); --n; }
+        if (!(reinterpret_cast<uintptr_t>(p) & 15)) {   // whole aligned blocks: four 16-byte loads each
+            for (; n >= 64; n -= 64, p += 64) {
+                const uint4 *q = reinterpret_cast<const uint4 *>(p);
+                uint32_t w[16];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint4 v = q[k];
+                    w[4 * k] = bswap(v.x); w[4 * k + 1] = bswap(v.y); w[4 * k + 2] = bswap(v.z); w[4 * k + 3] = bswap(v.w);
+                }
+                compress(st, w);
+            }
+        }
+        while (n) { byte(*p++); --n; }
+    }
+    __device__ void finish(uint8_t *out) {
+        const uint64_t bits = len * 8;
+        byte(0x80);
+        while (fill != 56) byte(0);
+        for (int i = 7; i >= 0; --i) byte((uint32_t)(bits >> (8 * i)) & 0xffu);
+        for (int i = 0; i < 32; ++i) out[i] = (uint8_t)(st[i / 4] >> (24 - 8 * (i % 4)));
+    }
+};
+
+__global__ void __launch_bounds__(64) sha256_messages(const ShaMsg *__restrict__ msgs, uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const ShaMsg m = msgs[i];
+    Sha s;
+    s.start();
+    s.update(m.data, m.bytes);
+    uint8_t got[32];
+    s.finish(got);
+    uint32_t differ = 0;
+    for (int k = 0; k < 32; ++k) {
+        if (m.digest) m.digest[k] = got[k];
+        if (m.expect) differ |= got[k] ^ m.expect[k];
+    }
+    if (m.verdict) *m.verdict = m.expect ? (differ ? 1u : 0u) : 0u;
+}
+
+__global__ void sha256_segments(const ShaMsg *__restrict__ segs, uint32_t n, uint8_t *digest) {
+    if (blockIdx.x || threadIdx.x) return;
+    Sha s;
+    s.start();
+    for (uint32_t i = 0; i < n; ++i) s.update(segs[i].data, segs[i].bytes);
+    s.finish(digest);
+}
+
+}  // namespace
+
+cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st) {
+    if (!n) return cudaSuccess;
+    sha256_messages<<<(n + 63) / 64, 64, 0, st>>>(msgs, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sha256_segments(const ShaMsg *segs, uint32_t n, uint8_t *digest, cudaStream_t st) {
+    sha256_segments<<<1, 1, 0, st>>>(segs, n, digest);
+    return cudaGetLastError();
+}
+
+}  // namespace wexb

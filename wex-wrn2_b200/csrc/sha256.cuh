@@ -1,0 +1,23 @@
+// SHA-256 kernels (sha256.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace wexb {
+
+// One message (or, for the segment kernel, one piece of a message) in device memory.
+struct ShaMsg {
+    const uint8_t *data;
+    uint64_t bytes;
+    uint8_t *digest;          // optional: the 32-byte digest
+    const uint8_t *expect;    // optional: a 32-byte digest to compare with
+    uint32_t *verdict;        // optional: 0 equal (or no expect), 1 differs
+    uint32_t pad;
+};
+
+// One thread per message: digests and verdicts of n messages.
+cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st);
+// One thread: the digest of the concatenation of n segments (data and bytes used).
+cudaError_t launch_sha256_segments(const ShaMsg *segs, uint32_t n, uint8_t *digest, cudaStream_t st);
+
+}  // namespace wexb
