@@ -130,7 +130,7 @@ static uint32_t tile_decode(const Model4 *md, const Geo *g, const Rec4 *r, uint3
 #define RENORM(lane)                                                                       \
     do {                                                                                   \
         if (x[lane] < W4_L) {                                                              \
-            if (ptr >= nwords) return err | W4_ERR_STRUCT;                                 \
+            if (ptr >= nwords) return W4_ERR_STRUCT;   /* the bits seen so far are dropped */ \
             x[lane] = x[lane] << 16 | rd16(words + 2 * ptr); ptr++;                        \
         }                                                                                  \
     } while (0)
