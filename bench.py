@@ -11,9 +11,10 @@ involved) and larger than L2 between steps.
 
   value  records resident in HBM (wexb_resident_*), the step's 384 records decoded by one queued
          decode (3 kernel launches), timed with CUDA events on the launching stream
-  e2e    the reference-facing drop-in: per layer one wex_cuda_decode_batch_to_device call of 8
-         records from pinned host memory (H2D inside the timed region, statuses read back), 48 calls
-         a step, timed by the host clock around the synchronous calls (max over ranks)
+  e2e    from pinned host memory through the C ABI: per layer one call of 8 records (H2D inside the
+         timed region, statuses read back), 48 calls a step, timed by the host clock (max over
+         ranks); the headline keeps --depth calls in flight (wexb_batch_submit / wexb_batch_wait),
+         e2e.sync is the synchronous drop-in wex_cuda_decode_batch_to_device
 
 N GPUs (torchrun): expert-parallel placement, rank r decodes the experts whose id = r mod N (weak
 scaling: 384 records per rank per step); the only collectives are the max-over-ranks timing and a
@@ -156,12 +157,18 @@ def dist_init():
     return world, rank, local
 
 
+def _reduce_device():
+    """Device of the reduction tensors: CUDA under NCCL, the host under gloo (the CPU rank tests)."""
+    import torch.distributed as dist
+    return 'cuda' if dist.get_backend() == 'nccl' else 'cpu'
+
+
 def max_over_ranks(x, world):
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device='cuda')
+    t = torch.tensor([x], dtype=torch.float64, device=_reduce_device())
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -171,9 +178,19 @@ def sum_over_ranks(vals, world):
         return vals
     import torch
     import torch.distributed as dist
-    t = torch.tensor(vals, dtype=torch.float64, device='cuda')
+    t = torch.tensor(vals, dtype=torch.float64, device=_reduce_device())
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return [float(v) for v in t.tolist()]
+
+
+def gather_outcomes(rows, world):
+    """The per-record outcome table of every rank, on every rank (one all-gather after the run)."""
+    if world == 1:
+        return list(rows)
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, list(rows))
+    return [r for part in out for r in part]
 
 
 def barrier(world):
@@ -346,28 +363,84 @@ def run_gpu(args, cfg):
     got = dst[check].cpu().numpy()
     verified = sum(int(got[i].tobytes() == experts[last[j]].expected) for i, j in enumerate(check))
     assert verified == len(check), 'decoded bytes differ from the source'
+    # per-record outcome table of the last step (status, digest of the checked slabs), all ranks
+    import hashlib
+    slab_digest = {j: hashlib.sha256(got[n].tobytes()).hexdigest()[:16] for n, j in enumerate(check)}
+    table = gather_outcomes([(rank, experts[i].layer, experts[i].index, int(st[j]), slab_digest.get(j, ''))
+                             for j, i in enumerate(last)], world)
 
-    # ---- e2e: the drop-in batch call, 8 records per layer, from pinned host memory ----------------
-    def e2e_step(s):
+    # ---- e2e: 8 records per layer per call, from pinned host memory, statuses read back ------------
+    # Argument arrays are built once per (step, layer) as an engine holds them; the timed region
+    # covers the calls themselves: uploads, kernels, status read-back.
+    import ctypes
+    L = wexcuda.lib()
+    B = cfg['batch']
+    entry_store = [np.frombuffer(bytes(e.entry), np.uint8).copy() for e in experts]
+    call_args = []
+    for s in range(steps_total):
         ids = step_idx[s]
-        bad_total = 0
+        per = []
         for l in range(layers):
-            sel = ids[l * cfg['batch']:(l + 1) * cfg['batch']]
-            bad, st = wexcuda.decode_batch_to_device([experts[i].entry for i in sel], [views[i] for i in sel], dev,
-                                                     dscale[3 * l * cfg['batch']:3 * (l + 1) * cfg['batch']],
-                                                     dweight[3 * l * cfg['batch']:3 * (l + 1) * cfg['batch']])
-            bad_total += bad
-        return bad_total
+            sel = ids[l * B:(l + 1) * B]
+            per.append((wexcuda._ptrs([entry_store[i].ctypes.data for i in sel]),
+                        wexcuda._ptrs([views[i].ctypes.data for i in sel]),
+                        wexcuda._ptrs(dscale[3 * l * B:3 * (l + 1) * B]), wexcuda._ptrs(dweight[3 * l * B:3 * (l + 1) * B]),
+                        (ctypes.c_int * B)()))
+        call_args.append(per)
+
+    def sync_step(s):
+        bad = 0
+        for ep, rp, sp, wp, st in call_args[s]:
+            bad += L.wex_cuda_decode_batch_to_device(B, ep, rp, dev, sp, wp, st)
+        return bad
+
+    def queued_step(s, pending):
+        bad = 0
+        for ep, rp, sp, wp, st in call_args[s]:
+            t = L.wexb_batch_submit(B, ep, rp, dev, sp, wp)
+            assert t >= 0
+            pending.append((t, st))
+            if len(pending) > args.depth:
+                t0_, st0 = pending.pop(0)
+                bad += L.wexb_batch_wait(t0_, st0)
+        return bad
+
+    def drain(pending):
+        bad = 0
+        while pending:
+            t_, st_ = pending.pop(0)
+            bad += L.wexb_batch_wait(t_, st_)
+        return bad
+
+    def timed(run):
+        barrier(world)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        run()
+        torch.cuda.synchronize()
+        dt = max_over_ranks(time.perf_counter() - t0, world)
+        barrier(world)
+        return dt
+
     for s in range(args.warmup):
-        assert e2e_step(s) == 0
-    barrier(world)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for s in range(args.warmup, steps_total):
-        assert e2e_step(s) == 0
-    torch.cuda.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    barrier(world)
+        assert sync_step(s) == 0
+    pend = []
+    for s in range(args.warmup):
+        assert queued_step(s, pend) == 0
+    assert drain(pend) == 0
+
+    def run_queued():
+        p, bad = [], 0
+        for s in range(args.warmup, steps_total):
+            bad += queued_step(s, p)
+        bad += drain(p)
+        assert bad == 0
+
+    def run_sync():
+        assert sum(sync_step(s) for s in range(args.warmup, steps_total)) == 0
+
+    e2e_s = timed(run_queued)
+    sync_s = timed(run_sync)
     clk = clocks.stop()
     got = dst[check].cpu().numpy()
     assert all(got[i].tobytes() == experts[last[j]].expected for i, j in enumerate(check))
@@ -383,6 +456,7 @@ def run_gpu(args, cfg):
     dec_all, stored_all, recs_all = totals
     value = dec_all / (value_ms / 1e3) / 1e9
     e2e = dec_all / e2e_s / 1e9
+    e2e_sync = dec_all / sync_s / 1e9
     # roofline of the dominant kernel (weights): algorithmic bytes = weight payload read + packed
     # weights written + scales read for the contexts, per launch, over its event-timed duration
     wk = [m[1] for m in kernel_ms if m]
@@ -400,8 +474,12 @@ def run_gpu(args, cfg):
         'config': config_desc(args, cfg),
         'e2e': {'value': round(e2e, 3), 'unit': 'GB/s', 'experts_per_s': round(recs_all / e2e_s, 1),
                 'h2d_bytes_per_step': int(h2d_per_step), 'd2h_bytes_per_step': 4 * k,
-                'api': 'wex_cuda_decode_batch_to_device, 8 records per call, 48 calls per step',
-                'ms_per_step': round(1e3 * e2e_s / args.steps, 3)},
+                'api': f'wexb_batch_submit/wexb_batch_wait, {B} records per call, {layers} calls per step, '
+                       f'{args.depth} calls in flight',
+                'ms_per_step': round(1e3 * e2e_s / args.steps, 3), 'gpu_launches': 3 * k * args.steps,
+                'sync': {'value': round(e2e_sync, 3), 'unit': 'GB/s',
+                         'api': 'wex_cuda_decode_batch_to_device (drop-in, synchronous)',
+                         'ms_per_step': round(1e3 * sync_s / args.steps, 3)}},
         'roofline': {'bound': 'hbm', 'kernel': 'nr3_weights', 'achieved': round(achieved, 2) if achieved else None,
                      'peak': hbm_peak, 'unit': 'GB/s', 'frac': round(achieved / hbm_peak, 5) if achieved else None,
                      'peak_source': 'measured' if peaks else 'fallback', 'traffic': None,
@@ -411,6 +489,8 @@ def run_gpu(args, cfg):
         'gpu_launches': launches,
         'clocks': clk,
         'verified_records': verified,
+        'outcomes': {'records': len(table), 'failed': sum(1 for r in table if r[3]),
+                     'verified_slabs': sum(1 for r in table if r[4])},
         'stored_over_decoded': round(stored / dec_bytes, 4),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -439,6 +519,7 @@ def main():
     ap.add_argument('--layers', type=int, default=0, help='layers per step (default: all of the config)')
     ap.add_argument('--cpu-seconds', type=float, default=12.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--depth', type=int, default=6, help='e2e: batch calls kept in flight')
     args = ap.parse_args()
     assert args.warmup >= 1
     cfg = CONFIGS[args.config]

@@ -17,6 +17,19 @@ extern "C" {
 /* Library ABI of these additions. */
 unsigned int wexb_abi(void);
 
+/* Queued batches: the device-destination batch of wex_cuda_decode_batch_to_device
+ * (the reference's c/tools/wex_cuda_bridge.cu:388-487) split into a submit that returns once the
+ * uploads and kernels are queued and a wait that returns the statuses, so that a caller can keep
+ * several batches in flight. Host records and destination pointers must stay valid until the wait.
+ * Returns a ticket >= 0 (also when no record could be queued: the wait then reports why), -1 for
+ * bad arguments, -3 when out of host memory. */
+int wexb_batch_submit(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
+                      unsigned char *const *dst_scale, unsigned char *const *dst_weight);
+/* Wait for a ticket: status[i] as wex_cuda_decode_batch_to_device (0 ok, -1 invalid, 1 unavailable;
+ * destinations untouched unless 0). Returns the number of non-zero statuses, -1 for an unknown or
+ * already-waited ticket. status may be NULL. */
+int wexb_batch_wait(int ticket, int *status);
+
 typedef struct WexbResident WexbResident;
 
 /* Validate n WNR2/WNR3 records (host memory) and copy them, with their stream offset tables, to

@@ -284,3 +284,31 @@ def test_resident_decode(torch_cuda, tiny):
     for j, x in enumerate(order):
         assert _slab(ts, j) == ex[x].expected
     res.close()
+
+
+def test_queued_batches(torch_cuda, tiny):
+    """wexb_batch_submit / wexb_batch_wait: several batches in flight, one with a damaged and an
+    unavailable record; each wait gives the statuses of the synchronous call; tickets are single-use."""
+    blob, ex = tiny
+    other = synth.make_experts(1024, 512, [(0, 0)], seed=98, sigma=0.03, train_every=1)[1][0]   # unregistered model
+    damaged = bytearray(ex[2].record); damaged[7000] ^= 8
+    calls = [([e.entry for e in ex], [e.record for e in ex], [0, 0, 0]),
+             ([ex[1].entry, other.entry, ex[2].entry], [ex[1].record, other.record, bytes(damaged)], [0, 1, -1]),
+             ([ex[2].entry] * 2, [ex[2].record] * 2, [0, 0])]
+    pending = []
+    for _ in range(3):
+        for entries, records, want in calls:
+            ts, sp, wp = _dst(torch_cuda, entries[0], len(entries))
+            pending.append((wexcuda.submit_batch_to_device(entries, records, 0, sp, wp), ts, records, want))
+    for t, ts, records, want in reversed(pending):
+        bad, st = t.wait()
+        assert st == want and bad == sum(1 for s in want if s)
+        for j, s in enumerate(st):
+            if s == 0:
+                x = next(e for e in ex if e.record == records[j])
+                assert _slab(ts, j) == x.expected
+            else:
+                assert _untouched(ts, j)
+    L = wexcuda.lib()
+    assert L.wexb_batch_wait(pending[0][0].ticket, None) == -1
+    assert L.wexb_batch_submit(0, None, None, 0, None, None) == -1

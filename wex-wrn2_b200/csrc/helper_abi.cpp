@@ -1,12 +1,13 @@
 // The CUDA helper C ABI (include/wex_cuda_helper.h) and the resident-record additions
 // (include/wexb200.h), over the sm_100a WNR2/WNR3 kernels.
 //
-// One call = one pipeline on a pooled workspace of the target device: all launch metadata of the
-// call (record descriptors, CTA tasks, commit jobs, error words, stream offsets) goes up in one
-// copy, then every record is uploaded on the copy stream in order; record j's kernels run on lane
-// j % 4 as soon as its upload event fires, so decode overlaps the uploads of the later records.
-// A record's destinations are written by the error-gated commit kernel (device destinations), or
-// copied back after its kernels (host destinations).
+// One call = a pooled workspace (grown buffers, two events) on the device's shared streams: all
+// launch metadata of the call (record descriptors, CTA tasks, commit jobs, error words, stream
+// offsets) goes up in one copy and every record after it, on the upload stream in call order; the
+// call's kernels (one grid each over all its records) and the read-back of its error words follow
+// on the call's kernel stream. Queued calls therefore overlap one call's decode with the next
+// call's uploads. A record's destinations are written by the error-gated commit kernel (device
+// destinations), or copied back after the kernels (host destinations).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -14,6 +15,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <utility>
 #include <vector>
 
 #include "bufs.h"
@@ -26,32 +28,49 @@
 namespace wexb {
 namespace {
 
+// Kernel streams per device, handed to calls in turn, so that the kernels of consecutive queued
+// calls may overlap.
 constexpr int kLanes = 4;
 
-// A call's device workspace: a copy stream, kLanes kernel streams, grown buffers. Pooled per device and
-// never freed (the reference's pools, c/tools/wex_cuda_bridge.cu:111-153, for the same reason: CUDA
+// The streams of a device, shared by every call on it: uploads in call order on `upload`, each
+// call's kernels and read-back on the next kernel stream. Created once, never destroyed (CUDA
 // cannot be called while the process unloads).
+struct Queues {
+    cudaStream_t upload = nullptr, lane[kLanes] = {};
+    unsigned next = 0;
+    bool ok = false;
+};
+std::mutex g_queues_mu;
+Queues g_queues[kMaxDevices];
+
+// The device's upload stream and the kernel stream of a new call (device current).
+bool device_streams(int device, cudaStream_t *up, cudaStream_t *st) {
+    std::lock_guard<std::mutex> lock(g_queues_mu);
+    Queues &q = g_queues[device];
+    if (!q.ok) {
+        bool ok = cudaStreamCreateWithFlags(&q.upload, cudaStreamNonBlocking) == cudaSuccess;
+        for (int l = 0; ok && l < kLanes; ++l) ok = cudaStreamCreateWithFlags(&q.lane[l], cudaStreamNonBlocking) == cudaSuccess;
+        if (!ok) { (void)cudaGetLastError(); return false; }   // streams made so far leak, on CUDA failure only
+        q.ok = true;
+    }
+    *up = q.upload;
+    *st = q.lane[q.next];
+    q.next = (q.next + 1u) % kLanes;
+    return true;
+}
+
+// A call's workspace: events and grown buffers. Pooled per device and never freed (the reference's
+// pools, c/tools/wex_cuda_bridge.cu:111-153, for the same reason). A queued call holds its
+// workspace until it is waited for.
 struct Workspace {
     int device = -1;
-    cudaStream_t copy = nullptr, lane[kLanes] = {};
-    cudaEvent_t lane_done[kLanes] = {};
-    std::vector<cudaEvent_t> uploaded;
+    cudaEvent_t uploads_done = nullptr, done = nullptr;
     DevBuf drec, dscratch, dmeta;
     PinBuf hmeta;
     bool init(int dev) {
-        if (cudaStreamCreateWithFlags(&copy, cudaStreamNonBlocking) != cudaSuccess) return false;
-        for (int l = 0; l < kLanes; ++l)
-            if (cudaStreamCreateWithFlags(&lane[l], cudaStreamNonBlocking) != cudaSuccess ||
-                cudaEventCreateWithFlags(&lane_done[l], cudaEventDisableTiming) != cudaSuccess) return false;
+        if (cudaEventCreateWithFlags(&uploads_done, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&done, cudaEventDisableTiming) != cudaSuccess) return false;
         device = dev;
-        return true;
-    }
-    bool events(size_t n) {
-        while (uploaded.size() < n) {
-            cudaEvent_t e;
-            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
-            uploaded.push_back(e);
-        }
         return true;
     }
 };
@@ -73,13 +92,6 @@ void give(Workspace *w) {
     std::lock_guard<std::mutex> lock(g_pool_mu);
     g_idle[w->device].push_back(w);
 }
-struct Lease {
-    Workspace *w;
-    explicit Lease(int device) : w(take(device)) {}
-    ~Lease() { give(w); }
-    Lease(const Lease &) = delete;
-    Lease &operator=(const Lease &) = delete;
-};
 
 // Byte layout of a call's metadata block (host pinned, copied to the device in one piece).
 struct MetaLayout {
@@ -97,71 +109,78 @@ struct MetaLayout {
 };
 
 enum class Dest { Device, Host, HostChecked };
+constexpr int kPending = 2;
 
-// n records (host memory) through the pipeline. dst_scale / dst_weight (Device) or dst_host (Host:
-// copied back after the kernels; HostChecked: copied back only after a clean decode). Follows the
-// reference batch's argument and status rules (c/tools/wex_cuda_bridge.cu:388-487).
-int run_batch(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
-              unsigned char *const *dst_scale, unsigned char *const *dst_weight, unsigned char *const *dst_host,
-              Dest mode, int *status) {
-    if (n <= 0) return 0;
+// One batch call between its submit and its finish.
+struct Call {
+    int n = 0, device = -1;
+    Dest mode = Dest::Device;
+    unsigned char *const *dst_host = nullptr;
+    std::vector<Plan> plans;
+    std::vector<int> status, pend;
+    std::vector<size_t> scr_off;
+    Workspace *w = nullptr;
+    size_t k = 0, broken_at = 0;
+    MetaLayout L;
+    int failures() const { int bad = 0; for (int v : status) bad += v != 0; return bad; }
+    void settle(int v) { for (int &s : status) if (s == kPending) s = v; }
+};
+
+// Validates n records (host memory) and queues their pipeline: dst_scale / dst_weight (Device) or
+// dst_host (Host: copied back after the kernels; HostChecked: copied back by finish() only after a
+// clean decode). Argument and status rules of the reference batch (c/tools/wex_cuda_bridge.cu:388-487).
+// False when nothing could be queued (c.status then final).
+bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
+            unsigned char *const *dst_scale, unsigned char *const *dst_weight, unsigned char *const *dst_host, Dest mode) {
     const bool host_dst = mode != Dest::Device;
-    if (!entries || !records || !(host_dst ? dst_host != nullptr : (dst_scale && dst_weight)) || !status) return n;
-    const int PENDING = 2;
-    std::vector<Plan> plans((size_t)n);
-    std::vector<int> pend;
+    c.n = n; c.device = device; c.mode = mode; c.dst_host = dst_host;
+    c.plans.assign((size_t)n, Plan{});
+    c.status.assign((size_t)n, -1);
     for (int i = 0; i < n; ++i) {
-        status[i] = -1;
         const WexEntry *e = entries[i];
         if (!e || !records[i]) continue;
         bool targets = host_dst ? dst_host[i] != nullptr : true;
         if (!host_dst) for (int m = 0; m < 3; ++m) if (!dst_scale[3 * i + m] || !dst_weight[3 * i + m]) targets = false;
-        if (!targets || plan_record(e, records[i], &plans[(size_t)i])) continue;
-        if (!model_registered(plans[(size_t)i].model_id)) { status[i] = 1; continue; }
-        status[i] = PENDING;
-        pend.push_back(i);
+        if (!targets || plan_record(e, records[i], &c.plans[(size_t)i])) continue;
+        if (!model_registered(c.plans[(size_t)i].model_id)) { c.status[(size_t)i] = 1; continue; }
+        c.status[(size_t)i] = kPending;
+        c.pend.push_back(i);
     }
-    auto failures = [&] { int bad = 0; for (int i = 0; i < n; ++i) bad += status[i] != 0; return bad; };
-    auto finish = [&](int v) { for (int i = 0; i < n; ++i) if (status[i] == PENDING) status[i] = v; };
-    if (pend.empty()) return failures();
+    if (c.pend.empty()) return false;
     if (device < 0 || device >= kMaxDevices || cudaSetDevice(device) != cudaSuccess) {
-        (void)cudaGetLastError(); finish(1); return failures();
+        (void)cudaGetLastError(); c.settle(1); return false;
     }
-    Lease lease(device);
-    Workspace *w = lease.w;
-    if (!w) { finish(1); return failures(); }
-    // device tables of every record's model
-    std::vector<Nr3Tables> tabs(pend.size());
+    std::vector<Nr3Tables> tabs;   // device tables of every record's model
     {
         std::vector<int> keep;
-        std::vector<Nr3Tables> kt;
-        for (size_t j = 0; j < pend.size(); ++j) {
-            if (model_tables(plans[(size_t)pend[j]].model_id, device, &tabs[j])) { status[pend[j]] = 1; continue; }
-            keep.push_back(pend[j]); kt.push_back(tabs[j]);
+        for (int i : c.pend) {
+            Nr3Tables t;
+            if (model_tables(c.plans[(size_t)i].model_id, device, &t)) { c.status[(size_t)i] = 1; continue; }
+            keep.push_back(i); tabs.push_back(t);
         }
-        pend.swap(keep); tabs.swap(kt);
+        c.pend.swap(keep);
     }
-    const size_t k = pend.size();
-    if (!k) return failures();
+    const size_t k = c.k = c.pend.size();
+    if (!k) return false;
+    Workspace *w = c.w = take(device);
+    if (!w) { c.settle(1); return false; }
     // layout
     const int wthreads = weight_threads();
-    std::vector<size_t> rec_off(k), scr_off(k), off_off(k), s0(k + 1), w0(k + 1);
+    std::vector<size_t> rec_off(k), off_off(k);
+    c.scr_off.assign(k, 0);
     std::vector<Nr3Task> stasks, wtasks;
     size_t rec_bytes = 0, scr_bytes = 0, noffs = 0;
     for (size_t j = 0; j < k; ++j) {
-        const Plan &p = plans[(size_t)pend[j]];
+        const Plan &p = c.plans[(size_t)c.pend[j]];
         rec_off[j] = rec_bytes; rec_bytes += align_up(p.total, 256);
-        scr_off[j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
+        c.scr_off[j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
         off_off[j] = noffs; noffs += p.streams() + 1;
-        s0[j] = stasks.size(); w0[j] = wtasks.size();
         plan_tasks(p, (uint32_t)j, wthreads, stasks, wtasks);
     }
-    s0[k] = stasks.size(); w0[k] = wtasks.size();
-    MetaLayout L;
+    MetaLayout &L = c.L;
     L.compute(k, stasks.size(), wtasks.size(), host_dst ? 0 : k, noffs);
-    if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total) ||
-        !w->events(k)) {
-        finish(1); return failures();
+    if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total)) {
+        c.settle(1); give(w); c.w = nullptr; return false;
     }
     uint8_t *hm = w->hmeta.p, *dm = w->dmeta.p;
     Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + L.recs);
@@ -176,9 +195,9 @@ int run_batch(int n, const WexEntry *const *entries, const unsigned char *const 
     std::memcpy(hm + L.stasks, stasks.data(), stasks.size() * sizeof(Nr3Task));
     std::memcpy(hm + L.wtasks, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
     for (size_t j = 0; j < k; ++j) {
-        const int i = pend[j];
-        const Plan &p = plans[(size_t)i];
-        uint8_t *scr = w->dscratch.p + scr_off[j];
+        const int i = c.pend[j];
+        const Plan &p = c.plans[(size_t)i];
+        uint8_t *scr = w->dscratch.p + c.scr_off[j];
         plan_offsets(p, hoffs + off_off[j]);
         plan_descriptor(p, tabs[j], w->drec.p + rec_off[j], reinterpret_cast<const uint32_t *>(dm + L.offs) + off_off[j],
                         scr, derrs + j, &hrecs[j]);
@@ -192,59 +211,89 @@ int run_batch(int n, const WexEntry *const *entries, const unsigned char *const 
             J.error = derrs + j;
         }
     }
-    // enqueue
-    size_t broken_at = k;
-    bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, w->copy) == cudaSuccess;
+    // enqueue: metadata and records on the upload stream; then, on the call's kernel stream, the
+    // three kernels (every record of the call in one grid each) and the read-back of the error words
+    cudaStream_t up = nullptr, st = nullptr;
+    if (!device_streams(device, &up, &st)) { c.settle(1); give(w); c.w = nullptr; return false; }
+    bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, up) == cudaSuccess;
     for (size_t j = 0; ok && j < k; ++j)
-        ok = cudaMemcpyAsync(w->drec.p + rec_off[j], records[pend[j]], plans[(size_t)pend[j]].total, cudaMemcpyHostToDevice,
-                             w->copy) == cudaSuccess &&
-             cudaEventRecord(w->uploaded[j], w->copy) == cudaSuccess;
-    if (!ok) broken_at = 0;
-    const int lanes = (int)std::min<size_t>(k, kLanes);
-    for (size_t j = 0; j < broken_at; ++j) {
-        const int i = pend[j];
-        const Plan &p = plans[(size_t)i];
-        cudaStream_t st = w->lane[j % kLanes];
-        const uint8_t *scr = w->dscratch.p + scr_off[j];
-        ok = cudaStreamWaitEvent(st, w->uploaded[j], 0) == cudaSuccess &&
-             launch_nr3_scales(drecs, dst_tasks + s0[j], (uint32_t)(s0[j + 1] - s0[j]), st) == cudaSuccess &&
-             launch_nr3_weights(drecs, dwt_tasks + w0[j], (uint32_t)(w0[j + 1] - w0[j]), wthreads, st) == cudaSuccess;
-        if (ok && mode == Dest::Device) ok = launch_commit(djobs + j, 1, st) == cudaSuccess;
-        if (ok && mode == Dest::Host) {
-            ok = cudaMemcpyAsync(dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-                 cudaMemcpyAsync(dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost,
-                                 st) == cudaSuccess;
-        }
-        if (!ok) { (void)cudaGetLastError(); broken_at = j; }
+        ok = cudaMemcpyAsync(w->drec.p + rec_off[j], records[c.pend[j]], c.plans[(size_t)c.pend[j]].total,
+                             cudaMemcpyHostToDevice, up) == cudaSuccess;
+    // the kernel stream waits for every upload, so `done`, recorded on it last, covers the whole call
+    if (cudaEventRecord(w->uploads_done, up) != cudaSuccess || cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess) {
+        (void)cudaGetLastError();
+        (void)cudaStreamSynchronize(up);
+        ok = false;
     }
-    bool synced = true;
-    for (int l = 0; l < lanes; ++l)
-        if (cudaEventRecord(w->lane_done[l], w->lane[l]) != cudaSuccess ||
-            cudaStreamWaitEvent(w->copy, w->lane_done[l], 0) != cudaSuccess) synced = false;
-    if (synced && cudaMemcpyAsync(herrs, derrs, k * 4, cudaMemcpyDeviceToHost, w->copy) != cudaSuccess) synced = false;
-    for (int l = 0; l < lanes; ++l) if (cudaStreamSynchronize(w->lane[l]) != cudaSuccess) synced = false;
-    if (cudaStreamSynchronize(w->copy) != cudaSuccess) synced = false;
+    if (ok)
+        ok = launch_nr3_scales(drecs, dst_tasks, (uint32_t)stasks.size(), st) == cudaSuccess &&
+             launch_nr3_weights(drecs, dwt_tasks, (uint32_t)wtasks.size(), wthreads, st) == cudaSuccess &&
+             (mode != Dest::Device || launch_commit(djobs, (uint32_t)k, st) == cudaSuccess);
+    for (size_t j = 0; ok && mode == Dest::Host && j < k; ++j) {
+        const int i = c.pend[j];
+        const Plan &p = c.plans[(size_t)i];
+        const uint8_t *scr = w->dscratch.p + c.scr_off[j];
+        ok = cudaMemcpyAsync(dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+             cudaMemcpyAsync(dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost,
+                             st) == cudaSuccess;
+    }
+    c.broken_at = ok ? k : 0;
+    if (!ok) (void)cudaGetLastError();
+    if (cudaMemcpyAsync(herrs, derrs, k * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaEventRecord(w->done, st) != cudaSuccess) {
+        (void)cudaGetLastError();
+        (void)cudaStreamSynchronize(st);
+        c.broken_at = 0;
+    }
+    return true;
+}
+
+// Waits for a submitted call, writes its statuses, releases its workspace.
+void finish(Call &c) {
+    Workspace *w = c.w;
+    if (!w) { c.settle(1); return; }
+    (void)cudaSetDevice(c.device);
+    const bool synced = cudaEventSynchronize(w->done) == cudaSuccess;
     if (!synced) (void)cudaGetLastError();
-    for (size_t j = 0; j < k; ++j) {
-        const int i = pend[j];
-        status[i] = (j >= broken_at || !synced) ? 1 : herrs[j] ? -1 : 0;
-        if (status[i] == -1) report_error_bits(herrs[j]);
+    const uint32_t *herrs = reinterpret_cast<const uint32_t *>(w->hmeta.p + c.L.errs);
+    for (size_t j = 0; j < c.k; ++j) {
+        const int i = c.pend[j];
+        c.status[(size_t)i] = (j >= c.broken_at || !synced) ? 1 : herrs[j] ? -1 : 0;
+        if (c.status[(size_t)i] == -1) report_error_bits(herrs[j]);
     }
-    if (mode == Dest::HostChecked && synced) {   // the single to-host call: copy back only a clean decode
-        for (size_t j = 0; j < k; ++j) {
-            const int i = pend[j];
-            if (status[i]) continue;
-            const Plan &p = plans[(size_t)i];
-            const uint8_t *scr = w->dscratch.p + scr_off[j];
-            if (cudaMemcpy(dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
-                cudaMemcpy(dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    if (c.mode == Dest::HostChecked && synced) {   // the single to-host call: copy back only a clean decode
+        for (size_t j = 0; j < c.k; ++j) {
+            const int i = c.pend[j];
+            if (c.status[(size_t)i]) continue;
+            const Plan &p = c.plans[(size_t)i];
+            const uint8_t *scr = w->dscratch.p + c.scr_off[j];
+            if (cudaMemcpy(c.dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
+                cudaMemcpy(c.dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost) != cudaSuccess) {
                 (void)cudaGetLastError();
-                status[i] = 1;   // the slab may now be partly written: the caller treats 1 as "decode again"
+                c.status[(size_t)i] = 1;   // the slab may now be partly written: the caller treats 1 as "decode again"
             }
         }
     }
-    return failures();
+    give(w);
+    c.w = nullptr;
 }
+
+int run_batch(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
+              unsigned char *const *dst_scale, unsigned char *const *dst_weight, unsigned char *const *dst_host,
+              Dest mode, int *status) {
+    if (n <= 0) return 0;
+    const bool host_dst = mode != Dest::Device;
+    if (!entries || !records || !(host_dst ? dst_host != nullptr : (dst_scale && dst_weight)) || !status) return n;
+    Call c;
+    if (submit(c, n, entries, records, device, dst_scale, dst_weight, dst_host, mode)) finish(c);
+    for (int i = 0; i < n; ++i) status[i] = c.status[(size_t)i];
+    return c.failures();
+}
+
+// ---- queued calls (tickets) ----------------------------------------------------------------------
+std::mutex g_calls_mu;
+std::vector<std::pair<int, Call *>> g_calls;
+int g_next_ticket = 0;
 
 }  // namespace
 }  // namespace wexb
@@ -309,6 +358,34 @@ WEXB_API int wex_cuda_host_unregister(void *pointer) {
     if (!pointer) return -1;
     if (cudaHostUnregister(pointer) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
     return 0;
+}
+
+WEXB_API int wexb_batch_submit(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
+                               unsigned char *const *dst_scale, unsigned char *const *dst_weight) {
+    if (n <= 0 || !entries || !records || !dst_scale || !dst_weight) return -1;
+    Call *c = new (std::nothrow) Call();
+    if (!c) return -3;
+    (void)submit(*c, n, entries, records, device, dst_scale, dst_weight, nullptr, Dest::Device);   // statuses final if not queued
+    std::lock_guard<std::mutex> lock(g_calls_mu);
+    const int t = g_next_ticket;
+    g_next_ticket = (g_next_ticket + 1) & 0x7fffffff;
+    g_calls.emplace_back(t, c);
+    return t;
+}
+
+WEXB_API int wexb_batch_wait(int ticket, int *status) {
+    Call *c = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_calls_mu);
+        for (size_t i = 0; i < g_calls.size(); ++i)
+            if (g_calls[i].first == ticket) { c = g_calls[i].second; g_calls.erase(g_calls.begin() + (std::ptrdiff_t)i); break; }
+    }
+    if (!c) return -1;
+    if (c->w) finish(*c);
+    if (status) for (int i = 0; i < c->n; ++i) status[i] = c->status[(size_t)i];
+    const int bad = c->failures();
+    delete c;
+    return bad;
 }
 
 // ---- resident records --------------------------------------------------------------------------

@@ -32,17 +32,33 @@ uint32_t fnv1a(const uint8_t *p, size_t n) {
     return h ? h : 1u;
 }
 
-// Table image: wrows [3][567][8 u32], wsf [3][567][16 u32], sdir [3][16384 u32], ssym [3][16384 u8].
+// Table image: per matrix the two-level weight block (wnr3.cuh), then sdir [3][16384 u32], ssym [3][16384 u8].
 void build_image(const uint8_t *blob, std::vector<uint8_t> &img) {
     img.assign(kTableBytes, 0);
-    uint32_t *wrows = reinterpret_cast<uint32_t *>(img.data());
-    uint32_t *wsf = reinterpret_cast<uint32_t *>(img.data() + kWRowsBytes);
-    uint32_t *sdir = reinterpret_cast<uint32_t *>(img.data() + kWRowsBytes + kWsfBytes);
-    uint8_t *ssym = img.data() + kWRowsBytes + kWsfBytes + kSdirBytes;
-    for (uint32_t r = 0; r < 3 * kContexts; ++r) {
-        const uint8_t *c = blob + 32 + 34u * r;
-        for (uint32_t i = 0; i < 8; ++i) wrows[8 * r + i] = rd16(c + 4 * i) | rd16(c + 4 * i + 2) << 16;
-        for (uint32_t s = 0; s < 16; ++s) wsf[16 * r + s] = rd16(c + 2 * s) | (rd16(c + 2 * s + 2) - rd16(c + 2 * s)) << 16;
+    uint32_t *sdir = reinterpret_cast<uint32_t *>(img.data() + kWTableBytes);
+    uint8_t *ssym = img.data() + kWTableBytes + kSdirBytes;
+    for (uint32_t m = 0; m < 3; ++m) {
+        uint32_t *l1 = reinterpret_cast<uint32_t *>(img.data() + (size_t)m * kWBlockBytes);
+        uint32_t *l2 = reinterpret_cast<uint32_t *>(img.data() + (size_t)m * kWBlockBytes + kWL1Bytes);
+        for (uint32_t srel = 0; srel < 7; ++srel) {
+            for (uint32_t pair = 0; pair < kPairs; ++pair) {
+                uint32_t pm = 8, mx = 8;   // pair 36: the block start
+                if (pair + 1 < kPairs) {
+                    for (mx = 0; (mx + 1) * (mx + 2) / 2 <= pair; ++mx) {}
+                    pm = pair - mx * (mx + 1) / 2;
+                }
+                const uint32_t idx = srel * kPairs + pair;
+                const uint8_t *c = blob + 32 + 34u * (m * kContexts + (srel * 9u + pm) * 9u + mx);
+                uint32_t cdf[17];
+                for (uint32_t k = 0; k < 17; ++k) cdf[k] = rd16(c + 2 * k);
+                l1[2 * idx] = cdf[4] | cdf[8] << 16;
+                l1[2 * idx + 1] = cdf[12] + 0x4000u;
+                for (uint32_t k = 0; k < 16; ++k) {
+                    const uint32_t f = cdf[k + 1] - cdf[k];
+                    l2[16 * idx + k] = cdf[k] << 18 | (f ? f - 1u : 0u) << 4 | k;
+                }
+            }
+        }
     }
     for (uint32_t m = 0; m < 3; ++m) {
         const uint8_t *c = blob + 32 + 3u * kContexts * 34u + 514u * m;
@@ -109,10 +125,9 @@ int model_tables(uint32_t id, int device, Nr3Tables *out) {
         m->dev[device] = p;
     }
     uint8_t *p = m->dev[device];
-    out->wrows = reinterpret_cast<const uint4 *>(p);
-    out->wsf = reinterpret_cast<const uint32_t *>(p + kWRowsBytes);
-    out->sdir = reinterpret_cast<const uint32_t *>(p + kWRowsBytes + kWsfBytes);
-    out->ssym = p + kWRowsBytes + kWsfBytes + kSdirBytes;
+    out->wblk = p;
+    out->sdir = reinterpret_cast<const uint32_t *>(p + kWTableBytes);
+    out->ssym = p + kWTableBytes + kSdirBytes;
     return 0;
 }
 
@@ -227,8 +242,8 @@ void plan_tasks(const Plan &p, uint32_t rec, int wthreads, std::vector<Nr3Task> 
 int weight_threads() {
     static int v = [] {
         const char *s = std::getenv("WEXB_WEIGHT_THREADS");
-        int t = s ? std::atoi(s) : 128;
-        return (t >= 32 && t <= kWeightThreadsMax && t % 32 == 0) ? t : 128;
+        const int t = s ? std::atoi(s) : 256;
+        return t == 128 ? 128 : 256;
     }();
     return v;
 }

@@ -22,21 +22,29 @@ constexpr uint32_t kModelBytes = 32u + 3u * kContexts * 34u + 3u * 514u;   // 59
 constexpr uint32_t kErrStruct = 1, kErrHash = 2, kErrCeil = 4, kErrCz = 8, kErrTimeout = 16;
 
 // Per model, per device: lookup tables derived from the WNM2 blob on the host.
-//   wrows[m][ctx]    cdf[0..15] of a weight context as 8 packed u16 pairs (two uint4)
-//   wsf[m][ctx][s]   start | frequency << 16 of weight symbol s
+//
+// Weight contexts. The reference's context (srel * 9 + pm) * 9 + mx (c/wex_neural_rans.h:130-133, 498-512)
+// only ever takes pm <= mx < 8 (pm the previous magnitude, mx the block's maximum so far) or the
+// block start pm = mx = 8, so each srel has 37 reachable contexts: pair index mx (mx + 1) / 2 + pm,
+// and 36 for the block start. The tables hold those 7 x 37 = 259 contexts of each matrix:
+//   level 1 [259] of 8 B   cdf[4] | cdf[8] << 16,  cdf[12] + 2^14   (picks the quartile q)
+//   level 2 [259][4] of 16 B, quartile q: for i = 4q .. 4q + 3 the word
+//           cdf[i] << 18 | (freq[i] - 1) << 4 | i   (a zero-frequency symbol is never selected)
 //   sdir[m][slot]    (slot - start) | frequency << 14 of the scale symbol owning slot
 //   ssym[m][slot]    that scale symbol
 struct Nr3Tables {
-    const uint4 *wrows;
-    const uint32_t *wsf;
+    const uint8_t *wblk;
     const uint32_t *sdir;
     const uint8_t *ssym;
 };
-constexpr size_t kWRowsBytes = 3ull * kContexts * 32u;
-constexpr size_t kWsfBytes = 3ull * kContexts * 16u * 4u;
+constexpr uint32_t kPairs = 37;                                        // contexts per srel
+constexpr uint32_t kWContexts = 7u * kPairs;                           // 259
+constexpr uint32_t kWL1Bytes = (kWContexts * 8u + 15u) & ~15u;         // 2,080
+constexpr uint32_t kWBlockBytes = kWL1Bytes + kWContexts * 64u;        // 18,656 per matrix
+constexpr size_t kWTableBytes = 3ull * kWBlockBytes;
 constexpr size_t kSdirBytes = 3ull * kTotal * 4u;
 constexpr size_t kSsymBytes = 3ull * kTotal;
-constexpr size_t kTableBytes = kWRowsBytes + kWsfBytes + kSdirBytes + kSsymBytes;
+constexpr size_t kTableBytes = kWTableBytes + kSdirBytes + kSsymBytes;
 
 // One record of a launch, in device memory.
 struct Nr3Record {
@@ -70,7 +78,7 @@ struct CommitJob {
 };
 
 constexpr int kScaleThreads = 64;
-constexpr int kWeightThreadsMax = 256;
+constexpr int kWeightThreadsMax = 256;   // weight CTAs have 128 or 256 threads (WEXB_WEIGHT_THREADS)
 
 cudaError_t launch_nr3_scales(const Nr3Record *recs, const Nr3Task *tasks, uint32_t ntasks, cudaStream_t st);
 cudaError_t launch_nr3_weights(const Nr3Record *recs, const Nr3Task *tasks, uint32_t ntasks, int threads,

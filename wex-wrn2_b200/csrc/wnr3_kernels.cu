@@ -6,10 +6,13 @@
 // cp.async copies kept 24 words ahead of the read position (ring word w of lane l at
 // ring[(w % 32) * blockDim + l]: conflict-free whatever position each lane is at).
 //
-// Weight symbol lookup: the 16 cumulative frequencies of the context are compared with the slot
-// all at once (packed 16-bit subtraction, sign bits gathered with PRMT, one POPC), then one shared
-// load fetches the symbol's start and frequency. Renormalisation is branch-free: from a valid
-// state a symbol leaves at least 2^9, so it takes 0, 1 or 2 bytes, read as one big-endian pair.
+// Weight symbol lookup, two shared loads: the context's level-1 entry (8 B) gives the quartile q
+// of the slot from three packed 16-bit comparisons (each a subtraction whose flag bit is set
+// exactly when cdf <= slot), then the quartile's four symbol words (16 B) are compared against
+// slot << 18 | 0x3ffff, and the last one not above it is the symbol, carrying its start,
+// frequency - 1 and index. Renormalisation is branch-free: from a valid state a symbol leaves at
+// least 2^9, so it takes 0, 1 or 2 bytes (from the count of leading zeros), read as one
+// big-endian pair.
 #include "wnr3.cuh"
 
 namespace wexb {
@@ -140,17 +143,6 @@ struct Reader {
     }
 };
 
-// Symbol of `slot` in a 16-entry cumulative row (cdf[0] = 0 < cdf[1] < ... < cdf[15] < 2^14), i.e.
-// the number of entries <= slot, minus one. Per 16-bit half, (slot | 0x8000) - cdf keeps bit 15
-// set exactly when cdf <= slot and never borrows from the other half.
-__device__ __forceinline__ uint32_t row_symbol(const uint4 a, const uint4 b, uint32_t slot) {
-    const uint32_t g = slot * 0x10001u | 0x80008000u;
-    const uint32_t p0 = __byte_perm(g - a.x, g - a.y, 0x7531), p1 = __byte_perm(g - a.z, g - a.w, 0x7531);
-    const uint32_t p2 = __byte_perm(g - b.x, g - b.y, 0x7531), p3 = __byte_perm(g - b.z, g - b.w, 0x7531);
-    const uint32_t m = 0x80808080u;
-    return (uint32_t)__popc((p0 & m) | ((p1 & m) >> 1) | ((p2 & m) >> 2) | ((p3 & m) >> 3)) - 1u;
-}
-
 // Non-zero iff one of the eight nibbles of w is 8 (-0).
 __device__ __forceinline__ uint32_t has_neg_zero(uint32_t w) {
     const uint32_t t = w ^ 0x88888888u;
@@ -232,23 +224,76 @@ __global__ void __launch_bounds__(kScaleThreads) nr3_scales(const Nr3Record *__r
 }
 
 // ---- kernel B: weight streams -----------------------------------------------------------------
-constexpr uint32_t kRowBytes = kContexts * 32u, kSfBytes = kContexts * 64u;
+// A lane's payload ring for the weight kernel: word w of the stream (counted from the stream's
+// first word) lives in slot w % 32, slot 32 repeats slot 0, so the two words under any read
+// position are slots s and s + 1 with no wrap. Slot s of lane l is ring[s * kThreads + l].
+template <int kThreads>
+struct WeightReader {
+    uint32_t *ring;          // this lane's slot 0
+    const uint32_t *src;     // the stream's first word in the record
+    uint32_t bit;            // bit offset of the next payload byte from the stream's first word
+    uint32_t req;            // next word to request
+    uint32_t last;           // the stream's last word
 
-__global__ void __launch_bounds__(kWeightThreadsMax, 2) nr3_weights(const Nr3Record *__restrict__ recs,
-                                                                    const Nr3Task *__restrict__ tasks) {
+    __device__ __forceinline__ void copy(uint32_t w, bool pred) { cp4(ring + (w & 31u) * kThreads, src + w, pred); }
+
+    // Opens [begin, end) of the record (length >= 4, checked on the host); returns the initial state.
+    __device__ __forceinline__ uint32_t open(const uint32_t *rec, uint32_t begin, uint32_t end) {
+        src = rec + (begin >> 2);
+        last = ((end - 1u) >> 2) - (begin >> 2);
+        const uint32_t target = min(kAhead, last + 1u);
+        for (uint32_t w = 0; w < target; ++w) copy(w, true);
+        cp4(ring + 32u * kThreads, src, true);
+        req = target;
+        cp_commit();
+        cp_wait<0>();
+        const uint32_t v = __funnelshift_r(ring[0], ring[kThreads], (begin & 3u) * 8u);
+        bit = (begin & 3u) * 8u + 32u;
+        return __byte_perm(v, 0, 0x0123);   // big-endian bytes begin .. begin + 3
+    }
+    // Every 16 symbols (at most 32 bytes): keep kAhead words requested, then wait for the words of
+    // the previous request, which cover every byte the next 16 symbols can read.
+    __device__ __forceinline__ void refill() {
+        const uint32_t target = min((bit >> 5) + kAhead, last + 1u);
+#pragma unroll
+        for (uint32_t k = 0; k < 8; ++k) copy(req + k, req + k < target);
+        const uint32_t k0 = (0u - req) & 31u;   // the word of slot 0 among them, mirrored to slot 32
+        cp4(ring + 32u * kThreads, src + req + k0, k0 < 8u && req + k0 < target);
+        req = max(req, min(req + 8u, target));
+        cp_commit();
+        cp_wait<1>();
+    }
+    // The next two payload bytes as a big-endian pair in bits 16..31. Past the stream's end the
+    // ring holds stale words: consuming them is caught by the final position check.
+    __device__ __forceinline__ uint32_t peek() const {
+        const uint32_t *p = ring + ((bit >> 5) & 31u) * kThreads;
+        return __byte_perm(__funnelshift_r(p[0], p[kThreads], bit), 0, 0x0144);
+    }
+    __device__ __forceinline__ void drain() const { cp_wait<0>(); }
+    // x in [2^9, 2^31) after a symbol: shift in 0, 1 or 2 bytes until x >= 2^23.
+    __device__ __forceinline__ uint32_t renorm(uint32_t x, uint32_t two) {
+        const uint32_t bits = ((uint32_t)__clz(x) - 1u) & 24u;
+        bit += bits;
+        return __funnelshift_l(two, x, bits);
+    }
+};
+
+template <int kThreads>
+__global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const Nr3Record *__restrict__ recs,
+                                                                         const Nr3Task *__restrict__ tasks) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar;
-    const uint4 *rows = reinterpret_cast<const uint4 *>(smem);
-    const uint32_t *sf = reinterpret_cast<const uint32_t *>(smem + kRowBytes);
-    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kRowBytes + kSfBytes);
+    const uint2 *level1 = reinterpret_cast<const uint2 *>(smem);
+    const uint4 *level2 = reinterpret_cast<const uint4 *>(smem + kWL1Bytes);
+    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kWBlockBytes);
     const Nr3Task task = tasks[blockIdx.x];
     const Nr3Record &R = recs[task.rec];
     const uint32_t m = task.matrix;
     {
-        void *dst[2] = {smem, smem + kRowBytes};
-        const void *src[2] = {R.t.wrows + (size_t)m * kContexts * 2u, R.t.wsf + (size_t)m * kContexts * 16u};
-        const uint32_t bytes[2] = {kRowBytes, kSfBytes};
-        if (!stage_tables(&bar, dst, src, bytes, 2)) {
+        void *dst[1] = {smem};
+        const void *src[1] = {R.t.wblk + (size_t)m * kWBlockBytes};
+        const uint32_t bytes[1] = {kWBlockBytes};
+        if (!stage_tables(&bar, dst, src, bytes, 1)) {
             if (threadIdx.x == 0) atomicOr(R.error, kErrTimeout);
             return;
         }
@@ -259,8 +304,8 @@ __global__ void __launch_bounds__(kWeightThreadsMax, 2) nr3_weights(const Nr3Rec
     const uint32_t first = j * R.wchunk, blocks = min(R.wchunk, R.wcount[m] - first) / 32u;
     uint8_t *scales = R.out + R.soff[m] + first / 32u;   // coded scales; the ceil inverse edits them
     uint4 *out = reinterpret_cast<uint4 *>(R.out + R.wout[m] + first / 2u);
-    Reader rd{ring + threadIdx.x, blockDim.x, reinterpret_cast<const uint32_t *>(R.rec), 0, 0, 0};
-    uint32_t x = rd.open(begin, end);
+    WeightReader<kThreads> rd{ring + threadIdx.x, nullptr, 0, 0, 0};
+    uint32_t x = rd.open(reinterpret_cast<const uint32_t *>(R.rec), begin, end);
     if (x < kRansL || x >= (kRansL << 8)) { atomicOr(R.error, kErrStruct); rd.drain(); return; }
     const bool nr3 = R.flags & 256u, cz = nr3 && (R.flags & 8u), ceil = nr3 && ((R.flags >> m) & 1u);
     const int anchor = (int)((R.word24 >> (8u * m)) & 0xffu);
@@ -270,20 +315,32 @@ __global__ void __launch_bounds__(kWeightThreadsMax, 2) nr3_weights(const Nr3Rec
     for (uint32_t b = 0; b < blocks; ++b) {
         const uint32_t next_scale = b + 1 < blocks ? scales[b + 1] : 0u;
         const int d = (int)scale - anchor;
-        const uint32_t base = (uint32_t)(min(max(d, -3), 3) + 3) * 81u;
-        uint32_t ctx = base + 80u, top = 0, w[4] = {0, 0, 0, 0};   // context of "no previous, no maximum"
+        const uint32_t srel = (uint32_t)(min(max(d, -3), 3) + 3) * kPairs;
+        const uint2 *l1 = level1 + srel;
+        const uint4 *l2 = level2 + 4u * srel;
+        uint32_t idx = kPairs - 1u, top = 0, w[4] = {0, 0, 0, 0};   // the block-start context
 #pragma unroll
         for (uint32_t k = 0; k < 32; ++k) {
             if (k == 0 || k == 16) rd.refill();
-            const uint32_t two = rd.peek(), slot = x & (kTotal - 1u);
-            const uint32_t sym = row_symbol(rows[2u * ctx], rows[2u * ctx + 1u], slot);
-            const uint32_t e = sf[ctx * 16u + sym];
-            x = (e >> 16) * (x >> kPrec) + slot - (e & 0xffffu);
+            const uint32_t two = rd.peek();
+            const uint2 c = l1[idx];
+            // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]: bits 15 and 31 of
+            // (slot | 0x8000) * 0x10001 - (cdf[4] | cdf[8] << 16), bit 14 of that minus cdf[12] + 2^14
+            const uint32_t gs = (x & (kTotal - 1u)) * 0x10001u + 0x80008000u;
+            const uint32_t q = __popc(((gs - c.x) & 0x80008000u) | ((gs - c.y) & 0x4000u));
+            const uint4 e = l2[4u * idx + q];
+            const uint32_t key = x * (1u << 18) + 0x3ffffu;   // slot << 18 | 0x3ffff
+            uint32_t p = e.x;
+            p = key >= e.y ? e.y : p;
+            p = key >= e.z ? e.z : p;
+            p = key >= e.w ? e.w : p;
+            const uint32_t xs = x >> kPrec;
+            x = ((p >> 4) & 0x3fffu) * xs + xs + ((key - p) >> 18);   // freq * (x >> 14) + slot - start
             x = rd.renorm(x, two);
-            w[k / 8u] |= sym << (4u * (k % 8u));
-            const uint32_t mag = sym & 7u;
+            w[k / 8u] += (p & 15u) << (4u * (k % 8u));
+            const uint32_t mag = p & 7u;
             top = max(top, mag);
-            ctx = base + mag * 9u + top;
+            idx = ((top * top + top) >> 1) + mag;
         }
         if (nr3) {   // hash and checks on the coded nibbles, then the ceil inverse
             h = mm3_block(mm3_block(mm3_block(mm3_block(h, w[0]), w[1]), w[2]), w[3]);
@@ -304,7 +361,7 @@ __global__ void __launch_bounds__(kWeightThreadsMax, 2) nr3_weights(const Nr3Rec
     }
     rd.drain();
     const uint32_t expect = nr3 ? kRansL + (mm3_final(h, 16u + blocks * 16u) & 0x7fffffu) : kRansL;
-    if (rd.pos != end) atomicOr(R.error, kErrStruct);
+    if (rd.bit != (end - (begin & ~3u)) * 8u) atomicOr(R.error, kErrStruct);
     else if (x != expect) atomicOr(R.error, nr3 ? kErrHash : kErrStruct);
 }
 
@@ -327,14 +384,16 @@ __global__ void commit_regions(const CommitJob *__restrict__ jobs) {
 }
 
 constexpr size_t scale_smem(int threads) { return kTotal * 5u + (size_t)kRingWords * 4u * threads; }
-constexpr size_t weight_smem(int threads) { return kRowBytes + kSfBytes + (size_t)kRingWords * 4u * threads; }
+constexpr size_t weight_smem(int threads) { return kWBlockBytes + (size_t)(kRingWords + 1u) * 4u * threads; }
 
 }  // namespace
 
 cudaError_t prepare_nr3_kernels() {
     cudaError_t e = cudaFuncSetAttribute(nr3_scales, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scale_smem(kScaleThreads));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(nr3_weights, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)weight_smem(kWeightThreadsMax));
+        e = cudaFuncSetAttribute(nr3_weights<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)weight_smem(128));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(nr3_weights<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)weight_smem(256));
     return e;
 }
 
@@ -346,8 +405,9 @@ cudaError_t launch_nr3_scales(const Nr3Record *recs, const Nr3Task *tasks, uint3
 
 cudaError_t launch_nr3_weights(const Nr3Record *recs, const Nr3Task *tasks, uint32_t ntasks, int threads, cudaStream_t st) {
     if (!ntasks) return cudaSuccess;
-    if (threads < 32 || threads > kWeightThreadsMax || threads % 32) return cudaErrorInvalidValue;
-    nr3_weights<<<ntasks, threads, weight_smem(threads), st>>>(recs, tasks);
+    if (threads == 256) nr3_weights<256><<<ntasks, 256, weight_smem(256), st>>>(recs, tasks);
+    else if (threads == 128) nr3_weights<128><<<ntasks, 128, weight_smem(128), st>>>(recs, tasks);
+    else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 

@@ -42,6 +42,8 @@ def lib():
         L.wex_cuda_host_unregister.argtypes = [P]
         L.wexb_abi.restype = U32
         L.wexb_last_error_bits.restype = U32
+        L.wexb_batch_submit.argtypes = [I, P, P, I, P, P]
+        L.wexb_batch_wait.argtypes = [I, P]
         L.wexb_resident_create.argtypes = [I, P, P, I, P, P]
         L.wexb_resident_bytes.argtypes = [P]; L.wexb_resident_bytes.restype = SZ
         L.wexb_resident_decode.argtypes = [P, I, P, P, P, P]
@@ -115,6 +117,31 @@ def decode_batch_to_host(entries, records, device, dsts):
     bad = lib().wex_cuda_decode_batch_to_host(n, ep, _ptrs([b[0] for b in bufs]), device, _ptrs([o[0] for o in outs]),
                                               status)
     return bad, list(status)[:n]
+
+
+class Ticket:
+    """A queued device batch (wexb_batch_submit); keeps its arguments alive until wait()."""
+
+    def __init__(self, entries, records, device, dst_scale, dst_weight):
+        self.n = len(entries)
+        ep, keep_e = _entries(entries)
+        bufs = [_buf(r) for r in records]
+        sp, wp = _ptrs(dst_scale), _ptrs(dst_weight)
+        self._keep = (ep, keep_e, bufs, sp, wp)
+        self.ticket = lib().wexb_batch_submit(self.n, ep, _ptrs([b[0] for b in bufs]), device, sp, wp)
+        if self.ticket < 0:
+            raise RuntimeError(f'wexb_batch_submit: {self.ticket}')
+
+    def wait(self):
+        """(failures, statuses)."""
+        status = (ctypes.c_int * max(self.n, 1))()
+        bad = lib().wexb_batch_wait(self.ticket, status)
+        self._keep = None
+        return bad, list(status)[:self.n]
+
+
+def submit_batch_to_device(entries, records, device, dst_scale, dst_weight):
+    return Ticket(entries, records, device, dst_scale, dst_weight)
 
 
 def host_register(array):
