@@ -2,7 +2,7 @@
 
   libwexb200.so      the CUDA decoder and every C-ABI entry point declared in include/*.h
                      (nvcc, sm_100a only)
-  libwexb_tools.so   the writer-side tools (synthetic MXFP4 experts, WNR3 encoder), host C
+  libwexb_tools.so   the writer-side tools (synthetic MXFP4 experts, WNR3 and WNR4 encoders), host C
 
 Run `python wex-wrn2_b200/build.py` or call build(). Rebuilds only what is older than its sources.
 """
@@ -38,7 +38,7 @@ def cuda_deps():
 
 
 def build_tools(verbose=False):
-    src = [os.path.join(CSRC, 'tools', 'wexb_tools.c')]
+    src = [os.path.join(CSRC, 'tools', 'wexb_tools.c'), os.path.join(CSRC, 'tools', 'wexb_wnr4.c')]
     if _stale(TOOLS_LIB, src):
         os.makedirs(LIB, exist_ok=True)
         cmd = ['gcc', '-O2', '-Wall', '-Wextra', '-shared', '-fPIC', '-o', TOOLS_LIB] + src + ['-lm', '-lpthread']

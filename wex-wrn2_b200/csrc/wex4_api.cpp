@@ -16,6 +16,7 @@
 #include "nr3_host.h"
 #include "sha256.cuh"
 #include "wex4_tools.h"
+#include "wnr4_host.h"
 
 #define WEXB_API extern "C" __attribute__((visibility("default")))
 
@@ -28,7 +29,8 @@ enum { OK = 0, E_ARG = -1, E_MAGIC = -2, E_HASH = -3, E_VERSION = -4, E_FEATURE 
 constexpr uint32_t kMagic = 0x57455834u, kPage = 4096;
 constexpr uint64_t kMaxBlobs = 1u << 16, kMaxRecords = 1u << 24, kMaxTensors = 1u << 24, kMaxIndex = 1ull << 28,
                    kMaxDecoded = 1u << 30;
-constexpr uint32_t kCodecRaw = 0, kCodecWnr3 = 5, kCodecWbp1 = 6, kRecValueExact = 1, kRecExpert = 2, kBlobWnm2 = 1;
+constexpr uint32_t kCodecRaw = 0, kCodecWnr3 = 5, kCodecWbp1 = 6, kCodecWnr4 = 8, kRecValueExact = 1, kRecExpert = 2,
+                   kBlobWnm2 = 1, kBlobWnm4 = 3;
 
 uint64_t page_align(uint64_t n) { return (n + kPage - 1) & ~(uint64_t)(kPage - 1); }
 
@@ -347,6 +349,11 @@ struct Job {
     bool nr3 = false;
     Plan plan{};
     Nr3Tables tabs{};
+    bool w4 = false;                       // a codec-8 (WNR4 kind MX) expert slab
+    W4Geo geo{};
+    W4Tables w4tab{};
+    uint64_t soff[3] = {}, woff[3] = {};   // its six tensors in the decoded record
+    bool host_refused = false;             // its header or tile table failed the host checks
     uint8_t *out_dev = nullptr;            // decoded bytes on the device (after the run)
     int status = OK;
 };
@@ -374,6 +381,35 @@ int prepare_wnr3(const View &v, Job &j, uint32_t model_id, int device) {
     return OK;
 }
 
+// Host verdicts of a codec-8 record (draft WNR4 kind MX, decoded on request): a non-EXPERT record
+// holding the six tensors of an expert slab (scales [rows, cols] of U8 / F8_E8M0, then weights
+// [rows, 16 cols] of U8 / I8), owning itself, with a kind-3 WNM4 blob whose FNV-1a id is the entry's.
+// The record's own header, tile table, owner and model are checked when its tiles are planned.
+int prepare_wnr4(const View &v, Job &j, const uint8_t *file, int device) {
+    const Record &rec = j.rec;
+    if (rec.flags || rec.tensor_count != 6 || !rec.blob) return E_UNSUPPORTED;
+    const Blob b = v.blob(rec.blob - 1);
+    if (b.kind != kBlobWnm4) return E_UNSUPPORTED;
+    uint32_t geo[13] = {0};
+    for (int m = 0; m < 3; ++m) {
+        const Tensor s = v.tensor(rec.first_tensor + m), w = v.tensor(rec.first_tensor + 3 + m);
+        if (s.rank != 2 || w.rank != 2 || (s.dtype != 2 && s.dtype != 6) || (w.dtype != 2 && w.dtype != 3) ||
+            w.shape[0] != s.shape[0] || w.shape[1] != 16 * s.shape[1] || s.shape[0] > 65535 || s.shape[1] > 4095)
+            return E_UNSUPPORTED;
+        geo[1 + m] = (uint32_t)(s.shape[0] * s.shape[1]); geo[4 + m] = (uint32_t)s.shape[1];
+        geo[7 + m] = (uint32_t)s.offset; geo[10 + m] = (uint32_t)w.offset;
+        j.soff[m] = s.offset; j.woff[m] = w.offset;
+        if (w.offset & 15) return E_UNSUPPORTED;   // 16-byte stores of packed weights
+    }
+    if (!wnr4_geo(geo, &j.geo)) return E_UNSUPPORTED;
+    uint32_t id = 0;
+    const int st = wnr4_tables(file + b.offset, (size_t)b.bytes, device, &j.w4tab, &id);
+    if (st < 0 || id != b.id) return E_BLOB;
+    if (st) return E_ARG;
+    j.w4 = true;
+    return OK;
+}
+
 // Runs every job with pre == OK: upload, SHA-256 checks, RAW padding checks, WNR3 decodes into device
 // memory. Sets job.status (E_HASH before E_DATA, as the reference orders them) and job.out_dev.
 // Returns false on a CUDA failure. The caller holds g_space.mu.
@@ -388,7 +424,7 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     std::vector<size_t> at(jobs.size()), scr(jobs.size()), offs(jobs.size());
     size_t stage_bytes = 0, out_bytes = 0, scr_bytes = 0, noffs = 0;
     std::vector<Nr3Task> stasks, wtasks;
-    std::vector<size_t> nr3_of;   // job index of each WNR3 descriptor
+    std::vector<size_t> nr3_of, w4_of;   // job index of each WNR3 / WNR4 descriptor
     for (size_t i = 0; i < jobs.size(); ++i) {
         Job &j = jobs[i];
         if (j.pre != OK) continue;
@@ -400,14 +436,44 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
             nr3_of.push_back(i);
             out_bytes += align_up(j.rec.decoded, 256);
         }
+        if (j.w4) { w4_of.push_back(i); out_bytes += align_up(j.rec.decoded, 256); }
     }
-    const size_t n = jobs.size(), k = nr3_of.size();
+    const size_t n = jobs.size(), k = nr3_of.size(), k4 = w4_of.size();
+    // codec-8 tiles, planned from the host bytes against the staged copies, grouped by model
+    std::vector<W4Rec> w4info(k4);
+    std::vector<W4Job> w4jobs;
+    std::vector<std::pair<size_t, size_t>> w4runs;   // (first job, job count) per model
+    std::vector<const W4Tables *> w4tabs;
+    std::vector<int> w4bad(k4, 0);
+    for (size_t q0 = 0; q0 < k4;) {
+        const uint32_t id = jobs[w4_of[q0]].w4tab.id;
+        std::vector<W4Job> by_m[3];
+        size_t q = q0;
+        for (; q < k4 && jobs[w4_of[q]].w4tab.id == id; ++q) {
+            Job &j = jobs[w4_of[q]];
+            std::vector<W4Job> mine[3];
+            std::memset(&w4info[q], 0, sizeof(W4Rec));
+            // tile addresses as offsets into the staging buffer until it has its final size
+            if (!wnr4_plan(j.stored, j.rec.stored, j.geo, j.r, id, reinterpret_cast<const uint8_t *>(at[w4_of[q]]), (uint32_t)q,
+                           &w4info[q], mine)) {
+                w4bad[q] = 1;
+                continue;
+            }
+            for (int m = 0; m < 3; ++m) by_m[m].insert(by_m[m].end(), mine[m].begin(), mine[m].end());
+        }
+        const std::vector<W4Job> order = wnr4_launch_order(by_m);
+        w4runs.push_back({w4jobs.size(), order.size()});
+        w4tabs.push_back(&jobs[w4_of[q0]].w4tab);
+        w4jobs.insert(w4jobs.end(), order.begin(), order.end());
+        q0 = q;
+    }
     size_t m = 0;
     auto take = [&](size_t bytes) { size_t a = m; m = align_up(m + bytes, 256); return a; };
     const size_t o_recs = take(k * sizeof(Nr3Record)), o_st = take(stasks.size() * sizeof(Nr3Task)),
                  o_wt = take(wtasks.size() * sizeof(Nr3Task)), o_jobs = take(k * sizeof(CommitJob)),
                  o_sha = take(n * sizeof(ShaMsg)), o_exp = take(n * 32), o_zero = take(n * sizeof(ZeroJob)),
-                 o_err = take(n * 4), o_ver = take(n * 4), o_offs = take(noffs * 4);
+                 o_err = take(n * 4), o_ver = take(n * 4), o_offs = take(noffs * 4),
+                 o_w4rec = take(k4 * sizeof(W4Rec)), o_w4job = take(w4jobs.size() * sizeof(W4Job));
     if (!S.stage.grow(stage_bytes) || !S.out.grow(out_bytes) || !S.scratch.grow(scr_bytes) || !S.meta.grow(m) ||
         !S.hmeta.grow(m)) return false;
     uint8_t *hm = S.hmeta.p, *dm = S.meta.p;
@@ -447,6 +513,17 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
         }
         J.error = derr + i;
     }
+    for (W4Job &t : w4jobs)
+        if (t.tile) t.tile = S.stage.p + reinterpret_cast<uintptr_t>(t.tile);
+    for (size_t q = 0; q < k4; ++q) {
+        Job &j = jobs[w4_of[q]];
+        j.out_dev = S.out.p + out_at; out_at += align_up(j.rec.decoded, 256);
+        if (w4bad[q]) { j.host_refused = true; continue; }
+        for (int mm = 0; mm < 3; ++mm) { w4info[q].dst_s[mm] = j.out_dev + j.soff[mm]; w4info[q].dst_w[mm] = j.out_dev + j.woff[mm]; }
+        w4info[q].error = derr + w4_of[q];
+    }
+    if (k4) std::memcpy(hm + o_w4rec, w4info.data(), k4 * sizeof(W4Rec));
+    if (!w4jobs.empty()) std::memcpy(hm + o_w4job, w4jobs.data(), w4jobs.size() * sizeof(W4Job));
     std::memcpy(hm + o_st, stasks.data(), stasks.size() * sizeof(Nr3Task));
     std::memcpy(hm + o_wt, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
     cudaStream_t st = S.st;
@@ -461,7 +538,11 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + o_recs);
     ok = ok && launch_nr3_scales(drecs, reinterpret_cast<const Nr3Task *>(dm + o_st), (uint32_t)stasks.size(), st) == cudaSuccess &&
          launch_nr3_weights(drecs, reinterpret_cast<const Nr3Task *>(dm + o_wt), (uint32_t)wtasks.size(), weight_threads(), st) == cudaSuccess &&
-         launch_commit(reinterpret_cast<const CommitJob *>(dm + o_jobs), (uint32_t)k, st) == cudaSuccess &&
+         launch_commit(reinterpret_cast<const CommitJob *>(dm + o_jobs), (uint32_t)k, st) == cudaSuccess;
+    for (size_t g = 0; ok && g < w4runs.size(); ++g)
+        ok = launch_wnr4(*w4tabs[g], reinterpret_cast<const W4Job *>(dm + o_w4job) + w4runs[g].first,
+                         (uint32_t)w4runs[g].second, reinterpret_cast<const W4Rec *>(dm + o_w4rec), st) == cudaSuccess;
+    ok = ok &&
          cudaMemcpyAsync(hm + o_err, dm + o_err, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
          cudaMemcpyAsync(hm + o_ver, dm + o_ver, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     if (cudaStreamSynchronize(st) != cudaSuccess) ok = false;
@@ -471,6 +552,7 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
         Job &j = jobs[i];
         if (j.pre != OK) { j.status = j.pre; continue; }
         if (j.expect_sha && hver[i]) j.status = E_HASH;
+        else if (j.host_refused) j.status = E_DATA;
         else if (herr[i]) { j.status = E_DATA; if (j.nr3) report_error_bits(herr[i]); }
         else j.status = OK;
     }
@@ -541,7 +623,7 @@ WEXB_API int wex4_decode_record_buf(const unsigned char *page, uint64_t file_byt
     else if (rec.codec != kCodecRaw) j.pre = E_UNSUPPORTED;
     const int pre = j.pre;
     if (pre != OK && !j.expect_sha) return pre;
-    if (pre != OK) { j.pre = OK; j.nr3 = false; j.rec.codec = 0xffff; }   // its hash is still checked first
+    if (pre != OK) { j.pre = OK; j.nr3 = false; j.w4 = false; j.rec.codec = 0xffff; }   // its hash is still checked first
     std::lock_guard<std::mutex> lock(g_space.mu);
     if (!run_jobs(jobs, device)) return E_ARG;
     if (j.status == E_HASH) return E_HASH;
@@ -587,6 +669,7 @@ WEXB_API int wex4_check(const unsigned char *file, uint64_t len, int flags, unsi
             continue;
         }
         if (j.rec.codec == kCodecWnr3) j.pre = prepare_wnr3(v, j, j.rec.blob ? model_ids[j.rec.blob - 1] : 0, device);
+        else if (j.rec.codec == kCodecWnr4 && (flags & WEX4_CHECK_CODEC8)) j.pre = prepare_wnr4(v, j, file, device);
         else if (j.rec.codec != kCodecRaw) j.pre = E_UNSUPPORTED;
     }
     std::lock_guard<std::mutex> lock(g_space.mu);
@@ -594,7 +677,7 @@ WEXB_API int wex4_check(const unsigned char *file, uint64_t len, int flags, unsi
     std::vector<int> pre(h.records);
     for (uint32_t r = 0; r < h.records; ++r) {
         pre[r] = jobs[r].pre;
-        if (jobs[r].pre != OK && jobs[r].expect_sha) { jobs[r].pre = OK; jobs[r].nr3 = false; jobs[r].rec.codec = 0xffff; }
+        if (jobs[r].pre != OK && jobs[r].expect_sha) { jobs[r].pre = OK; jobs[r].nr3 = false; jobs[r].w4 = false; jobs[r].rec.codec = 0xffff; }
     }
     if (!run_jobs(jobs, device)) return E_ARG;
     for (uint32_t r = 0; r < h.records; ++r) {   // the first failing record, in record order

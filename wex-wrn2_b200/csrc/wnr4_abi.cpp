@@ -12,6 +12,7 @@
 #include "nr3_host.h"
 #include "wnr4.cuh"
 #include "wnr4_cuda.h"
+#include "wnr4_host.h"
 
 #define WEXB_API extern "C" __attribute__((visibility("default")))
 
@@ -70,9 +71,36 @@ Model4 *find4(uint32_t id, int device) {
     return nullptr;
 }
 
+struct DeviceGuard {
+    int saved = -1;
+    DeviceGuard() { if (cudaGetDevice(&saved) != cudaSuccess) { (void)cudaGetLastError(); saved = -1; } }
+    ~DeviceGuard() { if (saved >= 0) (void)cudaSetDevice(saved); }
+};
+
+// Device tables of a validated blob on `device` (once per model and device): 0, or 1 on a CUDA failure.
+int register4(const uint8_t *blob, size_t, uint32_t pb, uint32_t id, int device) {
+    DeviceGuard guard;
+    std::lock_guard<std::mutex> lock(g_m4_mu);
+    for (Model4 *m : g_m4) if (m->id == id && m->device == device) return 0;
+    const std::vector<uint8_t> img = model4_image(blob, pb);
+    auto *m = new Model4();
+    m->id = id; m->pb = pb; m->rows = kW4Classes * 81u * pb; m->device = device;
+    if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&m->dev, img.size()) != cudaSuccess ||
+        cudaMemcpy(m->dev, img.data(), img.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        (void)cudaGetLastError();
+        if (m->dev) cudaFree(m->dev);
+        delete m;
+        return 1;
+    }
+    m->tab = {m->dev, m->rows, pb, w4_matrix_bytes(m->rows), id};
+    g_m4.push_back(m);
+    return 0;
+}
+
+}  // namespace
+
 // Geometry of a kind-MX expert slab (wnr4_geo, wnr4/wnr4.h:108-140).
-struct Geo { uint32_t scount[3], scols[3]; };
-bool geo_of(const uint32_t *v, Geo *g) {
+bool wnr4_geo(const uint32_t *v, W4Geo *g) {
     if (!v || v[0] != 0) return false;
     uint64_t lo[6], hi[6];
     for (int m = 0; m < 3; ++m) {
@@ -88,7 +116,7 @@ bool geo_of(const uint32_t *v, Geo *g) {
 
 // One record's header and tile table (wnr4/wnr4.h:317-346), its owner and model; appends its tiles
 // (matrix by matrix) to jobs[m]. drec = the record's device copy.
-bool plan_record4(const uint8_t *rec, size_t total, const Geo &g, uint32_t owner, uint32_t model_id, const uint8_t *drec,
+bool wnr4_plan(const uint8_t *rec, size_t total, const W4Geo &g, uint32_t owner, uint32_t model_id, const uint8_t *drec,
                   uint32_t index, W4Rec *info, std::vector<W4Job> jobs[3]) {
     if (!rec || total < 64 || (total & 4095) || rd32(rec) != kWnr4) return false;
     const uint32_t mid = rd32(rec + 4), own = rd32(rec + 8), kind = rec[12], flags = rec[13], G = rd16(rec + 14);
@@ -124,6 +152,27 @@ bool plan_record4(const uint8_t *rec, size_t total, const Geo &g, uint32_t owner
     return true;
 }
 
+std::vector<W4Job> wnr4_launch_order(const std::vector<W4Job> by_m[3]) {
+    std::vector<W4Job> jobs;
+    for (int m = 0; m < 3; ++m) {   // each matrix's tiles padded to whole CTAs (a CTA holds one matrix)
+        jobs.insert(jobs.end(), by_m[m].begin(), by_m[m].end());
+        while (jobs.size() % kW4Warps) jobs.push_back({nullptr, 0, 0, 0, (uint32_t)m, 0, 0});
+    }
+    return jobs;
+}
+
+int wnr4_tables(const uint8_t *blob, size_t bytes, int device, W4Tables *tab, uint32_t *id) {
+    uint32_t pb = 0;
+    if (model4_validate(blob, bytes, &pb, id)) return -1;
+    const int st = register4(blob, bytes, pb, *id, device);
+    if (st) return st;
+    Model4 *m = find4(*id, device);
+    if (!m) return 1;
+    *tab = m->tab;
+    return 0;
+}
+
+namespace {
 // ---- tickets ------------------------------------------------------------------------------------
 struct Slot {
     DevBuf drec, djob, dinfo, derr;
@@ -169,12 +218,6 @@ struct Rings {
 };
 thread_local Rings t_rings;
 
-struct DeviceGuard {
-    int saved = -1;
-    DeviceGuard() { if (cudaGetDevice(&saved) != cudaSuccess) { (void)cudaGetLastError(); saved = -1; } }
-    ~DeviceGuard() { if (saved >= 0) (void)cudaSetDevice(saved); }
-};
-
 int finish(Slot &s, int *status) {
     const int n = (int)s.status.size();
     const bool ok = !s.broken && cudaEventSynchronize(s.done) == cudaSuccess;
@@ -202,29 +245,14 @@ WEXB_API unsigned int wnr4_cuda_abi(void) { return 5u; }
 WEXB_API int wnr4_cuda_register_model(const unsigned char *blob, size_t bytes, int device) {
     uint32_t pb = 0, id = 0;
     if (model4_validate(blob, bytes, &pb, &id)) return -1;
-    DeviceGuard guard;
-    std::lock_guard<std::mutex> lock(g_m4_mu);
-    for (Model4 *m : g_m4) if (m->id == id && m->device == device) return 0;
-    const std::vector<uint8_t> img = model4_image(blob, pb);
-    auto *m = new Model4();
-    m->id = id; m->pb = pb; m->rows = kW4Classes * 81u * pb; m->device = device;
-    if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&m->dev, img.size()) != cudaSuccess ||
-        cudaMemcpy(m->dev, img.data(), img.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
-        (void)cudaGetLastError();
-        if (m->dev) cudaFree(m->dev);
-        delete m;
-        return 1;
-    }
-    m->tab = {m->dev, m->rows, pb, w4_matrix_bytes(m->rows), id};
-    g_m4.push_back(m);
-    return 0;
+    return register4(blob, bytes, pb, id, device);
 }
 
 WEXB_API int wnr4_cuda_batch_submit(int n, const uint32_t *geo, const unsigned char *const *records, const size_t *totals,
                                     const uint32_t *owners, uint32_t model_id, int device, unsigned char *const *dst_scale,
                                     unsigned char *const *dst_weight, void *stream) {
-    Geo g;
-    if (n <= 0 || !geo || !records || !totals || !owners || !dst_scale || !dst_weight || !geo_of(geo, &g)) return WNR4_E_ARGS;
+    W4Geo g;
+    if (n <= 0 || !geo || !records || !totals || !owners || !dst_scale || !dst_weight || !wnr4_geo(geo, &g)) return WNR4_E_ARGS;
     Model4 *md = find4(model_id, device);
     if (!md) return WNR4_E_MODEL;
     DeviceGuard guard;
@@ -255,8 +283,8 @@ WEXB_API int wnr4_cuda_batch_submit(int n, const uint32_t *geo, const unsigned c
                              !((reinterpret_cast<uintptr_t>(dw[0]) | reinterpret_cast<uintptr_t>(dw[1]) |
                                 reinterpret_cast<uintptr_t>(dw[2])) & 15u);
         std::vector<W4Job> mine[3];
-        if (targets && plan_record4(records[i], totals[i], g, owners[i], model_id, s.drec.p + at[(size_t)i], (uint32_t)i,
-                                    &info[i], mine)) {
+        if (targets && wnr4_plan(records[i], totals[i], g, owners[i], model_id, s.drec.p + at[(size_t)i], (uint32_t)i,
+                                 &info[i], mine)) {
             for (int m = 0; m < 3; ++m) {
                 info[i].dst_s[m] = ds[m]; info[i].dst_w[m] = dw[m];
                 by_m[m].insert(by_m[m].end(), mine[m].begin(), mine[m].end());
@@ -265,11 +293,7 @@ WEXB_API int wnr4_cuda_batch_submit(int n, const uint32_t *geo, const unsigned c
             s.status[(size_t)i] = 0;
         }
     }
-    std::vector<W4Job> jobs;
-    for (int m = 0; m < 3; ++m) {   // each matrix's tiles padded to whole CTAs (a CTA holds one matrix)
-        jobs.insert(jobs.end(), by_m[m].begin(), by_m[m].end());
-        while (jobs.size() % kW4Warps) jobs.push_back({nullptr, 0, 0, 0, (uint32_t)m, 0, 0});
-    }
+    const std::vector<W4Job> jobs = wnr4_launch_order(by_m);
     if (!s.djob.grow(sizeof(W4Job) * (jobs.size() + 1)) || !s.hjob.grow(sizeof(W4Job) * (jobs.size() + 1))) return WNR4_E_CUDA;
     if (!jobs.empty()) std::memcpy(s.hjob.p, jobs.data(), sizeof(W4Job) * jobs.size());
     cudaError_t e = cudaSuccess;

@@ -30,6 +30,11 @@ def tools():
         L.wexb_count_expert.argtypes = [P, P, I, P, P]
         L.wexb_build_model.argtypes = [P, P, P]; L.wexb_build_model.restype = U32
         L.wexb_encode_record.argtypes = [P, P, P, I, U32, U32, U32, U32, P, SZ, P, P]
+        L.wexb_w4_model_bytes.argtypes = [U32]; L.wexb_w4_model_bytes.restype = SZ
+        L.wexb_w4_counts_words.argtypes = [U32]; L.wexb_w4_counts_words.restype = SZ
+        L.wexb_w4_count.argtypes = [P, P, U32, P]
+        L.wexb_w4_build.argtypes = [U32, P, P]; L.wexb_w4_build.restype = U32
+        L.wexb_w4_encode.argtypes = [P, SZ, P, P, U32, U32, U32, P, SZ]; L.wexb_w4_encode.restype = ctypes.c_longlong
         assert L.wexb_tools_abi() == 1
         _tools = L
     return _tools
@@ -185,3 +190,37 @@ def make_experts(hidden, ffn, owners, seed=1, sigma=0.02, cz=False, mode=0, neg_
             blob = train_model([(e.entry, e.coded) for e in experts[::train_every]], nr3)
         list(pool.map(lambda e: e.encode(blob, wchunk, schunk, nr3), experts))
     return blob, experts
+
+
+# ---- WNR4 kind MX (draft codec 8) ------------------------------------------------------------------
+def train_model4(pairs, pb=1):
+    """WNM4 kind-MX blob trained on (entry, coded slab) pairs."""
+    L = tools()
+    counts = np.zeros(L.wexb_w4_counts_words(pb), np.uint64)
+    for entry, coded in pairs:
+        assert L.wexb_w4_count(entry, coded, pb, counts.ctypes.data) == 0
+    blob = ctypes.create_string_buffer(L.wexb_w4_model_bytes(pb))
+    assert L.wexb_w4_build(pb, counts.ctypes.data, blob) != 0
+    return blob.raw
+
+
+def encode4(blob4, entry, coded, flags, owner, G=32):
+    """WNR4 record of a coded expert (zero-padded to 4096), or None when not smaller than raw."""
+    cap = 2 * len(coded) + (1 << 20)
+    out = ctypes.create_string_buffer(cap)
+    n = tools().wexb_w4_encode(blob4, len(blob4), entry, coded, flags, owner, G, out, cap)
+    if n < 0:
+        raise ValueError('WNR4 encode failed')
+    return out.raw[:n] if n else None
+
+
+def geo4(entry):
+    """The 13 geometry words of an expert slab for the WNR4 ABI: kind 0, cells, cols, offsets."""
+    g = [0] * 13
+    for m in range(3):
+        r, c = struct.unpack_from('<HH', entry, 20 + 4 * m)
+        g[1 + m], g[4 + m] = r * c, c
+        g[7 + m] = struct.unpack_from('<I', entry, 44 + 4 * m)[0]
+        g[10 + m] = struct.unpack_from('<I', entry, 56 + 4 * m)[0]
+    return g
+
