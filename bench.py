@@ -25,6 +25,7 @@ compiled from its sources into oracle/_ref) on all host cores, one record per co
 sample of the same records.
 """
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -42,7 +43,15 @@ sys.path.insert(0, os.path.join(ROOT, 'wex-wrn2_b200'))
 CONFIGS = {
     'tiny': dict(hidden=1024, ffn=512, layers=1, experts=8, batch=8, cz=False, sigma=(0.02, 0.02), neg_zero=0.0),
     'mid': dict(hidden=2048, ffn=768, layers=48, experts=128, batch=8, cz=False, sigma=(0.01, 0.04), neg_zero=0.0),
-    'large': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03),
+    'large': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
+                  lean=True),
+    # containers: a WEX4 file per rank, checked and decoded by wex4_check (per-record SHA-256 against
+    # the index, codec dispatch, decode); tiny = the 8 experts plus one RAW expert, mixed = one routed
+    # step of large experts, 10 % uniform-random (stored RAW), 30 % WNR4 kind MX, the rest WNR3 CZ
+    'tiny-file': dict(hidden=1024, ffn=512, layers=1, experts=9, batch=9, cz=False, sigma=(0.02, 0.02), neg_zero=0.0,
+                      container=True, raw=(8,), wnr4_frac=0.0),
+    'mixed': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
+                  container=True, raw_frac=0.10, wnr4_frac=0.30),
 }
 SEED = 20261201
 MEASURED_PEAKS = os.path.join(ROOT, 'MEASURED_PEAKS.json')
@@ -81,7 +90,7 @@ def build_pool(cfg, owners, threads):
     blob, _ = synth.make_experts(cfg['hidden'], cfg['ffn'], train, seed=SEED, sigma=lambda l: sig[l], cz=cfg['cz'],
                                  neg_zero=cfg['neg_zero'], train_every=1, threads=threads)
     _, experts = synth.make_experts(cfg['hidden'], cfg['ffn'], owners, seed=SEED, sigma=lambda l: sig[l], cz=cfg['cz'],
-                                    neg_zero=cfg['neg_zero'], threads=threads, blob=blob)
+                                    neg_zero=cfg['neg_zero'], threads=threads, blob=blob, lean=cfg.get('lean', False))
     return blob, experts
 
 
@@ -211,14 +220,14 @@ def reference_decode_rate(experts, blob, cores, min_seconds=10.0, max_records=No
     if L is None:
         raise RuntimeError('oracle/_ref/wex_nr3_tools.so is missing: build it with `make -C oracle ref`')
     sample = [e for e in experts if e.codec == 5][: (max_records or len(experts))]
-    outs = [ctypes.create_string_buffer(len(e.source)) for e in sample]
+    outs = [ctypes.create_string_buffer(e.raw) for e in sample[:cores]]
 
     def one(i):
         e = sample[i % len(sample)]
-        st = L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, outs[i % len(sample)])
+        st = L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, outs[i % cores])
         if st != 0:
             raise RuntimeError('reference decoder refused a record')
-        return len(e.source)
+        return e.raw
     with ThreadPoolExecutor(cores) as pool:
         t0 = time.perf_counter()
         done, nbytes, n = 0, 0, 0
@@ -260,10 +269,10 @@ def run_reference(args, cfg):
         return 0
 
     def one(e):
-        out = ctypes.create_string_buffer(len(e.source))
+        out = ctypes.create_string_buffer(e.raw)
         if L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, out) != 0:
             raise RuntimeError('reference decoder refused a record')
-        return len(e.source)
+        return e.raw
     times, nbytes, nrec = [], 0, 0
     with ThreadPoolExecutor(cores) as pool:
         for s in range(args.warmup + args.steps):
@@ -289,6 +298,165 @@ def run_reference(args, cfg):
     }
     print(json.dumps(line))
     return 0
+
+
+# ---- WEX4 containers (tiny-file, mixed) --------------------------------------------------------------
+def container_owners(cfg, rank, world, layers):
+    """The experts of this rank's container: tiny-file all of them, mixed one routed step of its shard."""
+    if cfg['experts'] <= 16:
+        return [(0, i) for i in range(cfg['experts'])]
+    trace = routing_trace(cfg, 1, rank, world, layers)
+    return sorted({(l, int(e)) for l in range(layers) for e in trace[0][l]})
+
+
+def codec_plan(cfg, owners):
+    """Per owner: 0 RAW (uniform-random nibbles), 8 WNR4, 5 WNR3, by a seeded draw."""
+    if 'raw' in cfg:
+        return [0 if i in cfg['raw'] else 5 for i in range(len(owners))]
+    rng = np.random.default_rng([SEED, 77])
+    u = rng.random(len(owners))
+    return [0 if x < cfg['raw_frac'] else 8 if x < cfg['raw_frac'] + cfg['wnr4_frac'] else 5 for x in u]
+
+
+def build_container(cfg, owners, threads, verify_n=12):
+    """(file bytes, decoded bytes, codec counts, verification file, its expected digest). The
+    verification file holds the first verify_n records (every codec) with their expected digest."""
+    import synth
+    import wex4file
+    sig = layer_sigmas(cfg)
+    plan = codec_plan(cfg, owners)
+    seed = lambda l, i: SEED * 1000003 + l * 4099 + i
+    mk = lambda k: synth.Expert(cfg['hidden'], cfg['ffn'], owners[k][0], owners[k][1], seed(*owners[k]), sig[owners[k][0]],
+                                cfg['cz'], 1 if plan[k] == 0 else 0, cfg['neg_zero'])
+    layers = sorted({l for l, _ in owners})
+    train = [synth.Expert(cfg['hidden'], cfg['ffn'], l, 100000 + l, seed(l, 100000), sig[l], cfg['cz'], 0, cfg['neg_zero'])
+             for l in layers[:8]]
+    blob = synth.train_model([(e.entry, e.coded) for e in train])
+    blob4 = synth.train_model4([(e.entry, e.coded) for e in train[:4]]) if 8 in plan else None
+    del train
+
+    def make(k):
+        e = mk(k)
+        if plan[k] == 8:
+            rec = synth.encode4(blob4, e.entry, e.coded, e.flags, k, 32)   # owner = the record's index
+            r = wex4file.expert_record(e, 1, codec=wex4file.CODEC_WNR4, stored=rec) if rec else None
+        else:
+            r = None
+        if r is None:
+            e.encode(blob)
+            r = wex4file.expert_record(e, 0, value_exact=cfg['cz'])
+        keep = e.expected if k < verify_n else None
+        return r, len(e.source), keep
+    with ThreadPoolExecutor(threads) as pool:
+        made = list(pool.map(make, range(len(owners))))
+    recs = [m[0] for m in made]
+    blobs = [(wex4file.BLOB_WNM2, fnv1a(blob), blob)] + ([(wex4file.BLOB_WNM4, fnv1a(blob4), blob4)] if blob4 else [])
+    grid = (cfg['layers'], cfg['experts'])
+    data = wex4file.write(recs, blobs, grid=grid, value_exact=cfg['cz'])
+    counts = {c: sum(1 for r in recs if r.codec == c) for c in (0, 5, 8)}
+    vrecs = recs[:verify_n]   # a prefix keeps every WNR4 record at its own index (its owner)
+    vdata = wex4file.write(vrecs, blobs, grid=grid, value_exact=cfg['cz'])
+    vdigest = wex4file.content_digest(vrecs, [m[2] for m in made[:verify_n]])
+    return data, sum(m[1] for m in made), counts, vdata, vdigest
+
+
+def fnv1a(b):
+    h = 2166136261
+    for x in b:
+        h = ((h ^ x) * 16777619) & 0xffffffff
+    return h or 1
+
+
+def run_container(args, cfg):
+    import ctypes
+    import torch
+    import wexcuda
+    world, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    layers = args.layers or cfg['layers']
+    threads = max(1, (os.cpu_count() or 8) // max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world))))
+    owners = container_owners(cfg, rank, world, layers)
+    t0 = time.time()
+    data, decoded, counts, vdata, vdigest = build_container(cfg, owners, threads)
+    log(f'[rank {rank}] container of {len(owners)} records ({len(data) / 1e9:.2f} GB, codecs {counts}) built in '
+        f'{time.time() - t0:.1f} s')
+    L = wexcuda.lib()
+    L.wex4_check.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p]
+    buf = np.frombuffer(data, np.uint8).copy()
+    del data
+    assert wexcuda.host_register(buf) == 0
+    vbuf = np.frombuffer(vdata, np.uint8).copy()
+    digest = ctypes.create_string_buffer(32)
+    # verification (untimed): the digest of the first records equals the one of their source slabs
+    assert L.wex4_check(vbuf.ctypes.data, len(vbuf), 1 | 2 | 4, digest) == 0, 'verification file refused'
+    assert digest.raw == vdigest, 'content digest differs'
+    flags = 1 | 2 | 4 | (8 if len(owners) > 16 else 0)   # hashes, decode, codec 8 (digest only on small files)
+    h2d_gbs = measure_h2d(torch)
+    for _ in range(args.warmup):
+        assert L.wex4_check(buf.ctypes.data, len(buf), flags, digest) == 0
+    clocks = Clocks(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        assert L.wex4_check(buf.ctypes.data, len(buf), flags, digest) == 0
+    torch.cuda.synchronize()
+    dt = max_over_ranks(time.perf_counter() - t0, world)
+    barrier(world)
+    clk = clocks.stop()
+    dec_all, stored_all, recs_all = sum_over_ranks([decoded * args.steps, len(buf) * args.steps, len(owners) * args.steps],
+                                                   world)
+    value = dec_all / dt / 1e9
+    line = {
+        'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 3), 'unit': 'GB/s', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(1e3 * dt / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'experts_per_s': round(recs_all / dt, 1),
+        'config': {'workload': f'{args.config}: WEX4 container per rank, {len(owners)} expert records (hidden '
+                               f'{cfg["hidden"]}, FFN {cfg["ffn"]}), codecs {counts}, checked by wex4_check: '
+                               f'record SHA-256 against the index, codec dispatch, decode into HBM' +
+                               ('' if flags & 8 else ', content digest'),
+                   'placement': 'expert id mod world size', 'l2': 'inputs larger than L2 (126 MB) between steps'},
+        'e2e': {'value': round(value, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': int(len(buf)), 'd2h_bytes_per_step': 32,
+                'api': f'wex4_check(file, flags {flags}) from pinned host memory: the whole path',
+                'roofline': {'bound': 'h2d', 'achieved': round(len(buf) * args.steps / dt / 1e9, 2), 'peak': round(h2d_gbs, 2),
+                             'frac': round(len(buf) * args.steps / dt / 1e9 / h2d_gbs, 4)}},
+        'clocks': clk,
+        'verified': {'digest_records': min(12, len(owners)), 'statuses': 'all 0'},
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def measure_h2d(torch, mib=256, reps=5):
+    """Pinned host-to-device copy bandwidth of this GPU (GB/s), best of reps, CUDA events."""
+    src = torch.empty(mib << 20, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(mib << 20, dtype=torch.uint8, device='cuda')
+    best = 0.0
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        best = max(best, (mib << 20) / (a.elapsed_time(b) / 1e3) / 1e9)
+    return best
+
+
+def profile_traffic_per_record(config):
+    """DRAM bytes per record of the weight kernel from its committed ncu summary, if there is one."""
+    path = os.path.join(ROOT, 'profiles', f'nr3_weights_{config}.md')
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith('traffic_bytes_per_record:'):
+            return int(line.split(':')[1])
+    return None
 
 
 def config_desc(args, cfg):
@@ -318,7 +486,7 @@ def run_gpu(args, cfg):
     index = {(e.layer, e.index): i for i, e in enumerate(experts)}
     assert wexcuda.register_model(blob) == 0
     hostbuf, views = pinned_records(experts)
-    raw = len(experts[0].source)
+    raw = experts[0].raw
     k = layers * cfg['batch']
     # destinations of one step: 384 experts' six regions
     sizes = [r * c // 32 for r, c in [(cfg['ffn'], cfg['hidden']), (cfg['hidden'], cfg['ffn']), (cfg['ffn'], cfg['hidden'])]]
@@ -334,6 +502,7 @@ def run_gpu(args, cfg):
     res = wexcuda.Resident([e.entry for e in experts], views, dev)
     assert res.failures == 0
     res.profile(True)
+    h2d_gbs = measure_h2d(torch)
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     kernel_ms, launches = [], 0
@@ -361,10 +530,10 @@ def run_gpu(args, cfg):
     last = step_idx[steps_total - 1]
     check = list(range(0, k, max(1, k // 8)))[:8]
     got = dst[check].cpu().numpy()
-    verified = sum(int(got[i].tobytes() == experts[last[j]].expected) for i, j in enumerate(check))
+    verified = sum(int(hashlib.sha256(got[i].tobytes()).digest() == experts[last[j]].expected_sha)
+                   for i, j in enumerate(check))
     assert verified == len(check), 'decoded bytes differ from the source'
     # per-record outcome table of the last step (status, digest of the checked slabs), all ranks
-    import hashlib
     slab_digest = {j: hashlib.sha256(got[n].tobytes()).hexdigest()[:16] for n, j in enumerate(check)}
     table = gather_outcomes([(rank, experts[i].layer, experts[i].index, int(st[j]), slab_digest.get(j, ''))
                              for j, i in enumerate(last)], world)
@@ -443,10 +612,10 @@ def run_gpu(args, cfg):
     sync_s = timed(run_sync)
     clk = clocks.stop()
     got = dst[check].cpu().numpy()
-    assert all(got[i].tobytes() == experts[last[j]].expected for i, j in enumerate(check))
+    assert all(hashlib.sha256(got[i].tobytes()).digest() == experts[last[j]].expected_sha for i, j in enumerate(check))
 
     # ---- bytes ----------------------------------------------------------------------------------
-    dec_bytes = sum(len(experts[i].source) for s in range(args.warmup, steps_total) for i in step_idx[s])
+    dec_bytes = sum(experts[i].raw for s in range(args.warmup, steps_total) for i in step_idx[s])
     stored = sum(len(experts[i].record) for s in range(args.warmup, steps_total) for i in step_idx[s])
     wpay = sum(int.from_bytes(experts[i].record[12:16], 'little') for s in range(args.warmup, steps_total)
                for i in step_idx[s])
@@ -465,7 +634,13 @@ def run_gpu(args, cfg):
     peaks = json.load(open(MEASURED_PEAKS)) if os.path.exists(MEASURED_PEAKS) else {}
     hbm_peak = peaks.get('hbm_gbs', 6650.0)
     achieved = alg / (wk_ms / 1e3) / 1e9 if wk_ms else None
+    traffic_rec = profile_traffic_per_record(args.config)
     h2d_per_step = stored // args.steps + 0
+    # rooflines of the two paths (per GPU): the resident decode against HBM (records read, slabs written
+    # by the decoder and again by the commit copy), the end-to-end path against the measured H2D link
+    hbm_bytes = (stored + dec_bytes + 2 * dec_bytes) / args.steps
+    step_s = value_ms / 1e3 / args.steps
+    e2e_step_s = e2e_s / args.steps
     line = {
         'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 3), 'unit': 'GB/s', 'n_gpus': world,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(value_ms / args.steps, 3),
@@ -476,13 +651,24 @@ def run_gpu(args, cfg):
                 'h2d_bytes_per_step': int(h2d_per_step), 'd2h_bytes_per_step': 4 * k,
                 'api': f'wexb_batch_submit/wexb_batch_wait, {B} records per call, {layers} calls per step, '
                        f'{args.depth} calls in flight',
-                'ms_per_step': round(1e3 * e2e_s / args.steps, 3), 'gpu_launches': 3 * k * args.steps,
+                'ms_per_step': round(1e3 * e2e_s / args.steps, 3), 'gpu_launches': 3 * layers * args.steps,
                 'sync': {'value': round(e2e_sync, 3), 'unit': 'GB/s',
                          'api': 'wex_cuda_decode_batch_to_device (drop-in, synchronous)',
-                         'ms_per_step': round(1e3 * sync_s / args.steps, 3)}},
+                         'ms_per_step': round(1e3 * sync_s / args.steps, 3)},
+                'roofline': {'bound': 'h2d', 'achieved': round(h2d_per_step / e2e_step_s / 1e9, 2),
+                             'peak': round(h2d_gbs, 2), 'unit': 'GB/s (stored bytes per GPU)',
+                             'frac': round(h2d_per_step / e2e_step_s / 1e9 / h2d_gbs, 4),
+                             'peak_source': 'measured here: one pinned 256 MiB host-to-device copy, best of 5',
+                             'hbm_frac': round(hbm_bytes / e2e_step_s / 1e9 / hbm_peak, 4)}},
+        'value_roofline': {'bound': 'hbm', 'achieved': round(hbm_bytes / step_s / 1e9, 2), 'peak': hbm_peak, 'unit': 'GB/s',
+                           'frac': round(hbm_bytes / step_s / 1e9 / hbm_peak, 4),
+                           'bytes': 'records read + slabs written by the decoder and by the commit copy'},
         'roofline': {'bound': 'hbm', 'kernel': 'nr3_weights', 'achieved': round(achieved, 2) if achieved else None,
                      'peak': hbm_peak, 'unit': 'GB/s', 'frac': round(achieved / hbm_peak, 5) if achieved else None,
-                     'peak_source': 'measured' if peaks else 'fallback', 'traffic': None,
+                     'peak_source': 'measured' if peaks else 'fallback',
+                     'traffic': int(traffic_rec * k) if traffic_rec else None,
+                     'traffic_source': 'ncu dram__bytes_read.sum + dram__bytes_write.sum per record of a 64-record '
+                                       'launch, scaled to this launch' if traffic_rec else None,
                      'kernel_ms': round(wk_ms, 4) if wk_ms else None,
                      'alg_bytes_per_launch': int(alg),
                      'step_kernel_ms': [round(statistics.mean(m[i] for m in kernel_ms if m), 4) for i in range(3)]},
@@ -525,6 +711,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == 'reference':
         return run_reference(args, cfg)
+    if cfg.get('container'):
+        return run_container(args, cfg)
     return run_gpu(args, cfg)
 
 

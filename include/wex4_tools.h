@@ -19,6 +19,7 @@ extern "C" {
 #define WEX4_CHECK_HASHES 1     /* verify every blob and record SHA-256 */
 #define WEX4_CHECK_DECODE 2     /* decode every record and write the content digest */
 #define WEX4_CHECK_CODEC8 4     /* addition: also decode draft codec-8 (WNR4 kind MX) records */
+#define WEX4_CHECK_NO_DIGEST 8  /* addition: with WEX4_CHECK_DECODE, decode and verify but skip the digest */
 
 /* 1 (wex4/wex4_tools.c:25) */
 uint32_t wex4_tools_abi(void);
@@ -39,8 +40,8 @@ int wex4_decode_record_buf(const unsigned char *page, uint64_t file_bytes, const
 /* The legacy layers x experts table of 72-byte entries rebuilt from the index (wex4/wex4_tools.c:215-231). */
 int wex4_expert_table(const unsigned char *page, uint64_t file_bytes, const unsigned char *index, size_t index_len,
                       unsigned char *out);
-/* WBP1 (codec 6, non-expert tensors) is not built in this library: both return -1
- * (wex4/wex4_tools.c:27-35). */
+/* WBP1 (codec 6, non-expert tensors; wex4/wex4_tools.c:27-35): the canonical encoder (host) and the
+ * GPU decoder of one record into host memory (out is scratch until it returns 0); 0 or -1. */
 int wex4_bp_encode_record(const unsigned char *data, uint32_t decoded, uint32_t planes, uint32_t chunk_log2,
                           uint32_t transform, uint32_t owner, unsigned char *out, size_t capacity, size_t *written);
 int wex4_bp_decode_record(const unsigned char *record, size_t total, uint32_t decoded, uint32_t owner,

@@ -16,14 +16,6 @@ import wexcuda
 
 REF_VECTORS = '/root/reference/wex4/vectors'
 P, U32, U64, SZ, I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_int
-# WBP1 (codec 6) is not built in this library: files whose verdict depends on decoding a WBP1 record
-# differ from the reference (they are refused with WEX4_E_UNSUPPORTED instead of decoded / -14)
-WBP1_FILES = {'generic.wex4', 'generic-index-last.wex4', 'minor-version-9.wex4', 'unknown-optional-feature-bits.wex4',
-              'bytes-in-the-reserved-header-area.wex4', 'wbp1-record-sizes-not-a-multiple-of-the-planes.wex4',
-              'wbp1-records-of-4-and-8-planes.wex4', 'wbp1-record-header-damaged-record-hash-fixed.wex4',
-              'wbp1-record-stream-damaged-record-hash-fixed.wex4', 'wbp1-record-with-a-zero-page-too-many.wex4'}
-
-
 def lib():
     L = wexcuda.lib()
     L.wex4_tools_abi.restype = U32
@@ -118,8 +110,8 @@ def test_expert_table_matches_reference(golden_dir):
 @pytest.mark.gpu
 @pytest.mark.parametrize('flags', [1, 2, 3])
 def test_check_with_hashes_and_decode(golden_dir, flags):
-    """Verdict, class and content digest of wex4_check equal the reference's on the vectors (the ones
-    whose verdict depends on a WBP1 decode excepted)."""
+    """Verdict, class and content digest of wex4_check equal the reference's on every vector, the WBP1
+    (codec 6) ones included."""
     import torch
     assert torch.cuda.is_available()
     L = lib()
@@ -129,8 +121,6 @@ def test_check_with_hashes_and_decode(golden_dir, flags):
         data = open(os.path.join(golden_dir, 'vectors', name), 'rb').read()
         digest = ctypes.create_string_buffer(32)
         st = L.wex4_check(data, len(data), flags, digest)
-        if name in WBP1_FILES:
-            continue
         ref = oracle.ref_lib('wex4_tools_ref')
         want = ref.wex4_check(data, len(data), flags, None) if ref is not None else (item['ref_check'] if flags == 3 else None)
         if want is not None:

@@ -71,14 +71,20 @@ struct Sha {
     __device__ void update(const uint8_t *p, uint64_t n) {
         len += n;
         while (n && fill) { byte(*p++); --n; }
-        if (!(reinterpret_cast<uintptr_t>(p) & 15)) {   // whole aligned blocks: four 16-byte loads each
-            for (; n >= 64; n -= 64, p += 64) {
-                const uint4 *q = reinterpret_cast<const uint4 *>(p);
+        if (!(reinterpret_cast<uintptr_t>(p) & 15) && n >= 64) {   // whole aligned blocks: four 16-byte loads each,
+            const uint4 *q = reinterpret_cast<const uint4 *>(p);        // the next block's loads issued before
+            uint4 v[4];                                                  // this block's compression
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = __ldg(q + k);
+            for (; n >= 64; n -= 64, p += 64, q += 4) {
                 uint32_t w[16];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    const uint4 v = q[k];
-                    w[4 * k] = bswap(v.x); w[4 * k + 1] = bswap(v.y); w[4 * k + 2] = bswap(v.z); w[4 * k + 3] = bswap(v.w);
+                    w[4 * k] = bswap(v[k].x); w[4 * k + 1] = bswap(v[k].y); w[4 * k + 2] = bswap(v[k].z); w[4 * k + 3] = bswap(v[k].w);
+                }
+                if (n >= 128) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) v[k] = __ldg(q + 4 + k);
                 }
                 compress(st, w);
             }

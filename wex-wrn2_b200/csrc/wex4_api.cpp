@@ -16,6 +16,7 @@
 #include "nr3_host.h"
 #include "sha256.cuh"
 #include "wex4_tools.h"
+#include "wbp1_host.h"
 #include "wnr4_host.h"
 
 #define WEXB_API extern "C" __attribute__((visibility("default")))
@@ -354,6 +355,8 @@ struct Job {
     W4Tables w4tab{};
     uint64_t soff[3] = {}, woff[3] = {};   // its six tensors in the decoded record
     bool host_refused = false;             // its header or tile table failed the host checks
+    bool bp = false;                       // a WBP1 (codec 6) record
+    Wbp1Plan bpp{};
     uint8_t *out_dev = nullptr;            // decoded bytes on the device (after the run)
     int status = OK;
 };
@@ -410,6 +413,15 @@ int prepare_wnr4(const View &v, Job &j, const uint8_t *file, int device) {
     return OK;
 }
 
+// Host verdict of a WBP1 record before its decode (c/wex4.h:487-525, :684-685): the record header,
+// planes, CDFs, stream tables and padding.
+int prepare_wbp1(Job &j, int device) {
+    if (wbp1_parse(j.stored, j.rec.stored, j.rec.decoded, j.rec.owner, &j.bpp)) return E_DATA;
+    if (!wbp1_prepare(device)) return E_ARG;
+    j.bp = true;
+    return OK;
+}
+
 // Runs every job with pre == OK: upload, SHA-256 checks, RAW padding checks, WNR3 decodes into device
 // memory. Sets job.status (E_HASH before E_DATA, as the reference orders them) and job.out_dev.
 // Returns false on a CUDA failure. The caller holds g_space.mu.
@@ -424,7 +436,9 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     std::vector<size_t> at(jobs.size()), scr(jobs.size()), offs(jobs.size());
     size_t stage_bytes = 0, out_bytes = 0, scr_bytes = 0, noffs = 0;
     std::vector<Nr3Task> stasks, wtasks;
-    std::vector<size_t> nr3_of, w4_of;   // job index of each WNR3 / WNR4 descriptor
+    std::vector<size_t> nr3_of, w4_of, bp_of;   // job index of each WNR3 / WNR4 / WBP1 descriptor
+    std::vector<size_t> bp_scr(jobs.size()), bp_offs(jobs.size());
+    std::vector<Wbp1Task> bptasks;
     for (size_t i = 0; i < jobs.size(); ++i) {
         Job &j = jobs[i];
         if (j.pre != OK) continue;
@@ -437,7 +451,16 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
             out_bytes += align_up(j.rec.decoded, 256);
         }
         if (j.w4) { w4_of.push_back(i); out_bytes += align_up(j.rec.decoded, 256); }
+        if (j.bp) {
+            uint64_t plane_at[8];
+            bp_scr[i] = scr_bytes; scr_bytes += align_up(wbp1_scratch(j.bpp, plane_at), 256);
+            bp_offs[i] = noffs; noffs += j.bpp.total_streams + 1;
+            wbp1_tasks(j.bpp, (uint32_t)bp_of.size(), bptasks);
+            bp_of.push_back(i);
+            out_bytes += align_up(j.rec.decoded, 256);
+        }
     }
+    const size_t kb = bp_of.size();
     const size_t n = jobs.size(), k = nr3_of.size(), k4 = w4_of.size();
     // codec-8 tiles, planned from the host bytes against the staged copies, grouped by model
     std::vector<W4Rec> w4info(k4);
@@ -473,7 +496,8 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
                  o_wt = take(wtasks.size() * sizeof(Nr3Task)), o_jobs = take(k * sizeof(CommitJob)),
                  o_sha = take(n * sizeof(ShaMsg)), o_exp = take(n * 32), o_zero = take(n * sizeof(ZeroJob)),
                  o_err = take(n * 4), o_ver = take(n * 4), o_offs = take(noffs * 4),
-                 o_w4rec = take(k4 * sizeof(W4Rec)), o_w4job = take(w4jobs.size() * sizeof(W4Job));
+                 o_w4rec = take(k4 * sizeof(W4Rec)), o_w4job = take(w4jobs.size() * sizeof(W4Job)),
+                 o_bprec = take(kb * sizeof(Wbp1Record)), o_bptask = take(bptasks.size() * sizeof(Wbp1Task));
     if (!S.stage.grow(stage_bytes) || !S.out.grow(out_bytes) || !S.scratch.grow(scr_bytes) || !S.meta.grow(m) ||
         !S.hmeta.grow(m)) return false;
     uint8_t *hm = S.hmeta.p, *dm = S.meta.p;
@@ -522,6 +546,16 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
         for (int mm = 0; mm < 3; ++mm) { w4info[q].dst_s[mm] = j.out_dev + j.soff[mm]; w4info[q].dst_w[mm] = j.out_dev + j.woff[mm]; }
         w4info[q].error = derr + w4_of[q];
     }
+    for (size_t q = 0; q < kb; ++q) {
+        Job &j = jobs[bp_of[q]];
+        const size_t i = bp_of[q];
+        j.out_dev = S.out.p + out_at; out_at += align_up(j.rec.decoded, 256);
+        wbp1_offsets(j.bpp, j.stored, reinterpret_cast<uint32_t *>(hm + o_offs) + bp_offs[i]);
+        reinterpret_cast<Wbp1Record *>(hm + o_bprec)[q] =
+            wbp1_descriptor(j.bpp, S.stage.p + at[i], reinterpret_cast<const uint32_t *>(dm + o_offs) + bp_offs[i],
+                            S.scratch.p + bp_scr[i], j.out_dev, derr + i);
+    }
+    if (!bptasks.empty()) std::memcpy(hm + o_bptask, bptasks.data(), bptasks.size() * sizeof(Wbp1Task));
     if (k4) std::memcpy(hm + o_w4rec, w4info.data(), k4 * sizeof(W4Rec));
     if (!w4jobs.empty()) std::memcpy(hm + o_w4job, w4jobs.data(), w4jobs.size() * sizeof(W4Job));
     std::memcpy(hm + o_st, stasks.data(), stasks.size() * sizeof(Nr3Task));
@@ -539,6 +573,9 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     ok = ok && launch_nr3_scales(drecs, reinterpret_cast<const Nr3Task *>(dm + o_st), (uint32_t)stasks.size(), st) == cudaSuccess &&
          launch_nr3_weights(drecs, reinterpret_cast<const Nr3Task *>(dm + o_wt), (uint32_t)wtasks.size(), weight_threads(), st) == cudaSuccess &&
          launch_commit(reinterpret_cast<const CommitJob *>(dm + o_jobs), (uint32_t)k, st) == cudaSuccess;
+    ok = ok && launch_wbp1_streams(reinterpret_cast<const Wbp1Record *>(dm + o_bprec),
+                                   reinterpret_cast<const Wbp1Task *>(dm + o_bptask), (uint32_t)bptasks.size(), st) == cudaSuccess &&
+         launch_wbp1_join(reinterpret_cast<const Wbp1Record *>(dm + o_bprec), (uint32_t)kb, st) == cudaSuccess;
     for (size_t g = 0; ok && g < w4runs.size(); ++g)
         ok = launch_wnr4(*w4tabs[g], reinterpret_cast<const W4Job *>(dm + o_w4job) + w4runs[g].first,
                          (uint32_t)w4runs[g].second, reinterpret_cast<const W4Rec *>(dm + o_w4rec), st) == cudaSuccess;
@@ -620,10 +657,11 @@ WEXB_API int wex4_decode_record_buf(const unsigned char *page, uint64_t file_byt
     j.expect_sha = check_sha ? rec.sha : nullptr;
     // WBP1 (codec 6) is not built here; codec 8 and unknown codecs are unsupported, as in the reference
     if (rec.codec == kCodecWnr3) j.pre = prepare_wnr3(v, j, model_id, device);
+    else if (rec.codec == kCodecWbp1) j.pre = prepare_wbp1(j, device);
     else if (rec.codec != kCodecRaw) j.pre = E_UNSUPPORTED;
     const int pre = j.pre;
     if (pre != OK && !j.expect_sha) return pre;
-    if (pre != OK) { j.pre = OK; j.nr3 = false; j.w4 = false; j.rec.codec = 0xffff; }   // its hash is still checked first
+    if (pre != OK) { j.pre = OK; j.nr3 = false; j.w4 = false; j.bp = false; j.rec.codec = 0xffff; }   // its hash is still checked first
     std::lock_guard<std::mutex> lock(g_space.mu);
     if (!run_jobs(jobs, device)) return E_ARG;
     if (j.status == E_HASH) return E_HASH;
@@ -670,6 +708,7 @@ WEXB_API int wex4_check(const unsigned char *file, uint64_t len, int flags, unsi
         }
         if (j.rec.codec == kCodecWnr3) j.pre = prepare_wnr3(v, j, j.rec.blob ? model_ids[j.rec.blob - 1] : 0, device);
         else if (j.rec.codec == kCodecWnr4 && (flags & WEX4_CHECK_CODEC8)) j.pre = prepare_wnr4(v, j, file, device);
+        else if (j.rec.codec == kCodecWbp1) j.pre = prepare_wbp1(j, device);
         else if (j.rec.codec != kCodecRaw) j.pre = E_UNSUPPORTED;
     }
     std::lock_guard<std::mutex> lock(g_space.mu);
@@ -677,7 +716,9 @@ WEXB_API int wex4_check(const unsigned char *file, uint64_t len, int flags, unsi
     std::vector<int> pre(h.records);
     for (uint32_t r = 0; r < h.records; ++r) {
         pre[r] = jobs[r].pre;
-        if (jobs[r].pre != OK && jobs[r].expect_sha) { jobs[r].pre = OK; jobs[r].nr3 = false; jobs[r].w4 = false; jobs[r].rec.codec = 0xffff; }
+        if (jobs[r].pre != OK && jobs[r].expect_sha) {
+            jobs[r].pre = OK; jobs[r].nr3 = false; jobs[r].w4 = false; jobs[r].bp = false; jobs[r].rec.codec = 0xffff;
+        }
     }
     if (!run_jobs(jobs, device)) return E_ARG;
     for (uint32_t r = 0; r < h.records; ++r) {   // the first failing record, in record order
@@ -686,7 +727,7 @@ WEXB_API int wex4_check(const unsigned char *file, uint64_t len, int flags, unsi
         if (pre[r] != OK) return pre[r];
         if (j.status != OK) return j.status;
     }
-    if (!(flags & WEX4_CHECK_DECODE)) return OK;
+    if (!(flags & WEX4_CHECK_DECODE) || (flags & WEX4_CHECK_NO_DIGEST)) return OK;
     // the content digest: per tensor in table order {u16 name_len, name, u8 dtype, u8 rank, u64 shape[8],
     // u64 nbytes, bytes} (wex4/wex4_tools.c:125-158), hashed on the GPU by one thread over the segments
     std::vector<uint8_t> metas;
@@ -730,9 +771,26 @@ WEXB_API int wex4_check(const unsigned char *file, uint64_t len, int flags, unsi
     return OK;
 }
 
-WEXB_API int wex4_bp_encode_record(const unsigned char *, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
-                                   unsigned char *, size_t, size_t *) { return -1; }
-WEXB_API int wex4_bp_decode_record(const unsigned char *, size_t, uint32_t, uint32_t, unsigned char *) { return -1; }
+WEXB_API int wex4_bp_encode_record(const unsigned char *data, uint32_t decoded, uint32_t planes, uint32_t chunk_log2,
+                                   uint32_t transform, uint32_t owner, unsigned char *out, size_t capacity, size_t *written) {
+    return wbp1_encode(data, decoded, planes, chunk_log2, transform, owner, out, capacity, written);
+}
+
+WEXB_API int wex4_bp_decode_record(const unsigned char *record, size_t total, uint32_t decoded, uint32_t owner,
+                                   unsigned char *out) {
+    if (!record || !out) return -1;
+    const int device = current_device();
+    if (device < 0) return -1;
+    std::vector<Job> jobs(1);
+    Job &j = jobs[0];
+    j.rec.codec = kCodecWbp1; j.rec.stored = (uint32_t)total; j.rec.decoded = decoded; j.rec.owner = owner;
+    j.stored = record;
+    if (total > 0xffffffffull || prepare_wbp1(j, device) != OK) return -1;
+    std::lock_guard<std::mutex> lock(g_space.mu);
+    if (!run_jobs(jobs, device) || j.status != OK) return -1;
+    if (cudaMemcpy(out, j.out_dev, decoded, cudaMemcpyDeviceToHost) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
+    return 0;
+}
 WEXB_API int wex4_fuzz_check(const unsigned char *, uint64_t, int, unsigned char *) { return E_UNSUPPORTED; }
 WEXB_API int wex4_fuzz_run(const unsigned char *, uint64_t, uint64_t, uint32_t, int, uint64_t *) { return E_UNSUPPORTED; }
 WEXB_API int wex4_store_probe(const char *, const unsigned char *, unsigned char *, uint64_t, uint32_t *) { return E_UNSUPPORTED; }

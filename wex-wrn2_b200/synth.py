@@ -174,9 +174,12 @@ class Expert:
 
 
 def make_experts(hidden, ffn, owners, seed=1, sigma=0.02, cz=False, mode=0, neg_zero=0.0, train_every=8,
-                 wchunk=2048, schunk=512, nr3=True, threads=None, blob=None):
+                 wchunk=2048, schunk=512, nr3=True, threads=None, blob=None, lean=False):
     """Experts for (layer, index) owners, a WNM2 model trained on every train_every-th of them (or the
-    given blob), and their records. Generation and encoding run on host threads."""
+    given blob), and their records. Generation and encoding run on host threads. lean (with a given
+    blob): each expert keeps only its entry, record, decoded size (.raw) and the SHA-256 of its
+    expected slab (.expected_sha), so that large pools fit in host memory."""
+    import hashlib
     sig = sigma if callable(sigma) else (lambda layer: sigma)
     threads = threads or min(32, os.cpu_count() or 4)
 
@@ -184,11 +187,23 @@ def make_experts(hidden, ffn, owners, seed=1, sigma=0.02, cz=False, mode=0, neg_
         i, (layer, idx) = i_owner
         md = mode(i) if callable(mode) else mode
         return Expert(hidden, ffn, layer, idx, seed * 1000003 + layer * 4099 + idx, sig(layer), cz, md, neg_zero, nr3)
+
+    def make_encoded(i_owner):
+        e = make(i_owner).encode(blob, wchunk, schunk, nr3)
+        e.raw = len(e.source)
+        e.expected_sha = hashlib.sha256(e.expected).digest()
+        if lean:
+            e.source = e.coded = e.expected = None
+        return e
     with ThreadPoolExecutor(threads) as pool:
+        if blob is not None:
+            return blob, list(pool.map(make_encoded, enumerate(owners)))
         experts = list(pool.map(make, enumerate(owners)))
-        if blob is None:
-            blob = train_model([(e.entry, e.coded) for e in experts[::train_every]], nr3)
+        blob = train_model([(e.entry, e.coded) for e in experts[::train_every]], nr3)
         list(pool.map(lambda e: e.encode(blob, wchunk, schunk, nr3), experts))
+    for e in experts:
+        e.raw = len(e.source)
+        e.expected_sha = hashlib.sha256(e.expected).digest()
     return blob, experts
 
 
