@@ -705,7 +705,7 @@ def main():
     ap.add_argument('--layers', type=int, default=0, help='layers per step (default: all of the config)')
     ap.add_argument('--cpu-seconds', type=float, default=12.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--depth', type=int, default=6, help='e2e: batch calls kept in flight')
+    ap.add_argument('--depth', type=int, default=3, help='e2e: batch calls kept in flight')
     args = ap.parse_args()
     assert args.warmup >= 1
     cfg = CONFIGS[args.config]

@@ -364,10 +364,22 @@ struct Job {
 struct Space {   // the container layer's device workspace: one call at a time
     std::mutex mu;
     int device = -1;
-    cudaStream_t st = nullptr;
+    cudaStream_t st = nullptr, sh = nullptr;   // uploads and decodes; record hashes
+    std::vector<cudaEvent_t> landed;           // one per group of kShaGroup uploaded records, then one for sh
     DevBuf stage, out, scratch, meta;
     PinBuf hmeta;
+    bool events(size_t n) {
+        while (landed.size() < n) {
+            cudaEvent_t e;
+            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
+            landed.push_back(e);
+        }
+        return true;
+    }
 };
+// Records whose SHA-256 starts together, as soon as their uploads have landed: a record hash is one
+// serial chain per record, so the hashes run beside the uploads of later records and the decodes.
+constexpr size_t kShaGroup = 16;
 Space g_space;
 
 // Host verdicts of a WNR3 record before its decode (c/wex4.h:685-697): entry, model id, owner and
@@ -429,8 +441,16 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     Space &S = g_space;
     if (cudaSetDevice(device) != cudaSuccess) { (void)cudaGetLastError(); return false; }
     if (S.device != device) {
-        if (S.st) { S.stage.release(); S.out.release(); S.scratch.release(); S.meta.release(); cudaStreamDestroy(S.st); }
-        if (cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) != cudaSuccess) { (void)cudaGetLastError(); S.st = nullptr; return false; }
+        if (S.st) {
+            S.stage.release(); S.out.release(); S.scratch.release(); S.meta.release();
+            cudaStreamDestroy(S.st); cudaStreamDestroy(S.sh);
+            for (cudaEvent_t e : S.landed) cudaEventDestroy(e);
+            S.landed.clear();
+        }
+        if (cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&S.sh, cudaStreamNonBlocking) != cudaSuccess) {
+            (void)cudaGetLastError(); S.st = S.sh = nullptr; S.device = -1; return false;
+        }
         S.device = device;
     }
     std::vector<size_t> at(jobs.size()), scr(jobs.size()), offs(jobs.size());
@@ -560,13 +580,24 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     if (!w4jobs.empty()) std::memcpy(hm + o_w4job, w4jobs.data(), w4jobs.size() * sizeof(W4Job));
     std::memcpy(hm + o_st, stasks.data(), stasks.size() * sizeof(Nr3Task));
     std::memcpy(hm + o_wt, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
-    cudaStream_t st = S.st;
-    bool ok = true;
-    for (size_t i = 0; ok && i < n; ++i)
-        if (jobs[i].pre == OK)
+    cudaStream_t st = S.st, sh = S.sh;
+    const size_t groups = (n + kShaGroup - 1) / kShaGroup;
+    bool ok = S.events(groups + 1) && cudaMemcpyAsync(dm, hm, m, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    // uploads in record order; each group's hashes start on sh once its records have landed
+    uint32_t sha_at = 0;
+    for (size_t g = 0; ok && g < groups; ++g) {
+        const size_t i1 = std::min(n, (g + 1) * kShaGroup);
+        uint32_t msgs = 0;
+        for (size_t i = g * kShaGroup; ok && i < i1; ++i) {
+            if (jobs[i].pre != OK) continue;
             ok = cudaMemcpyAsync(S.stage.p + at[i], jobs[i].stored, jobs[i].rec.stored, cudaMemcpyHostToDevice, st) == cudaSuccess;
-    ok = ok && cudaMemcpyAsync(dm, hm, m, cudaMemcpyHostToDevice, st) == cudaSuccess &&
-         launch_sha256_messages(reinterpret_cast<const ShaMsg *>(dm + o_sha), nsha, st) == cudaSuccess;
+            msgs += jobs[i].expect_sha != nullptr;
+        }
+        if (ok && msgs)
+            ok = cudaEventRecord(S.landed[g], st) == cudaSuccess && cudaStreamWaitEvent(sh, S.landed[g], 0) == cudaSuccess &&
+                 launch_sha256_messages(reinterpret_cast<const ShaMsg *>(dm + o_sha) + sha_at, msgs, sh) == cudaSuccess;
+        sha_at += msgs;
+    }
     for (uint32_t z = 0; ok && z < nzero; z += 65535)
         ok = launch_zero_check(reinterpret_cast<const ZeroJob *>(dm + o_zero) + z, std::min<uint32_t>(65535, nzero - z), st) == cudaSuccess;
     const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + o_recs);
@@ -579,10 +610,12 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     for (size_t g = 0; ok && g < w4runs.size(); ++g)
         ok = launch_wnr4(*w4tabs[g], reinterpret_cast<const W4Job *>(dm + o_w4job) + w4runs[g].first,
                          (uint32_t)w4runs[g].second, reinterpret_cast<const W4Rec *>(dm + o_w4rec), st) == cudaSuccess;
-    ok = ok &&
+    // the hashes rejoin the decode stream before the verdicts come back
+    ok = ok && cudaEventRecord(S.landed[groups], sh) == cudaSuccess && cudaStreamWaitEvent(st, S.landed[groups], 0) == cudaSuccess &&
          cudaMemcpyAsync(hm + o_err, dm + o_err, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
          cudaMemcpyAsync(hm + o_ver, dm + o_ver, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     if (cudaStreamSynchronize(st) != cudaSuccess) ok = false;
+    if (cudaStreamSynchronize(sh) != cudaSuccess) ok = false;
     if (!ok) { (void)cudaGetLastError(); return false; }
     const uint32_t *herr = reinterpret_cast<const uint32_t *>(hm + o_err), *hver = reinterpret_cast<const uint32_t *>(hm + o_ver);
     for (size_t i = 0; i < n; ++i) {
