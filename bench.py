@@ -162,7 +162,7 @@ def dist_init():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300))
     return world, rank, local
 
 
@@ -240,6 +240,61 @@ def reference_decode_rate(experts, blob, cores, min_seconds=10.0, max_records=No
                 break
         dt = time.perf_counter() - t0
     return dt, done, nbytes
+
+
+def reference_file_rate(data, cores, min_seconds=10.0, lib='wex4_tools_ref'):
+    """Check and decode the records of a WEX4 file with the reference's CPU tools, one record per host
+    thread, until min_seconds of work: wex4_decode_record_buf of oracle/_ref/<lib>.so (SHA-256 against
+    the index, then RAW / WNR3 / WBP1 decode; wex4_tools_fast.so is its fast WNR3 decoder), and for
+    codec-8 records the SHA-256 then the reference WNR4 decoder (oracle/_ref/wnr4_tools.so).
+    Returns (seconds, records, decoded bytes)."""
+    sys.path.insert(0, os.path.join(ROOT, 'oracle'))
+    import ctypes
+    import oracle
+    import synth
+    L, W = oracle.ref_lib(lib), oracle.ref_lib('wnr4_tools')
+    if L is None or W is None:
+        raise RuntimeError(f'oracle/_ref/{lib}.so or wnr4_tools.so is missing: build them with `make -C oracle ref`')
+    f = oracle.Wex4File(data)
+    blobs = [f.blob(i) for i in range(len(f.blobs))]
+    handles = {i: W.wnr4t_model_open(b, len(b)) for i, b in enumerate(blobs) if f.blobs[i]['kind'] == 3}
+    geos = {}
+    for r, rec in enumerate(f.records):
+        if rec['codec'] == 8:
+            ts = f.tensors[rec['first']:rec['first'] + 6]
+            g = [0] * 13
+            for m in range(3):
+                g[1 + m], g[4 + m] = ts[m]['shape'][0] * ts[m]['shape'][1], ts[m]['shape'][1]
+                g[7 + m], g[10 + m] = ts[m]['offset'], ts[3 + m]['offset']
+            geos[r] = (ctypes.c_uint32 * 13)(*g)
+    outs = [ctypes.create_string_buffer(f.max_decoded) for _ in range(cores)]
+
+    def one(i):
+        r = i % len(f.records)
+        rec, out = f.records[r], outs[i % cores]
+        stored = f.stored(r)
+        if rec['codec'] == 8:
+            if hashlib.sha256(stored).digest() != rec['sha']:
+                raise RuntimeError('record hash differs')
+            st = W.wnr4t_decode(handles[rec['blob'] - 1], geos[r], stored, len(stored), r, out, 1)
+        else:
+            blob = blobs[rec['blob'] - 1] if rec['blob'] else None
+            st = L.wex4_decode_record_buf(f.page, f.file_bytes, f.index, len(f.index), r, stored, blob, 1, out)
+        if st != 0:
+            raise RuntimeError(f'reference refused record {r}: {st}')
+        return rec['decoded']
+    with ThreadPoolExecutor(cores) as pool:
+        t0 = time.perf_counter()
+        n, nbytes = 0, 0
+        while True:
+            nbytes += sum(pool.map(one, range(n, n + cores)))
+            n += cores
+            if time.perf_counter() - t0 >= min_seconds:
+                break
+        dt = time.perf_counter() - t0
+    for h in handles.values():
+        W.wnr4t_model_close(h)
+    return dt, n, nbytes
 
 
 # ---- the two arms ---------------------------------------------------------------------------------
@@ -425,6 +480,14 @@ def run_container(args, cfg):
         'clocks': clk,
         'verified': {'digest_records': min(12, len(owners)), 'statuses': 'all 0'},
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = os.cpu_count() or 1
+        dt, n, nb = reference_file_rate(bytes(buf), cores, min_seconds=args.cpu_seconds)
+        line['cpu_baseline'] = {'value': round(nb / dt / 1e9, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
+                                'experts_per_s': round(n / dt, 2),
+                                'sample': f'{n} records of the same file, one per host thread: the reference tool\'s '
+                                          f'wex4_decode_record_buf (SHA-256, then decode; codec 8: SHA-256 and the '
+                                          f'reference WNR4 decoder), {dt:.1f} s'}
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
@@ -686,6 +749,17 @@ def run_gpu(args, cfg):
                                 'experts_per_s': round(n / dt, 2),
                                 'sample': f'{n} records of the same pool, one per host thread, reference '
                                           f'wex_nr2_decode, {dt:.1f} s'}
+        # the stronger comparator: the reference's fast CPU decoder, through its WEX4 tool, on a file of
+        # 32 records of the pool
+        import wex4file
+        sample = sorted({(e.layer, e.index): e for e in experts if e.codec == 5}.values(), key=lambda e: (e.layer, e.index))[:32]
+        fdata = wex4file.write([wex4file.expert_record(e) for e in sample], [(wex4file.BLOB_WNM2, fnv1a(blob), blob)],
+                               grid=(cfg['layers'], cfg['experts']), value_exact=cfg['cz'])
+        fdt, fn, fnb = reference_file_rate(fdata, cores, min_seconds=args.cpu_seconds / 2, lib='wex4_tools_fast')
+        line['cpu_baseline']['fast'] = {'value': round(fnb / fdt / 1e9, 4), 'unit': 'GB/s', 'cores': cores,
+                                        'experts_per_s': round(fn / fdt, 2),
+                                        'sample': f'{fn} records, one per host thread: the reference fast decoder '
+                                                  f'(wex4_tools built with WEX4_FAST_NR3, SHA-256 checked), {fdt:.1f} s'}
     res.close()
     if rank == 0:
         print(json.dumps(line))

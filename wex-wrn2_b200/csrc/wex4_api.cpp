@@ -364,8 +364,8 @@ struct Job {
 struct Space {   // the container layer's device workspace: one call at a time
     std::mutex mu;
     int device = -1;
-    cudaStream_t st = nullptr, sh = nullptr;   // uploads and decodes; record hashes
-    std::vector<cudaEvent_t> landed;           // one per group of kShaGroup uploaded records, then one for sh
+    cudaStream_t st = nullptr, sh[4] = {};     // uploads and decodes; record hashes, groups in turn
+    std::vector<cudaEvent_t> landed;           // one per group of uploaded records, then one per hash stream
     DevBuf stage, out, scratch, meta;
     PinBuf hmeta;
     bool events(size_t n) {
@@ -377,9 +377,11 @@ struct Space {   // the container layer's device workspace: one call at a time
         return true;
     }
 };
-// Records whose SHA-256 starts together, as soon as their uploads have landed: a record hash is one
-// serial chain per record, so the hashes run beside the uploads of later records and the decodes.
-constexpr size_t kShaGroup = 16;
+// Record hashes: one serial chain per record (a single thread hashes a large record at tens of MB/s),
+// so every record's hash must run concurrently with all the others. The records are split into
+// kShaStreams groups in record order; each group's hashes start on its own stream as soon as the
+// group's uploads have landed, beside the later uploads and the decodes.
+constexpr int kShaStreams = 4;
 Space g_space;
 
 // Host verdicts of a WNR3 record before its decode (c/wex4.h:685-697): entry, model id, owner and
@@ -443,14 +445,14 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     if (S.device != device) {
         if (S.st) {
             S.stage.release(); S.out.release(); S.scratch.release(); S.meta.release();
-            cudaStreamDestroy(S.st); cudaStreamDestroy(S.sh);
+            cudaStreamDestroy(S.st);
+            for (cudaStream_t h : S.sh) cudaStreamDestroy(h);
             for (cudaEvent_t e : S.landed) cudaEventDestroy(e);
             S.landed.clear();
         }
-        if (cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) != cudaSuccess ||
-            cudaStreamCreateWithFlags(&S.sh, cudaStreamNonBlocking) != cudaSuccess) {
-            (void)cudaGetLastError(); S.st = S.sh = nullptr; S.device = -1; return false;
-        }
+        bool made = cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) == cudaSuccess;
+        for (int h = 0; made && h < kShaStreams; ++h) made = cudaStreamCreateWithFlags(&S.sh[h], cudaStreamNonBlocking) == cudaSuccess;
+        if (!made) { (void)cudaGetLastError(); S.device = -1; return false; }   // streams made so far leak
         S.device = device;
     }
     std::vector<size_t> at(jobs.size()), scr(jobs.size()), offs(jobs.size());
@@ -580,19 +582,20 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     if (!w4jobs.empty()) std::memcpy(hm + o_w4job, w4jobs.data(), w4jobs.size() * sizeof(W4Job));
     std::memcpy(hm + o_st, stasks.data(), stasks.size() * sizeof(Nr3Task));
     std::memcpy(hm + o_wt, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
-    cudaStream_t st = S.st, sh = S.sh;
-    const size_t groups = (n + kShaGroup - 1) / kShaGroup;
-    bool ok = S.events(groups + 1) && cudaMemcpyAsync(dm, hm, m, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    cudaStream_t st = S.st;
+    const size_t groups = kShaStreams, per_group = (n + groups - 1) / groups;
+    bool ok = S.events(groups + kShaStreams) && cudaMemcpyAsync(dm, hm, m, cudaMemcpyHostToDevice, st) == cudaSuccess;
     // uploads in record order; each group's hashes start on sh once its records have landed
     uint32_t sha_at = 0;
     for (size_t g = 0; ok && g < groups; ++g) {
-        const size_t i1 = std::min(n, (g + 1) * kShaGroup);
+        const size_t i1 = std::min(n, (g + 1) * per_group);
         uint32_t msgs = 0;
-        for (size_t i = g * kShaGroup; ok && i < i1; ++i) {
+        for (size_t i = g * per_group; ok && i < i1; ++i) {
             if (jobs[i].pre != OK) continue;
             ok = cudaMemcpyAsync(S.stage.p + at[i], jobs[i].stored, jobs[i].rec.stored, cudaMemcpyHostToDevice, st) == cudaSuccess;
             msgs += jobs[i].expect_sha != nullptr;
         }
+        cudaStream_t sh = S.sh[g];
         if (ok && msgs)
             ok = cudaEventRecord(S.landed[g], st) == cudaSuccess && cudaStreamWaitEvent(sh, S.landed[g], 0) == cudaSuccess &&
                  launch_sha256_messages(reinterpret_cast<const ShaMsg *>(dm + o_sha) + sha_at, msgs, sh) == cudaSuccess;
@@ -611,11 +614,14 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
         ok = launch_wnr4(*w4tabs[g], reinterpret_cast<const W4Job *>(dm + o_w4job) + w4runs[g].first,
                          (uint32_t)w4runs[g].second, reinterpret_cast<const W4Rec *>(dm + o_w4rec), st) == cudaSuccess;
     // the hashes rejoin the decode stream before the verdicts come back
-    ok = ok && cudaEventRecord(S.landed[groups], sh) == cudaSuccess && cudaStreamWaitEvent(st, S.landed[groups], 0) == cudaSuccess &&
+    for (int h = 0; ok && h < kShaStreams; ++h)
+        ok = cudaEventRecord(S.landed[groups + h], S.sh[h]) == cudaSuccess &&
+             cudaStreamWaitEvent(st, S.landed[groups + h], 0) == cudaSuccess;
+    ok = ok &&
          cudaMemcpyAsync(hm + o_err, dm + o_err, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
          cudaMemcpyAsync(hm + o_ver, dm + o_ver, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     if (cudaStreamSynchronize(st) != cudaSuccess) ok = false;
-    if (cudaStreamSynchronize(sh) != cudaSuccess) ok = false;
+    for (cudaStream_t h : S.sh) if (cudaStreamSynchronize(h) != cudaSuccess) ok = false;
     if (!ok) { (void)cudaGetLastError(); return false; }
     const uint32_t *herr = reinterpret_cast<const uint32_t *>(hm + o_err), *hver = reinterpret_cast<const uint32_t *>(hm + o_ver);
     for (size_t i = 0; i < n; ++i) {

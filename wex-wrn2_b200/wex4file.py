@@ -46,10 +46,11 @@ def expert_record(expert, blob_index=0, value_exact=False, codec=None, stored=No
     codec = expert.codec if codec is None else codec
     stored = expert.record if stored is None else stored
     tensors = expert_tensors(f'layers.{expert.layer}.experts.{expert.index}', expert.hidden, expert.ffn)
+    decoded = sum(t[3] for t in tensors)
     if codec == CODEC_WNR4:
-        return Record(stored, len(expert.source), codec, tensors, 0, 1 + blob_index)
+        return Record(stored, decoded, codec, tensors, 0, 1 + blob_index)
     flags = FLAG_EXPERT | (FLAG_VALUE_EXACT if value_exact and codec == CODEC_WNR3 else 0)
-    return Record(stored, len(expert.source), codec, tensors, flags, 1 + blob_index if codec == CODEC_WNR3 else 0,
+    return Record(stored, decoded, codec, tensors, flags, 1 + blob_index if codec == CODEC_WNR3 else 0,
                   expert.layer << 16 | expert.index)
 
 
