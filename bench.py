@@ -460,6 +460,15 @@ def run_container(args, cfg):
     dt = max_over_ranks(time.perf_counter() - t0, world)
     barrier(world)
     clk = clocks.stop()
+    # the two halves of a check, each alone (one call each, after the timed region): hashes only, and
+    # decodes only
+    parts = {}
+    for name, fl in (('hashes_only_ms', 1), ('decode_only_ms', flags & ~1)):
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        assert L.wex4_check(buf.ctypes.data, len(buf), fl, digest) == 0
+        torch.cuda.synchronize()
+        parts[name] = round(1e3 * (time.perf_counter() - t1), 2)
     dec_all, stored_all, recs_all = sum_over_ranks([decoded * args.steps, len(buf) * args.steps, len(owners) * args.steps],
                                                    world)
     value = dec_all / dt / 1e9
@@ -479,6 +488,7 @@ def run_container(args, cfg):
                              'frac': round(len(buf) * args.steps / dt / 1e9 / h2d_gbs, 4)}},
         'clocks': clk,
         'verified': {'digest_records': min(12, len(owners)), 'statuses': 'all 0'},
+        'parts': parts,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cores = os.cpu_count() or 1

@@ -71,22 +71,36 @@ struct Sha {
     __device__ void update(const uint8_t *p, uint64_t n) {
         len += n;
         while (n && fill) { byte(*p++); --n; }
-        if (n >= 64) {   // whole blocks at any alignment: aligned 4-byte words joined by funnel shifts
-            const uint32_t shift = (uint32_t)(reinterpret_cast<uintptr_t>(p) & 3u) * 8u;
-            const uint32_t *q = reinterpret_cast<const uint32_t *>(reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)3);
-            const uint32_t *stop = reinterpret_cast<const uint32_t *>(p + (n & ~(uint64_t)63));
-            uint32_t v[17];
+        if (n >= 64 && !(reinterpret_cast<uintptr_t>(p) & 15)) {   // aligned whole blocks: four 16-byte loads each,
+            const uint4 *q = reinterpret_cast<const uint4 *>(p);     // the next block's issued before this block's
+            const uint4 *stop = q + 4 * (n / 64);                     // compression, an L2 prefetch 8 blocks ahead
+            uint4 v[4];
 #pragma unroll
-            for (int k = 0; k < 17; ++k) v[k] = (k < 16 || shift) ? __ldg(q + k) : 0u;
-            for (; n >= 64; n -= 64, p += 64, q += 16) {
-                // the L2 prefetch runs 8 blocks ahead of the compression (a no-op past the message)
-                if (q + 16 * 8 < stop) asm volatile("prefetch.global.L2 [%0];" :: "l"(q + 16 * 8));
+            for (int k = 0; k < 4; ++k) v[k] = __ldg(q + k);
+            for (; n >= 64; n -= 64, p += 64, q += 4) {
+                if (q + 32 < stop) asm volatile("prefetch.global.L2 [%0];" :: "l"(q + 32));
                 uint32_t w[16];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) w[k] = bswap(__funnelshift_r(v[k], v[k + 1], shift));
+                for (int k = 0; k < 4; ++k) {
+                    w[4 * k] = bswap(v[k].x); w[4 * k + 1] = bswap(v[k].y); w[4 * k + 2] = bswap(v[k].z); w[4 * k + 3] = bswap(v[k].w);
+                }
                 if (n >= 128) {
 #pragma unroll
-                    for (int k = 0; k < 17; ++k) v[k] = (k < 16 || shift) ? __ldg(q + 16 + k) : 0u;
+                    for (int k = 0; k < 4; ++k) v[k] = __ldg(q + 4 + k);
+                }
+                compress(st, w);
+            }
+        } else if (n >= 64) {   // unaligned whole blocks: aligned 4-byte words joined by funnel shifts
+            const uint32_t shift = (uint32_t)(reinterpret_cast<uintptr_t>(p) & 3u) * 8u;
+            const uint32_t *q = reinterpret_cast<const uint32_t *>(reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)3);
+            for (; n >= 64; n -= 64, p += 64, q += 16) {
+                uint32_t w[16], next = __ldg(q);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const uint32_t cur = next;
+                    // the 17th word holds the block's last bytes only when the block is unaligned
+                    next = (k < 15 || shift) ? __ldg(q + k + 1) : 0u;
+                    w[k] = bswap(__funnelshift_r(cur, next, shift));
                 }
                 compress(st, w);
             }
