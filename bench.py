@@ -45,6 +45,9 @@ CONFIGS = {
     'mid': dict(hidden=2048, ffn=768, layers=48, experts=128, batch=8, cz=False, sigma=(0.01, 0.04), neg_zero=0.0),
     'large': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
                   lean=True),
+    # whole-box streaming: 1536 large experts, each rank decodes all of its shard every step
+    'box': dict(hidden=7168, ffn=2048, layers=8, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
+                lean=True, all_experts=True),
     # containers: a WEX4 file per rank, checked and decoded by wex4_check (per-record SHA-256 against
     # the index, codec dispatch, decode); tiny = the 8 experts plus one RAW expert, mixed = one routed
     # step of large experts, 10 % uniform-random (stored RAW), 30 % WNR4 kind MX, the rest WNR3 CZ
@@ -69,8 +72,11 @@ def layer_sigmas(cfg):
 
 
 def routing_trace(cfg, steps, rank, world, layers):
-    """[step][layer] -> 8 distinct expert ids of this rank's shard (id % world == rank), Zipf(1.1)."""
+    """[step][layer] -> 8 distinct expert ids of this rank's shard (id % world == rank), Zipf(1.1); for a
+    streaming config (all_experts) every expert of the shard, every step."""
     shard = np.arange(rank, cfg['experts'], world)
+    if cfg.get('all_experts'):
+        return [[[int(e) for e in shard] for _ in range(layers)] for _ in range(steps)]
     trace = []
     for layer in range(layers):
         rng = np.random.default_rng([SEED, layer, rank])
@@ -162,7 +168,8 @@ def dist_init():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300))
+        os.environ.setdefault('NCCL_DEBUG', 'WARN')   # rank 0's stdout carries only the JSON line
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=torch.device('cuda', local))
     return world, rank, local
 
 
@@ -298,19 +305,49 @@ def reference_file_rate(data, cores, min_seconds=10.0, lib='wex4_tools_ref'):
 
 
 # ---- the two arms ---------------------------------------------------------------------------------
+def run_reference_container(args, cfg):
+    """The reference arm of a container config: rank 0's file checked and decoded record by record by the
+    reference's CPU tools on all host cores (a bounded sample of records per step)."""
+    cores = os.cpu_count() or 1
+    layers = args.layers or cfg['layers']
+    owners = container_owners(cfg, 0, int(os.environ.get('WORLD_SIZE', '1')), layers)
+    data, decoded, counts, _, _ = build_container(cfg, owners, cores)
+    times = []
+    for s in range(args.warmup + args.steps):
+        dt, n, nb = reference_file_rate(data, cores, min_seconds=max(1.0, args.cpu_seconds / (args.warmup + args.steps)))
+        if s >= args.warmup:
+            times.append((dt, n, nb))
+    total = sum(t[0] for t in times)
+    nbytes, nrec = sum(t[2] for t in times), sum(t[1] for t in times)
+    value = nbytes / total / 1e9
+    print(json.dumps({
+        'impl': 'reference', 'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 4), 'unit': 'GB/s',
+        'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(1e3 * total / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'experts_per_s': round(nrec / total, 2),
+        'config': {'workload': f'{args.config}: WEX4 container of {len(owners)} expert records, codecs {counts}'},
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
+                         'sample': 'records of the file, one per host thread, the reference tool (SHA-256, decode)'},
+        'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
+    return 0
+
+
 def run_reference(args, cfg):
     world, rank, local = int(os.environ.get('WORLD_SIZE', '1')), int(os.environ.get('RANK', '0')), 0
     if rank != 0:
         return 0
+    if cfg.get('container'):
+        return run_reference_container(args, cfg)
     cores = os.cpu_count() or 1
     layers = args.layers or cfg['layers']
     trace = routing_trace(cfg, args.warmup + args.steps, 0, 1, layers)
+    k = sum(len(trace[0][l]) for l in range(layers))   # records per step of the GPU arm's workload
     # one step of the reference arm: ceil(cores / 8) layer batches of the trace (bounded sample)
     per_step = max(1, min(layers, -(-cores // cfg['batch'])))
     owners = []
     for s in range(args.warmup + args.steps):
         for l in range(per_step):
-            for e in trace[s][(s * per_step + l) % layers]:
+            for e in trace[s][(s * per_step + l) % layers][:cfg['batch']]:
                 if ((s * per_step + l) % layers, int(e)) not in owners:
                     owners.append(((s * per_step + l) % layers, int(e)))
     blob, experts = build_pool(cfg, owners, threads=cores)
@@ -332,7 +369,7 @@ def run_reference(args, cfg):
     with ThreadPoolExecutor(cores) as pool:
         for s in range(args.warmup + args.steps):
             recs = [by_owner[((s * per_step + l) % layers, int(e))] for l in range(per_step)
-                    for e in trace[s][(s * per_step + l) % layers]]
+                    for e in trace[s][(s * per_step + l) % layers][:cfg['batch']]]
             t0 = time.perf_counter()
             b = sum(pool.map(one, recs))
             dt = time.perf_counter() - t0
@@ -345,7 +382,7 @@ def run_reference(args, cfg):
         'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(1e3 * total / args.steps, 3),
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
         'experts_per_s': round(nrec / total, 2),
-        'config': config_desc(args, cfg),
+        'config': config_desc(args, cfg, k),
         'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
                          'sample': f'{per_step} layer batch(es) of {cfg["batch"]} records per step, one record per '
                                    f'host thread, reference wex_nr2_decode'},
@@ -532,11 +569,17 @@ def profile_traffic_per_record(config):
     return None
 
 
-def config_desc(args, cfg):
+def config_desc(args, cfg, records):
+    if cfg.get('all_experts'):
+        return {'workload': f'{args.config}: streaming decode of every expert of the rank\'s shard (expert id mod '
+                            f'world size) each step, WNR3 MXFP4 experts, hidden {cfg["hidden"]}, expert FFN {cfg["ffn"]}, '
+                            f'{cfg["layers"] * cfg["experts"]} experts in all' + (', canonical zero' if cfg['cz'] else ''),
+                'records_per_step_per_gpu': records, 'chunks': '2048:512', 'placement': 'expert id mod world size',
+                'l2': 'inputs larger than L2 (126 MB) between steps'}
     return {'workload': f'{args.config}: routed decode of WNR3 MXFP4 experts, hidden {cfg["hidden"]}, expert FFN '
                         f'{cfg["ffn"]}, {args.layers or cfg["layers"]} layers x {cfg["experts"]} experts, top-'
                         f'{cfg["batch"]} Zipf(1.1) per layer per step' + (', canonical zero' if cfg['cz'] else ''),
-            'records_per_step_per_gpu': (args.layers or cfg['layers']) * cfg['batch'],
+            'records_per_step_per_gpu': records,
             'chunks': '2048:512', 'placement': 'expert id mod world size',
             'l2': 'inputs larger than L2 (126 MB) between steps'}
 
@@ -560,7 +603,7 @@ def run_gpu(args, cfg):
     assert wexcuda.register_model(blob) == 0
     hostbuf, views = pinned_records(experts)
     raw = experts[0].raw
-    k = layers * cfg['batch']
+    k = sum(len(trace[0][l]) for l in range(layers))   # records per step
     # destinations of one step: 384 experts' six regions
     sizes = [r * c // 32 for r, c in [(cfg['ffn'], cfg['hidden']), (cfg['hidden'], cfg['ffn']), (cfg['ffn'], cfg['hidden'])]]
     dst = torch.empty((k, raw), dtype=torch.uint8, device='cuda')
@@ -622,13 +665,14 @@ def run_gpu(args, cfg):
     for s in range(steps_total):
         ids = step_idx[s]
         per = []
-        for l in range(layers):
-            sel = ids[l * B:(l + 1) * B]
+        for c in range(0, k, B):   # one call per B records (a layer's batch)
+            sel = ids[c:c + B]
             per.append((wexcuda._ptrs([entry_store[i].ctypes.data for i in sel]),
                         wexcuda._ptrs([views[i].ctypes.data for i in sel]),
-                        wexcuda._ptrs(dscale[3 * l * B:3 * (l + 1) * B]), wexcuda._ptrs(dweight[3 * l * B:3 * (l + 1) * B]),
+                        wexcuda._ptrs(dscale[3 * c:3 * (c + B)]), wexcuda._ptrs(dweight[3 * c:3 * (c + B)]),
                         (ctypes.c_int * B)()))
         call_args.append(per)
+    ncalls = len(call_args[0])
 
     def sync_step(s):
         bad = 0
@@ -719,12 +763,12 @@ def run_gpu(args, cfg):
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(value_ms / args.steps, 3),
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
         'experts_per_s': round(recs_all / (value_ms / 1e3), 1),
-        'config': config_desc(args, cfg),
+        'config': config_desc(args, cfg, k),
         'e2e': {'value': round(e2e, 3), 'unit': 'GB/s', 'experts_per_s': round(recs_all / e2e_s, 1),
                 'h2d_bytes_per_step': int(h2d_per_step), 'd2h_bytes_per_step': 4 * k,
-                'api': f'wexb_batch_submit/wexb_batch_wait, {B} records per call, {layers} calls per step, '
+                'api': f'wexb_batch_submit/wexb_batch_wait, {B} records per call, {ncalls} calls per step, '
                        f'{args.depth} calls in flight',
-                'ms_per_step': round(1e3 * e2e_s / args.steps, 3), 'gpu_launches': 3 * layers * args.steps,
+                'ms_per_step': round(1e3 * e2e_s / args.steps, 3), 'gpu_launches': 3 * ncalls * args.steps,
                 'sync': {'value': round(e2e_sync, 3), 'unit': 'GB/s',
                          'api': 'wex_cuda_decode_batch_to_device (drop-in, synchronous)',
                          'ms_per_step': round(1e3 * sync_s / args.steps, 3)},
