@@ -67,3 +67,21 @@ def test_two_cpu_ranks():
     for rank, layer, expert, _, _ in table:
         assert owner.setdefault((layer, expert), rank) == rank
     assert {r for r, *_ in table} == {0, 1}
+
+
+def test_streaming_trace_covers_every_expert_once_per_step():
+    """The whole-box config: each rank decodes all of its shard every step, and the shards of all ranks
+    partition the experts of every layer."""
+    sys.path.insert(0, ROOT)
+    import bench
+    cfg = bench.CONFIGS['box']
+    for world in (1, 2, 8):
+        seen = {}
+        for rank in range(world):
+            trace = bench.routing_trace(cfg, 2, rank, world, cfg['layers'])
+            assert trace[0] == trace[1]
+            for l, layer in enumerate(trace[0]):
+                assert all(e % world == rank for e in layer)
+                for e in layer:
+                    assert seen.setdefault((l, e), rank) == rank
+        assert len(seen) == cfg['layers'] * cfg['experts']

@@ -116,19 +116,96 @@ struct Sha {
     }
 };
 
-__global__ void __launch_bounds__(64) sha256_messages(const ShaMsg *__restrict__ msgs, uint32_t n) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const ShaMsg m = msgs[i];
-    Sha s;
-    s.start();
-    s.update(m.data, m.bytes);
-    uint8_t got[32];
-    s.finish(got);
+// Record hashes, two warps per 32 messages (lane l of both warps serves message l of the CTA). A single
+// thread's chain is issue-bound on the integer pipe, so the work is split: warp 1 loads each 64-byte
+// block (or builds the padded last blocks) and expands its schedule into W[t] + K[t] in shared memory;
+// warp 0 runs only the 64 rounds from there. Two slots alternate, with one CTA barrier per block;
+// messages shorter than the CTA's longest keep their final state through the extra blocks.
+constexpr int kShaLanes = 32;
+__device__ __forceinline__ uint32_t msg_blocks(uint64_t bytes) { return (uint32_t)((bytes + 9 + 63) / 64); }
+
+__device__ __forceinline__ void produce_block(const uint8_t *data, uint64_t bytes, uint32_t b, uint32_t w[16]) {
+    const uint64_t at = 64ull * b;
+    if (at + 64 <= bytes) {   // a whole data block (data is 16-byte aligned)
+        const uint4 *q = reinterpret_cast<const uint4 *>(data + at);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 v = __ldg(q + k);
+            w[4 * k] = bswap(v.x); w[4 * k + 1] = bswap(v.y); w[4 * k + 2] = bswap(v.z); w[4 * k + 3] = bswap(v.w);
+        }
+        return;
+    }
+    // the message end: data bytes, 0x80, zeros, and in the last block the bit length (big-endian)
+    const uint64_t bits = bytes * 8;
+    const bool last = b + 1 == msg_blocks(bytes);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        uint32_t v = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint64_t pos = at + 4 * k + j;
+            const uint32_t byte = pos < bytes ? data[pos] : pos == bytes ? 0x80u : 0u;
+            v = v << 8 | byte;
+        }
+        w[k] = v;
+    }
+    if (last) { w[14] = (uint32_t)(bits >> 32); w[15] = (uint32_t)bits; }
+}
+
+__global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *__restrict__ msgs, uint32_t n) {
+    __shared__ uint32_t sched[2][64][kShaLanes];   // [slot][round][lane]: W[t] + K[t]
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t i = blockIdx.x * kShaLanes + lane;
+    const bool active = i < n;
+    const ShaMsg m = active ? msgs[i] : ShaMsg{nullptr, 0, nullptr, nullptr, nullptr, 0};
+    const uint32_t mine = active ? msg_blocks(m.bytes) : 0u;
+    const uint32_t blocks = __reduce_max_sync(0xffffffffu, mine);
+    if (warp == 1) {   // producer
+        for (uint32_t b = 0; b < blocks; ++b) {
+            if (b < mine) {
+                if (64ull * (b + 8) + 64 <= m.bytes) asm volatile("prefetch.global.L2 [%0];" :: "l"(m.data + 64ull * (b + 8)));
+                uint32_t w[16];
+                produce_block(m.data, m.bytes, b, w);
+                uint32_t (*out)[kShaLanes] = sched[b & 1];
+#pragma unroll
+                for (int t = 0; t < 64; ++t) {
+                    uint32_t wt;
+                    if (t < 16) {
+                        wt = w[t];
+                    } else {
+                        const uint32_t w15 = w[(t - 15) & 15], w2 = w[(t - 2) & 15];
+                        wt = w[t & 15] + (ror(w15, 7) ^ ror(w15, 18) ^ (w15 >> 3)) + w[(t - 7) & 15] +
+                             (ror(w2, 17) ^ ror(w2, 19) ^ (w2 >> 10));
+                        w[t & 15] = wt;
+                    }
+                    out[t][lane] = wt + kSha[t];
+                }
+            }
+            __syncthreads();
+        }
+        return;
+    }
+    uint32_t st[8];   // consumer
+    init(st);
+    for (uint32_t b = 0; b < blocks; ++b) {
+        __syncthreads();
+        if (b >= mine) continue;
+        const uint32_t (*in)[kShaLanes] = sched[b & 1];
+        uint32_t a = st[0], bb = st[1], c = st[2], d = st[3], e = st[4], f = st[5], g = st[6], h = st[7];
+#pragma unroll
+        for (int t = 0; t < 64; ++t) {
+            const uint32_t t1 = h + (ror(e, 6) ^ ror(e, 11) ^ ror(e, 25)) + ((e & f) ^ (~e & g)) + in[t][lane];
+            const uint32_t t2 = (ror(a, 2) ^ ror(a, 13) ^ ror(a, 22)) + ((a & bb) ^ (a & c) ^ (bb & c));
+            h = g; g = f; f = e; e = d + t1; d = c; c = bb; bb = a; a = t1 + t2;
+        }
+        st[0] += a; st[1] += bb; st[2] += c; st[3] += d; st[4] += e; st[5] += f; st[6] += g; st[7] += h;
+    }
+    if (!active) return;
     uint32_t differ = 0;
     for (int k = 0; k < 32; ++k) {
-        if (m.digest) m.digest[k] = got[k];
-        if (m.expect) differ |= got[k] ^ m.expect[k];
+        const uint8_t got = (uint8_t)(st[k / 4] >> (24 - 8 * (k % 4)));
+        if (m.digest) m.digest[k] = got;
+        if (m.expect) differ |= got ^ m.expect[k];
     }
     if (m.verdict) *m.verdict = m.expect ? (differ ? 1u : 0u) : 0u;
 }
@@ -145,7 +222,7 @@ __global__ void sha256_segments(const ShaMsg *__restrict__ segs, uint32_t n, uin
 
 cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st) {
     if (!n) return cudaSuccess;
-    sha256_messages<<<(n + 63) / 64, 64, 0, st>>>(msgs, n);
+    sha256_messages<<<(n + kShaLanes - 1) / kShaLanes, 2 * kShaLanes, 0, st>>>(msgs, n);
     return cudaGetLastError();
 }
 

@@ -15,7 +15,7 @@ struct ShaMsg {
     uint32_t pad;
 };
 
-// One thread per message: digests and verdicts of n messages.
+// Digests and verdicts of n messages (each 16-byte aligned).
 cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st);
 // One thread: the digest of the concatenation of n segments (data and bytes used).
 cudaError_t launch_sha256_segments(const ShaMsg *segs, uint32_t n, uint8_t *digest, cudaStream_t st);
