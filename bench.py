@@ -179,6 +179,27 @@ def _reduce_device():
     return 'cuda' if dist.get_backend() == 'nccl' else 'cpu'
 
 
+def bind_to_gpu_numa_node(local):
+    """Run this rank on the CPUs of its GPU's NUMA node, so that the pinned host records it allocates
+    and fills (first touch) are local to the GPU's PCIe root. Returns the node, or None when the
+    topology is not visible."""
+    import torch
+    try:
+        props = torch.cuda.get_device_properties(local)
+        bus = f'{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0'
+        node = int(open(f'/sys/bus/pci/devices/{bus}/numa_node').read())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in open(f'/sys/devices/system/node/node{node}/cpulist').read().strip().split(','):
+            lo, _, hi = part.partition('-')
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        os.sched_setaffinity(0, cpus)
+        return node
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def max_over_ranks(x, world):
     if world == 1:
         return x
@@ -590,11 +611,17 @@ def run_gpu(args, cfg):
     world, rank, local = dist_init()
     torch.cuda.set_device(local)
     dev = local
+    numa = bind_to_gpu_numa_node(local) if world > 1 else None
     layers = args.layers or cfg['layers']
     steps_total = args.warmup + args.steps
     trace = routing_trace(cfg, steps_total, rank, world, layers)
     owners = sorted({(l, int(e)) for s in range(steps_total) for l in range(layers) for e in trace[s][l]})
-    threads = max(1, (os.cpu_count() or 8) // max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world))))
+    local_world = max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world)))
+    if numa is not None:   # the node's CPUs shared by the ranks bound to it
+        nodes = sum(1 for d in os.listdir('/sys/devices/system/node') if d.startswith('node') and d[4:].isdigit())
+        threads = max(1, len(os.sched_getaffinity(0)) // max(1, -(-local_world // max(1, nodes))))
+    else:
+        threads = max(1, (os.cpu_count() or 8) // local_world)
     t0 = time.time()
     blob, experts = build_pool(cfg, owners, threads)
     log(f'[rank {rank}] {len(experts)} experts generated and encoded in {time.time() - t0:.1f} s')
