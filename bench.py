@@ -210,6 +210,10 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def min_over_ranks(x, world):
+    return -max_over_ranks(-x, world)
+
+
 def sum_over_ranks(vals, world):
     if world == 1:
         return vals
@@ -504,7 +508,8 @@ def run_container(args, cfg):
     assert L.wex4_check(vbuf.ctypes.data, len(vbuf), 1 | 2 | 4, digest) == 0, 'verification file refused'
     assert digest.raw == vdigest, 'content digest differs'
     flags = 1 | 2 | 4 | (8 if len(owners) > 16 else 0)   # hashes, decode, codec 8 (digest only on small files)
-    h2d_gbs = measure_h2d(torch)
+    barrier(world)
+    h2d_gbs = min_over_ranks(measure_h2d(torch), world)   # every rank copying at once
     for _ in range(args.warmup):
         assert L.wex4_check(buf.ctypes.data, len(buf), flags, digest) == 0
     clocks = Clocks(local)
@@ -646,6 +651,8 @@ def run_gpu(args, cfg):
     assert res.failures == 0
     res.profile(True)
     h2d_gbs = measure_h2d(torch)
+    barrier(world)
+    h2d_together = min_over_ranks(measure_h2d(torch), world) if world > 1 else h2d_gbs   # every rank copying at once
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     kernel_ms, launches = [], 0
@@ -800,9 +807,11 @@ def run_gpu(args, cfg):
                          'api': 'wex_cuda_decode_batch_to_device (drop-in, synchronous)',
                          'ms_per_step': round(1e3 * sync_s / args.steps, 3)},
                 'roofline': {'bound': 'h2d', 'achieved': round(h2d_per_step / e2e_step_s / 1e9, 2),
-                             'peak': round(h2d_gbs, 2), 'unit': 'GB/s (stored bytes per GPU)',
-                             'frac': round(h2d_per_step / e2e_step_s / 1e9 / h2d_gbs, 4),
-                             'peak_source': 'measured here: one pinned 256 MiB host-to-device copy, best of 5',
+                             'peak': round(h2d_together, 2), 'unit': 'GB/s (stored bytes per GPU)',
+                             'frac': round(h2d_per_step / e2e_step_s / 1e9 / h2d_together, 4),
+                             'peak_source': 'measured here: one pinned 256 MiB host-to-device copy, best of 5, '
+                                            'every rank copying at once (the slowest rank)',
+                             'peak_one_gpu': round(h2d_gbs, 2),
                              'hbm_frac': round(hbm_bytes / e2e_step_s / 1e9 / hbm_peak, 4)}},
         'value_roofline': {'bound': 'hbm', 'achieved': round(hbm_bytes / step_s / 1e9, 2), 'peak': hbm_peak, 'unit': 'GB/s',
                            'frac': round(hbm_bytes / step_s / 1e9 / hbm_peak, 4),
