@@ -1,7 +1,7 @@
 /* ORACLE — test infrastructure only. Never linked, loaded or called by the product.
  *
  * A plain-C restatement of the reference's CPU semantics for the WEX4 expert decode path, used by
- * tests/, the smoke check and the bench's CPU-baseline leg as the checker of the CUDA decoder.
+ * tests/, the smoke check and the bench's CPU-baseline leg to check the CUDA decoder against.
  * Each function names the reference lines it follows (paths inside the reference project).
  * Parity of this restatement is pinned in tests/ against:
  *   - the reference's own compiled CPU tools (oracle/_ref/, built by `make -C oracle ref`),

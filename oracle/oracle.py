@@ -128,7 +128,7 @@ def ref_lib(name):
 # ---- a minimal WEX4 index reader (c/wex4.h:185-236), enough to pull records out of a file ------
 class Wex4File:
     """Header fields, blob / record / tensor rows of a WEX4 file held in memory (no validation
-    beyond what slicing needs: the reference tools judge validity in the tests)."""
+    beyond what slicing needs: the reference tools decide validity in the tests)."""
 
     def __init__(self, data):
         self.data = data = bytes(data)
