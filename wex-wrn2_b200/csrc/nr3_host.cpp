@@ -52,10 +52,10 @@ void build_image(const uint8_t *blob, std::vector<uint8_t> &img) {
                 uint32_t cdf[17];
                 for (uint32_t k = 0; k < 17; ++k) cdf[k] = rd16(c + 2 * k);
                 l1[2 * idx] = cdf[4] | cdf[8] << 16;
-                l1[2 * idx + 1] = cdf[12] + 0x4000u;
-                for (uint32_t k = 0; k < 16; ++k) {
-                    const uint32_t f = cdf[k + 1] - cdf[k];
-                    l2[16 * idx + k] = cdf[k] << 18 | (f ? f - 1u : 0u) << 4 | k;
+                l1[2 * idx + 1] = cdf[12] | kTotal << 16;
+                for (uint32_t q = 0; q < 4; ++q) {
+                    l2[8 * idx + 2 * q] = cdf[4 * q] | cdf[4 * q + 1] << 16;
+                    l2[8 * idx + 2 * q + 1] = cdf[4 * q + 2] | cdf[4 * q + 3] << 16;
                 }
             }
         }

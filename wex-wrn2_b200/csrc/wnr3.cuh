@@ -27,9 +27,9 @@ constexpr uint32_t kErrStruct = 1, kErrHash = 2, kErrCeil = 4, kErrCz = 8, kErrT
 // only ever takes pm <= mx < 8 (pm the previous magnitude, mx the block's maximum so far) or the
 // block start pm = mx = 8, so each srel has 37 reachable contexts: pair index mx (mx + 1) / 2 + pm,
 // and 36 for the block start. The tables hold those 7 x 37 = 259 contexts of each matrix:
-//   level 1 [259] of 8 B   cdf[4] | cdf[8] << 16,  cdf[12] + 2^14   (picks the quartile q)
-//   level 2 [259][4] of 16 B, quartile q: for i = 4q .. 4q + 3 the word
-//           cdf[i] << 18 | (freq[i] - 1) << 4 | i   (a zero-frequency symbol is never selected)
+//   level 1 [259] of 8 B   cdf[4] | cdf[8] << 16,  cdf[12] | 2^14 << 16   (picks the quartile q; its
+//                          fields are also cdf[4q + 4], the end of quartile q)
+//   level 2 [259][4] of 8 B, quartile q: cdf[4q] | cdf[4q+1] << 16,  cdf[4q+2] | cdf[4q+3] << 16
 //   sdir[m][slot]    (slot - start) | frequency << 14 of the scale symbol owning slot
 //   ssym[m][slot]    that scale symbol
 struct Nr3Tables {
@@ -40,7 +40,7 @@ struct Nr3Tables {
 constexpr uint32_t kPairs = 37;                                        // contexts per srel
 constexpr uint32_t kWContexts = 7u * kPairs;                           // 259
 constexpr uint32_t kWL1Bytes = (kWContexts * 8u + 15u) & ~15u;         // 2,080
-constexpr uint32_t kWBlockBytes = kWL1Bytes + kWContexts * 64u;        // 18,656 per matrix
+constexpr uint32_t kWBlockBytes = kWL1Bytes + kWContexts * 32u;        // 10,368 per matrix
 constexpr size_t kWTableBytes = 3ull * kWBlockBytes;
 constexpr size_t kSdirBytes = 3ull * kTotal * 4u;
 constexpr size_t kSsymBytes = 3ull * kTotal;

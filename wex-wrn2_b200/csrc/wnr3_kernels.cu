@@ -6,13 +6,13 @@
 // cp.async copies kept 24 words ahead of the read position (ring word w of lane l at
 // ring[(w % 32) * blockDim + l]: conflict-free whatever position each lane is at).
 //
-// Weight symbol lookup, two shared loads: the context's level-1 entry (8 B) gives the quartile q
-// of the slot from three packed 16-bit comparisons (each a subtraction whose flag bit is set
-// exactly when cdf <= slot), then the quartile's four symbol words (16 B) are compared against
-// slot << 18 | 0x3ffff, and the last one not above it is the symbol, carrying its start,
-// frequency - 1 and index. Renormalisation is branch-free: from a valid state a symbol leaves at
-// least 2^9, so it takes 0, 1 or 2 bytes (from the count of leading zeros), read as one
-// big-endian pair.
+// Weight symbol lookup, two 8-byte shared loads: the context's level-1 entry gives the quartile q of
+// the slot from three packed 16-bit comparisons (each a subtraction whose flag bit is set exactly when
+// cdf <= slot), then the quartile's four cumulative frequencies give the symbol's rank r in it the
+// same way; start and end are the two adjacent 16-bit fields r, r + 1 of the quartile row followed by
+// its end (a field of the level-1 entry), taken by one funnel shift. Renormalisation is branch-free:
+// from a valid state a symbol leaves at least 2^9, so it takes 0, 1 or 2 bytes (from the count of
+// leading zeros), read as one big-endian pair.
 #include "wnr3.cuh"
 #include "rans_device.cuh"
 
@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const N
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar;
     const uint2 *level1 = reinterpret_cast<const uint2 *>(smem);
-    const uint4 *level2 = reinterpret_cast<const uint4 *>(smem + kWL1Bytes);
+    const uint2 *level2 = reinterpret_cast<const uint2 *>(smem + kWL1Bytes);
     uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kWBlockBytes);
     const Nr3Task task = tasks[blockIdx.x];
     const Nr3Record &R = recs[task.rec];
@@ -195,28 +195,32 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const N
         const int d = (int)scale - anchor;
         const uint32_t srel = (uint32_t)(min(max(d, -3), 3) + 3) * kPairs;
         const uint2 *l1 = level1 + srel;
-        const uint4 *l2 = level2 + 4u * srel;
+        const uint2 *l2 = level2 + 4u * srel;
         uint32_t idx = kPairs - 1u, top = 0, w[4] = {0, 0, 0, 0};   // the block-start context
 #pragma unroll
         for (uint32_t k = 0; k < 32; ++k) {
             if (k == 0 || k == 16) rd.refill();
             const uint32_t two = rd.peek();
             const uint2 c = l1[idx];
-            // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]: bits 15 and 31 of
-            // (slot | 0x8000) * 0x10001 - (cdf[4] | cdf[8] << 16), bit 14 of that minus cdf[12] + 2^14
-            const uint32_t gs = (x & (kTotal - 1u)) * 0x10001u + 0x80008000u;
-            const uint32_t q = __popc(((gs - c.x) & 0x80008000u) | ((gs - c.y) & 0x4000u));
-            const uint4 e = l2[4u * idx + q];
-            const uint32_t key = x * (1u << 18) + 0x3ffffu;   // slot << 18 | 0x3ffff
-            uint32_t p = e.x;
-            p = key >= e.y ? e.y : p;
-            p = key >= e.z ? e.z : p;
-            p = key >= e.w ? e.w : p;
-            const uint32_t xs = x >> kPrec;
-            x = ((p >> 4) & 0x3fffu) * xs + xs + ((key - p) >> 18);   // freq * (x >> 14) + slot - start
+            const uint32_t slot = x & (kTotal - 1u), gs = slot * 0x10001u + 0x80008000u;
+            // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]
+            const uint32_t d1 = gs - c.y;
+            const uint32_t q = __popc(((gs - c.x) & 0x80008000u) | ((d1 >> 1) & 0x4000u));
+            const uint2 row = l2[4u * idx + q];   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
+            // r = [cdf[4q+1] <= slot] + [cdf[4q+2] <= slot] + [cdf[4q+3] <= slot]
+            const uint32_t r = __popc(((gs - row.y) & 0x80008000u) | ((gs - row.x) >> 31));
+            // cdf[4q+4]: field q of cdf[4], cdf[8], cdf[12], 2^14
+            const uint32_t bw = (q & 2u) ? c.y : c.x;
+            const uint32_t bound = (bw >> ((q & 1u) << 4)) & 0xffffu;
+            // start | end << 16 = fields r, r + 1 of cdf[4q .. 4q+3], bound
+            const uint32_t lo = (r & 2u) ? row.y : row.x, hi = (r & 2u) ? bound : row.y;
+            const uint32_t pair = __funnelshift_r(lo, hi, (r & 1u) << 4);
+            const uint32_t start = pair & 0xffffu, freq = (pair >> 16) - start;
+            x = freq * (x >> kPrec) + slot - start;
+            const uint32_t sym = 4u * q + r;
             x = rd.renorm(x, two);
-            w[k / 8u] += (p & 15u) << (4u * (k % 8u));
-            const uint32_t mag = p & 7u;
+            w[k / 8u] += sym << (4u * (k % 8u));
+            const uint32_t mag = sym & 7u;
             top = max(top, mag);
             idx = ((top * top + top) >> 1) + mag;
         }
