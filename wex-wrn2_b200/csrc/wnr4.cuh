@@ -13,14 +13,23 @@ constexpr uint32_t kW4L = 0x10000u;
 constexpr uint32_t kW4Classes = 7;           // MX: scale class = clamp(scale - anchor, -3, 3) + 3
 constexpr uint32_t kW4Err = 1, kW4ErrHash = 2, kW4ErrCeil = 4, kW4ErrCz = 8;
 
-// Per model and device. Per matrix: `rows` weight rows of cdf[0..15] (u16, 32 B), then the scale CDF
-// cdf[0..256] (u16) padded to 544 B, whose first 32 B hold the coarse row cdf[0], cdf[16], .., cdf[240].
+// Per model and device, per matrix: the weight rows of the reachable contexts, then the scale block.
+// A weight context (cls * 9 + pm) * 9 + mx (wnr4/wnr4.h, kind MX) only takes pm <= mx < 8 or the block
+// start pm = mx = 8: 37 pairs per class (pair index mx (mx + 1) / 2 + pm, 36 for the block start), and
+// pb position buckets each (pb = 5: bucket k - 27 for the last four nibbles of a cell). Row index
+// (cls * 37 + pair) * pb + bucket, rows = 7 * 37 * pb:
+//   level 1 [rows] of 8 B    cdf[4] | cdf[8] << 16,  cdf[12] | 2^14 << 16   (padded to 16 B)
+//   level 2 [rows][4] of 8 B quartile q: cdf[4q] | cdf[4q+1] << 16,  cdf[4q+2] | cdf[4q+3] << 16
+// The scale block: the coarse row cdf[0], cdf[16], .., cdf[240], then the scale CDF cdf[0..256] (u16).
 struct W4Tables {
     const uint8_t *base;   // [3][matrix_bytes]
     uint32_t rows, pb, matrix_bytes, id;
 };
+constexpr uint32_t kW4Pairs = 37;
 constexpr uint32_t kW4ScaleBlock = 32u + 514u + 30u;   // coarse row, cdf[0..256], padding to a multiple of 16 B
-inline uint32_t w4_matrix_bytes(uint32_t rows) { return rows * 32u + kW4ScaleBlock; }
+__host__ __device__ inline uint32_t w4_rows(uint32_t pb) { return kW4Classes * kW4Pairs * pb; }
+__host__ __device__ inline uint32_t w4_l1_bytes(uint32_t rows) { return (rows * 8u + 15u) & ~15u; }
+__host__ __device__ inline uint32_t w4_matrix_bytes(uint32_t rows) { return w4_l1_bytes(rows) + rows * 32u + kW4ScaleBlock; }
 
 // One record of a batch.
 struct W4Rec {

@@ -50,15 +50,37 @@ int model4_validate(const uint8_t *b, size_t bytes, uint32_t *pb, uint32_t *id) 
     return 0;
 }
 
-// Device image: per matrix the weight rows (cdf[0..15], 32 B each), then the scale block.
+// Device image (wnr4.cuh): per matrix the two-level weight rows of the reachable contexts, then the
+// scale block.
 std::vector<uint8_t> model4_image(const uint8_t *b, uint32_t pb) {
-    const uint32_t rows = kW4Classes * 81u * pb, mb = w4_matrix_bytes(rows);
+    const uint32_t full = kW4Classes * 81u * pb, rows = w4_rows(pb), mb = w4_matrix_bytes(rows), l1b = w4_l1_bytes(rows);
     std::vector<uint8_t> img(3ull * mb, 0);
     for (uint32_t m = 0; m < 3; ++m) {
         uint8_t *dst = img.data() + (size_t)m * mb;
-        for (uint32_t r = 0; r < rows; ++r) std::memcpy(dst + 32ull * r, b + 32 + 34ull * (m * rows + r), 32);
-        const uint8_t *sc = b + 32 + 3ull * rows * 34u + 514u * m;
-        uint8_t *blk = dst + 32ull * rows;
+        uint32_t *l1 = reinterpret_cast<uint32_t *>(dst), *l2 = reinterpret_cast<uint32_t *>(dst + l1b);
+        for (uint32_t cls = 0; cls < kW4Classes; ++cls)
+            for (uint32_t pair = 0; pair < kW4Pairs; ++pair) {
+                uint32_t pm = 8, mx = 8;   // pair 36: the block start
+                if (pair + 1 < kW4Pairs) {
+                    for (mx = 0; (mx + 1) * (mx + 2) / 2 <= pair; ++mx) {}
+                    pm = pair - mx * (mx + 1) / 2;
+                }
+                for (uint32_t bucket = 0; bucket < pb; ++bucket) {
+                    const uint32_t ctx = (cls * 9u + pm) * 9u + mx, src = pb == 1 ? ctx : ctx * 5u + bucket;
+                    const uint32_t row = (cls * kW4Pairs + pair) * pb + bucket;
+                    const uint8_t *c = b + 32 + 34ull * (m * full + src);
+                    uint32_t cdf[16];
+                    for (uint32_t k = 0; k < 16; ++k) cdf[k] = rd16(c + 2 * k);
+                    l1[2 * row] = cdf[4] | cdf[8] << 16;
+                    l1[2 * row + 1] = cdf[12] | (1u << 14) << 16;
+                    for (uint32_t q = 0; q < 4; ++q) {
+                        l2[8 * row + 2 * q] = cdf[4 * q] | cdf[4 * q + 1] << 16;
+                        l2[8 * row + 2 * q + 1] = cdf[4 * q + 2] | cdf[4 * q + 3] << 16;
+                    }
+                }
+            }
+        const uint8_t *sc = b + 32 + 3ull * full * 34u + 514u * m;
+        uint8_t *blk = dst + l1b + 32ull * rows;
         for (uint32_t k = 0; k < 16; ++k) std::memcpy(blk + 2 * k, sc + 32 * k, 2);   // cdf[16k]
         std::memcpy(blk + 32, sc, 514);
     }
@@ -84,7 +106,7 @@ int register4(const uint8_t *blob, size_t, uint32_t pb, uint32_t id, int device)
     for (Model4 *m : g_m4) if (m->id == id && m->device == device) return 0;
     const std::vector<uint8_t> img = model4_image(blob, pb);
     auto *m = new Model4();
-    m->id = id; m->pb = pb; m->rows = kW4Classes * 81u * pb; m->device = device;
+    m->id = id; m->pb = pb; m->rows = w4_rows(pb); m->device = device;
     if (cudaSetDevice(device) != cudaSuccess || cudaMalloc(&m->dev, img.size()) != cudaSuccess ||
         cudaMemcpy(m->dev, img.data(), img.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
         (void)cudaGetLastError();

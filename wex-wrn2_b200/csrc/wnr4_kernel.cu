@@ -7,6 +7,9 @@
 // words base + l and base + 32 + l) by shuffle; when the read position passes base + 32 the window
 // slides with one coalesced 64-byte load, consumed steps later. A CTA holds kW4Warps tiles of one
 // matrix, with that matrix's weight rows and scale CDF staged into shared memory by one TMA bulk copy.
+// A weight symbol takes two 8-byte shared loads: the row's level-1 entry gives the quartile q from
+// three packed 16-bit comparisons, the quartile's four cumulative frequencies give the rank r in it,
+// and start and end are adjacent fields taken by one funnel shift (tables in wnr4.cuh).
 #include "wnr4.cuh"
 
 namespace wexb {
@@ -91,8 +94,9 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
     }
     if (!J.n) return;
     const W4Rec &R = recs[J.rec];
-    const uint4 *rows = reinterpret_cast<const uint4 *>(smem);
-    const uint8_t *sblock = smem + tab.rows * 32u;
+    const uint2 *level1 = reinterpret_cast<const uint2 *>(smem);
+    const uint2 *level2 = reinterpret_cast<const uint2 *>(smem + w4_l1_bytes(tab.rows));
+    const uint8_t *sblock = smem + w4_l1_bytes(tab.rows) + tab.rows * 32u;
     const uint4 *coarse = reinterpret_cast<const uint4 *>(sblock);
     const uint16_t *scdf = reinterpret_cast<const uint16_t *>(sblock + 32);
     const uint16_t *tile16 = reinterpret_cast<const uint16_t *>(J.tile);   // 2-byte aligned only
@@ -137,22 +141,29 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
             const int d = (int)scale - anchor;
             cls = (uint32_t)(min(max(d, -3), 3) + 3);
         }
-        uint32_t pm = 8, mx = 8, w[4] = {0, 0, 0, 0};
+        // the context as a row index (cls * 37 + pair) * pb + bucket; pair 36 = the block start
+        const uint32_t pb = tab.pb, cls_row = cls * kW4Pairs * pb;
+        uint32_t pair = kW4Pairs - 1u, top = 0, w[4] = {0, 0, 0, 0};
 #pragma unroll
         for (uint32_t k = 0; k < 32; ++k) {
             const bool act = active && !(tail && k >= 28);
             if (act) {
-                const uint32_t ctx = (cls * 9u + pm) * 9u + mx;
-                const uint32_t row = tab.pb == 1 ? ctx : ctx * 5u + (k + 5u <= 32u ? 0u : k - 27u);
-                const uint32_t slot = x & 0x3fffu;
-                const uint32_t y = row_count(rows[2u * row], rows[2u * row + 1u], slot) - 1u;
-                const uint16_t *cdf = reinterpret_cast<const uint16_t *>(rows + 2u * row);
-                const uint32_t start = cdf[y], next = y < 15u ? cdf[y + 1] : 16384u;
-                x = (next - start) * (x >> 14) + slot - start;
+                const uint32_t row = cls_row + pair * pb + (k + 5u <= 32u ? 0u : (pb == 1u ? 0u : k - 27u));
+                const uint2 c = level1[row];
+                const uint32_t slot = x & 0x3fffu, gs = slot * 0x10001u + 0x80008000u;
+                // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]: flag bits of packed subtractions
+                const uint32_t q = __popc(((gs - c.x) & 0x80008000u) | (((gs - c.y) >> 1) & 0x4000u));
+                const uint2 rq = level2[4u * row + q];   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
+                const uint32_t r = __popc(((gs - rq.y) & 0x80008000u) | ((gs - rq.x) >> 31));
+                const uint32_t bw = (q & 2u) ? c.y : c.x, bound = (bw >> ((q & 1u) << 4)) & 0xffffu;   // cdf[4q+4]
+                const uint32_t pr = __funnelshift_r((r & 2u) ? rq.y : rq.x, (r & 2u) ? bound : rq.y, (r & 1u) << 4);
+                const uint32_t start = pr & 0xffffu, y = 4u * q + r;
+                x = ((pr >> 16) - start) * (x >> 14) + slot - start;
                 if (cz && y == 8u) err |= kW4ErrCz;
                 w[k / 8u] |= y << (4u * (k % 8u));
-                pm = y & 7u;
-                mx = mx == 8u ? pm : max(mx, pm);
+                const uint32_t mag = y & 7u;
+                top = max(top, mag);
+                pair = ((top * top + top) >> 1) + mag;
             }
             // out of words: the structure bit alone, as the reference reports it (earlier bits dropped)
             if (!renorm(x, act && x < kW4L, ptr, win, lane)) { if (lane == 0) atomicOr(R.error, kW4Err); return; }
@@ -162,15 +173,15 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
         if (active) {
             if (tail) {
                 for (uint32_t q = 0; q < 4; ++q) {
-                    const uint32_t y = (left >> (4u * q)) & 15u, a = y & 7u;
+                    const uint32_t y = (left >> (4u * q)) & 15u;
                     if (cz && y == 8u) err |= kW4ErrCz;
-                    mx = mx == 8u ? a : max(mx, a);
+                    top = max(top, y & 7u);
                 }
                 w[3] |= left << 16;
                 x = kW4L;
             }
             hash = mm3_block(mm3_block(mm3_block(mm3_block(hash, w[0]), w[1]), w[2]), w[3]);
-            if (ceil && mx == 5u) {
+            if (ceil && top == 5u) {
                 if (!scale) err |= kW4ErrCeil;
                 else {
                     so[cell] = (uint8_t)(scale - 1u);
@@ -202,7 +213,7 @@ cudaError_t launch_wnr4(const W4Tables &tab, const W4Job *jobs, uint32_t njobs, 
     if (cudaGetDevice(&dev) != cudaSuccess) return cudaGetLastError();
     if (dev != configured_device) {
         const cudaError_t e = cudaFuncSetAttribute(wnr4_tiles, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)w4_matrix_bytes(kW4Classes * 81u * 5u));
+                                                   (int)w4_matrix_bytes(w4_rows(5)));
         if (e != cudaSuccess) return e;
         configured_device = dev;
     }
