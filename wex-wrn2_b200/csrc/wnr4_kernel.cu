@@ -143,31 +143,40 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
         }
         // the context as a row index (cls * 37 + pair) * pb + bucket; pair 36 = the block start
         const uint32_t pb = tab.pb, cls_row = cls * kW4Pairs * pb;
-        uint32_t pair = kW4Pairs - 1u, top = 0, w[4] = {0, 0, 0, 0};
+        uint32_t pair = kW4Pairs - 1u, top = 0, w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+        // four groups of 8 nibbles, one packed word each (the words rotate through w0..w3), so that only
+        // 8 copies of the step are unrolled
+#pragma unroll 1
+        for (uint32_t g8 = 0; g8 < 4; ++g8) {
+            uint32_t word = 0;
 #pragma unroll
-        for (uint32_t k = 0; k < 32; ++k) {
-            const bool act = active && !(tail && k >= 28);
-            if (act) {
-                const uint32_t row = cls_row + pair * pb + (k + 5u <= 32u ? 0u : (pb == 1u ? 0u : k - 27u));
-                const uint2 c = level1[row];
-                const uint32_t slot = x & 0x3fffu, gs = slot * 0x10001u + 0x80008000u;
-                // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]: flag bits of packed subtractions
-                const uint32_t q = __popc(((gs - c.x) & 0x80008000u) | (((gs - c.y) >> 1) & 0x4000u));
-                const uint2 rq = level2[4u * row + q];   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
-                const uint32_t r = __popc(((gs - rq.y) & 0x80008000u) | ((gs - rq.x) >> 31));
-                const uint32_t bw = (q & 2u) ? c.y : c.x, bound = (bw >> ((q & 1u) << 4)) & 0xffffu;   // cdf[4q+4]
-                const uint32_t pr = __funnelshift_r((r & 2u) ? rq.y : rq.x, (r & 2u) ? bound : rq.y, (r & 1u) << 4);
-                const uint32_t start = pr & 0xffffu, y = 4u * q + r;
-                x = ((pr >> 16) - start) * (x >> 14) + slot - start;
-                if (cz && y == 8u) err |= kW4ErrCz;
-                w[k / 8u] |= y << (4u * (k % 8u));
-                const uint32_t mag = y & 7u;
-                top = max(top, mag);
-                pair = ((top * top + top) >> 1) + mag;
+            for (uint32_t kk = 0; kk < 8; ++kk) {
+                const uint32_t k = 8u * g8 + kk;
+                const bool act = active && !(tail && k >= 28u);
+                if (act) {
+                    const uint32_t row = cls_row + pair * pb + ((k + 5u <= 32u || pb == 1u) ? 0u : k - 27u);
+                    const uint2 c = level1[row];
+                    const uint32_t slot = x & 0x3fffu, gs = slot * 0x10001u + 0x80008000u;
+                    // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]: flag bits of packed subtractions
+                    const uint32_t q = __popc(((gs - c.x) & 0x80008000u) | (((gs - c.y) >> 1) & 0x4000u));
+                    const uint2 rq = level2[4u * row + q];   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
+                    const uint32_t r = __popc(((gs - rq.y) & 0x80008000u) | ((gs - rq.x) >> 31));
+                    const uint32_t bw = (q & 2u) ? c.y : c.x, bound = (bw >> ((q & 1u) << 4)) & 0xffffu;   // cdf[4q+4]
+                    const uint32_t pr = __funnelshift_r((r & 2u) ? rq.y : rq.x, (r & 2u) ? bound : rq.y, (r & 1u) << 4);
+                    const uint32_t start = pr & 0xffffu, y = 4u * q + r;
+                    x = ((pr >> 16) - start) * (x >> 14) + slot - start;
+                    if (cz && y == 8u) err |= kW4ErrCz;
+                    word |= y << (4u * kk);
+                    const uint32_t mag = y & 7u;
+                    top = max(top, mag);
+                    pair = ((top * top + top) >> 1) + mag;
+                }
+                // out of words: the structure bit alone, as the reference reports it (earlier bits dropped)
+                if (!renorm(x, act && x < kW4L, ptr, win, lane)) { if (lane == 0) atomicOr(R.error, kW4Err); return; }
             }
-            // out of words: the structure bit alone, as the reference reports it (earlier bits dropped)
-            if (!renorm(x, act && x < kW4L, ptr, win, lane)) { if (lane == 0) atomicOr(R.error, kW4Err); return; }
+            w0 = w1; w1 = w2; w2 = w3; w3 = word;
         }
+        uint32_t w[4] = {w0, w1, w2, w3};
         const uint32_t left = x - kW4L;
         if (__any_sync(kFull, tail && (x < kW4L || left > 0xffffu))) { atomicOr(R.error, kW4Err | err); return; }
         if (active) {
