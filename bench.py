@@ -48,6 +48,9 @@ CONFIGS = {
     # whole-box streaming: 1536 large experts, each rank decodes all of its shard every step
     'box': dict(hidden=7168, ffn=2048, layers=8, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
                 lean=True, all_experts=True),
+    # WNR4 kind MX (draft codec 8) through the ABI 5: large experts, G = 32, one batch call per layer
+    'wnr4': dict(hidden=7168, ffn=2048, layers=2, experts=8, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
+                 wnr4=True),
     # containers: a WEX4 file per rank, checked and decoded by wex4_check (per-record SHA-256 against
     # the index, codec dispatch, decode); tiny = the 8 experts plus one RAW expert, mixed = one routed
     # step of large experts, 10 % uniform-random (stored RAW), 30 % WNR4 kind MX, the rest WNR3 CZ
@@ -357,12 +360,65 @@ def run_reference_container(args, cfg):
     return 0
 
 
+def run_reference_wnr4(args, cfg):
+    """The reference arm of the wnr4 config: the reference's CPU WNR4 decoder (oracle/_ref/wnr4_tools.so,
+    wnr4t_decode) on the same records, one record per host thread, all cores."""
+    import ctypes
+    import synth
+    sys.path.insert(0, os.path.join(ROOT, 'oracle'))
+    import oracle
+    W = oracle.ref_lib('wnr4_tools')
+    if W is None:
+        print(json.dumps({'impl': 'reference', 'unavailable': 'oracle/_ref/wnr4_tools.so was not built'}))
+        return 0
+    cores = os.cpu_count() or 1
+    sig = layer_sigmas(cfg)
+    owners = [(l, i) for l in range(cfg['layers']) for i in range(cfg['batch'])]
+    with ThreadPoolExecutor(cores) as pool:
+        ex = list(pool.map(lambda o: synth.Expert(cfg['hidden'], cfg['ffn'], o[0], o[1], SEED * 31 + o[0] * 4099 + o[1],
+                                                  sig[o[0]], cfg['cz'], 0, cfg['neg_zero']), owners))
+        blob4 = synth.train_model4([(e.entry, e.coded) for e in ex[:4]])
+        recs = list(pool.map(lambda k: synth.encode4(blob4, ex[k].entry, ex[k].coded, ex[k].flags, k, 32), range(len(ex))))
+    geo = (ctypes.c_uint32 * 13)(*synth.geo4(ex[0].entry))
+    raw = len(ex[0].source)
+    h = W.wnr4t_model_open(blob4, len(blob4))
+    outs = [ctypes.create_string_buffer(raw) for _ in range(cores)]
+
+    def one(i):
+        k = i % len(recs)
+        if W.wnr4t_decode(h, geo, recs[k], len(recs[k]), k, outs[i % cores], 1) != 0:
+            raise RuntimeError('reference WNR4 decoder refused a record')
+        return raw
+    times = []
+    with ThreadPoolExecutor(cores) as pool:
+        for s in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            nb = sum(pool.map(one, range(s * cores, (s + 1) * cores)))
+            if s >= args.warmup:
+                times.append((time.perf_counter() - t0, nb))
+    W.wnr4t_model_close(h)
+    total = sum(t for t, _ in times)
+    value = sum(b for _, b in times) / total / 1e9
+    print(json.dumps({
+        'impl': 'reference', 'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 4), 'unit': 'GB/s',
+        'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(1e3 * total / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'experts_per_s': round(cores * args.steps / total, 2),
+        'config': {'workload': f'wnr4: WNR4 kind-MX records of hidden {cfg["hidden"]}, FFN {cfg["ffn"]}'},
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
+                         'sample': f'{cores} records per step, one per host thread, reference wnr4t_decode'},
+        'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
+    return 0
+
+
 def run_reference(args, cfg):
     world, rank, local = int(os.environ.get('WORLD_SIZE', '1')), int(os.environ.get('RANK', '0')), 0
     if rank != 0:
         return 0
     if cfg.get('container'):
         return run_reference_container(args, cfg)
+    if cfg.get('wnr4'):
+        return run_reference_wnr4(args, cfg)
     cores = os.cpu_count() or 1
     layers = args.layers or cfg['layers']
     trace = routing_trace(cfg, args.warmup + args.steps, 0, 1, layers)
@@ -414,6 +470,110 @@ def run_reference(args, cfg):
         'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line))
+    return 0
+
+
+# ---- WNR4 kind MX through its ABI ---------------------------------------------------------------------
+def run_wnr4(args, cfg):
+    """Every step decodes all experts of the config (layers x batch), one wnr4_cuda_decode_batch call of
+    `batch` records per layer, from pinned host memory into HBM (H2D inside the timed region)."""
+    import ctypes
+    import torch
+    import synth
+    import wexcuda
+    world, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    U32, SZ, P, I = ctypes.c_uint32, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int
+    W = wexcuda.lib()
+    W.wnr4_cuda_register_model.argtypes = [P, SZ, I]
+    W.wnr4_cuda_batch_submit.argtypes = [I, P, P, P, P, U32, I, P, P, P]
+    W.wnr4_cuda_batch_wait.argtypes = [I, P]
+    sig = layer_sigmas(cfg)
+    owners = [(l, rank + world * i) for l in range(cfg['layers']) for i in range(cfg['batch'])]
+    threads = max(1, (os.cpu_count() or 8) // max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world))))
+    t0 = time.time()
+    with ThreadPoolExecutor(threads) as pool:
+        ex = list(pool.map(lambda o: synth.Expert(cfg['hidden'], cfg['ffn'], o[0], o[1], SEED * 31 + o[0] * 4099 + o[1],
+                                                  sig[o[0]], cfg['cz'], 0, cfg['neg_zero']), owners))
+        blob4 = synth.train_model4([(e.entry, e.coded) for e in ex[:4]])
+        recs = list(pool.map(lambda k: synth.encode4(blob4, ex[k].entry, ex[k].coded, ex[k].flags, k, 32), range(len(ex))))
+    log(f'[rank {rank}] {len(ex)} WNR4 records encoded in {time.time() - t0:.1f} s')
+    assert all(r is not None for r in recs)
+    mid = int.from_bytes(recs[0][4:8], 'little')
+    assert W.wnr4_cuda_register_model(blob4, len(blob4), local) == 0
+    host, at = np.empty(sum(len(r) for r in recs), np.uint8), 0
+    views = []
+    for r in recs:
+        host[at:at + len(r)] = np.frombuffer(r, np.uint8)
+        views.append(host[at:at + len(r)])
+        at += len(r)
+    assert wexcuda.host_register(host) == 0
+    raw = len(ex[0].source)
+    expected = [hashlib.sha256(e.expected).digest() for e in ex]
+    del ex
+    k = len(recs)
+    dst = torch.empty((k, raw), dtype=torch.uint8, device='cuda')
+    entry = synth.expert_entry(cfg['hidden'], cfg['ffn'])
+    soff = [int.from_bytes(entry[44 + 4 * m:48 + 4 * m], 'little') for m in range(3)]
+    woff = [int.from_bytes(entry[56 + 4 * m:60 + 4 * m], 'little') for m in range(3)]
+    B = cfg['batch']
+    geo = (U32 * 13)(*synth.geo4(entry))
+    calls = []
+    for c in range(0, k, B):
+        sel = range(c, min(k, c + B))
+        calls.append((len(sel), wexcuda._ptrs([views[i].ctypes.data for i in sel]), (SZ * len(sel))(*[len(recs[i]) for i in sel]),
+                      (U32 * len(sel))(*sel),
+                      wexcuda._ptrs([dst.data_ptr() + j * raw + soff[m] for j in sel for m in range(3)]),
+                      wexcuda._ptrs([dst.data_ptr() + j * raw + woff[m] for j in sel for m in range(3)])))
+    stream = torch.cuda.current_stream()
+
+    def step():
+        tickets = [W.wnr4_cuda_batch_submit(n, geo, rp, tp, op, mid, local, sp, wp, P(stream.cuda_stream))
+                   for n, rp, tp, op, sp, wp in calls]
+        assert all(t >= 0 for t in tickets), tickets
+        for (n, *_), t in zip(calls, tickets):
+            st = (ctypes.c_int * n)()
+            assert W.wnr4_cuda_batch_wait(t, st) == 0, list(st)
+    for _ in range(args.warmup):
+        step()
+    h2d_gbs = measure_h2d(torch)
+    clocks = Clocks(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    barrier(world)
+    clk = clocks.stop()
+    got = [hashlib.sha256(bytes(dst[j].cpu().numpy())).digest() for j in (0, k - 1)]
+    assert got == [expected[0], expected[k - 1]], 'decoded bytes differ from the source'
+    dec_all, stored_all = sum_over_ranks([k * raw * args.steps, len(host) * args.steps], world)
+    value = dec_all / (ms / 1e3) / 1e9
+    line = {
+        'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 3), 'unit': 'GB/s', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'experts_per_s': round(k * world * args.steps / (ms / 1e3), 1),
+        'config': {'workload': f'wnr4: WNR4 kind-MX records (draft codec 8, G = 32, canonical zero) of {k} experts of '
+                               f'hidden {cfg["hidden"]}, FFN {cfg["ffn"]} per rank, decoded every step by '
+                               f'wnr4_cuda_batch_submit / wait, {B} records per call, from pinned host memory',
+                   'l2': 'inputs larger than L2 (126 MB) between steps'},
+        'e2e': {'value': round(value, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': int(len(host)), 'd2h_bytes_per_step': 4 * k,
+                'roofline': {'bound': 'h2d', 'achieved': round(stored_all / (ms / 1e3) / 1e9 / world, 2),
+                             'peak': round(h2d_gbs, 2),
+                             'frac': round(stored_all / (ms / 1e3) / 1e9 / world / h2d_gbs, 4)}},
+        'clocks': clk, 'verified_records': 2,
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
     return 0
 
 
@@ -877,6 +1037,8 @@ def main():
         return run_reference(args, cfg)
     if cfg.get('container'):
         return run_container(args, cfg)
+    if cfg.get('wnr4'):
+        return run_wnr4(args, cfg)
     return run_gpu(args, cfg)
 
 
