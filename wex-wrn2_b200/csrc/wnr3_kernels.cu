@@ -209,10 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const N
             const uint2 row = l2[4u * idx + q];   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
             // r = [cdf[4q+1] <= slot] + [cdf[4q+2] <= slot] + [cdf[4q+3] <= slot]
             const uint32_t r = __popc(((gs - row.y) & 0x80008000u) | ((gs - row.x) >> 31));
-            // cdf[4q+4]: field q of cdf[4], cdf[8], cdf[12], 2^14
-            const uint32_t bw = (q & 2u) ? c.y : c.x;
-            const uint32_t bound = (bw >> ((q & 1u) << 4)) & 0xffffu;
-            // start | end << 16 = fields r, r + 1 of cdf[4q .. 4q+3], bound
+            // cdf[4q+4] in bits 0..15: field q of cdf[4], cdf[8], cdf[12], 2^14 (bytes 2q, 2q + 1)
+            const uint32_t bound = __byte_perm(c.x, c.y, 0x10u + 0x22u * q);
+            // start | end << 16 = fields r, r + 1 of cdf[4q .. 4q+3], bound (only its low half reaches pair)
             const uint32_t lo = (r & 2u) ? row.y : row.x, hi = (r & 2u) ? bound : row.y;
             const uint32_t pair = __funnelshift_r(lo, hi, (r & 1u) << 4);
             const uint32_t start = pair & 0xffffu, freq = (pair >> 16) - start;
