@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const N
             const uint32_t bound = __byte_perm(c.x, c.y, 0x10u + 0x22u * q);
             // start | end << 16 = fields r, r + 1 of cdf[4q .. 4q+3], bound (only its low half reaches pair)
             const uint32_t lo = (r & 2u) ? row.y : row.x, hi = (r & 2u) ? bound : row.y;
-            const uint32_t pair = __funnelshift_r(lo, hi, (r & 1u) << 4);
+            const uint32_t pair = __funnelshift_r(lo, hi, r << 4);   // the shift counts mod 32: 0 or 16
             const uint32_t start = pair & 0xffffu, freq = (pair >> 16) - start;
             x = freq * (x >> kPrec) + slot - start;
             const uint32_t sym = 4u * q + r;

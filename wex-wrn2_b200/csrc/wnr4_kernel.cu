@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
                     const uint2 rq = level2[4u * row + q];   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
                     const uint32_t r = __popc(((gs - rq.y) & 0x80008000u) | ((gs - rq.x) >> 31));
                     const uint32_t bound = __byte_perm(c.x, c.y, 0x10u + 0x22u * q);   // cdf[4q+4] in bits 0..15
-                    const uint32_t pr = __funnelshift_r((r & 2u) ? rq.y : rq.x, (r & 2u) ? bound : rq.y, (r & 1u) << 4);
+                    const uint32_t pr = __funnelshift_r((r & 2u) ? rq.y : rq.x, (r & 2u) ? bound : rq.y, r << 4);   // mod 32
                     const uint32_t start = pr & 0xffffu, y = 4u * q + r;
                     x = ((pr >> 16) - start) * (x >> 14) + slot - start;
                     if (cz && y == 8u) err |= kW4ErrCz;
