@@ -105,7 +105,7 @@ WEXB_API int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned
         g_na_slot[device][slot] = p.model_id;
     }
     uint8_t *const tab = base + kNaTables + slot * kNaTableStride;
-    const Nr3Tables t{tab, reinterpret_cast<const uint32_t *>(tab + kWTableBytes), tab + kWTableBytes + kSdirBytes};
+    const Nr3Tables t{tab, tab + kWTableBytes, reinterpret_cast<const uint16_t *>(tab + kWTableBytes + kSsymBytes)};
     // this call's metadata, written in full (the array keeps the previous call's bytes)
     plan_offsets(p, reinterpret_cast<uint32_t *>(g_na_host + kNaOffs));
     Nr3Task *tasks = reinterpret_cast<Nr3Task *>(g_na_host + kNaTasks);

@@ -1,6 +1,8 @@
 // Host side of the WNR2/WNR3 decoder (see nr3_host.h).
 #include "nr3_host.h"
 
+#include <cstring>
+
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -32,11 +34,11 @@ uint32_t fnv1a(const uint8_t *p, size_t n) {
     return h ? h : 1u;
 }
 
-// Table image: per matrix the two-level weight block (wnr3.cuh), then sdir [3][16384 u32], ssym [3][16384 u8].
+// Table image: per matrix the two-level weight block (wnr3.cuh), then ssym [3][16384 u8], scdf [3][528 B].
 void build_image(const uint8_t *blob, std::vector<uint8_t> &img) {
     img.assign(kTableBytes, 0);
-    uint32_t *sdir = reinterpret_cast<uint32_t *>(img.data() + kWTableBytes);
-    uint8_t *ssym = img.data() + kWTableBytes + kSdirBytes;
+    uint8_t *ssym = img.data() + kWTableBytes;
+    uint8_t *scdf = img.data() + kWTableBytes + kSsymBytes;
     for (uint32_t m = 0; m < 3; ++m) {
         uint32_t *l1 = reinterpret_cast<uint32_t *>(img.data() + (size_t)m * kWBlockBytes);
         uint32_t *l2 = reinterpret_cast<uint32_t *>(img.data() + (size_t)m * kWBlockBytes + kWL1Bytes);
@@ -64,11 +66,9 @@ void build_image(const uint8_t *blob, std::vector<uint8_t> &img) {
         const uint8_t *c = blob + 32 + 3u * kContexts * 34u + 514u * m;
         for (uint32_t s = 0; s < 256; ++s) {
             const uint32_t lo = rd16(c + 2 * s), hi = rd16(c + 2 * s + 2);
-            for (uint32_t slot = lo; slot < hi; ++slot) {
-                sdir[m * kTotal + slot] = (slot - lo) | (hi - lo) << 14;
-                ssym[m * kTotal + slot] = (uint8_t)s;
-            }
+            for (uint32_t slot = lo; slot < hi; ++slot) ssym[m * kTotal + slot] = (uint8_t)s;
         }
+        std::memcpy(scdf + (size_t)m * kScdfBytes, c, 514);
     }
 }
 Model *find_locked(uint32_t id) {
@@ -126,8 +126,8 @@ int model_tables(uint32_t id, int device, Nr3Tables *out) {
     }
     uint8_t *p = m->dev[device];
     out->wblk = p;
-    out->sdir = reinterpret_cast<const uint32_t *>(p + kWTableBytes);
-    out->ssym = p + kWTableBytes + kSdirBytes;
+    out->ssym = p + kWTableBytes;
+    out->scdf = reinterpret_cast<const uint16_t *>(p + kWTableBytes + kSsymBytes);
     return 0;
 }
 

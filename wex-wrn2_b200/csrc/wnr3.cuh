@@ -30,21 +30,21 @@ constexpr uint32_t kErrStruct = 1, kErrHash = 2, kErrCeil = 4, kErrCz = 8, kErrT
 //   level 1 [259] of 8 B   cdf[4] | cdf[8] << 16,  cdf[12] | 2^14 << 16   (picks the quartile q; its
 //                          fields are also cdf[4q + 4], the end of quartile q)
 //   level 2 [259][4] of 8 B, quartile q: cdf[4q] | cdf[4q+1] << 16,  cdf[4q+2] | cdf[4q+3] << 16
-//   sdir[m][slot]    (slot - start) | frequency << 14 of the scale symbol owning slot
-//   ssym[m][slot]    that scale symbol
+//   ssym[m][slot]    the scale symbol owning slot (16,384 B per matrix)
+//   scdf[m]          the scale CDF cdf[0..256] (u16), padded to 528 B
 struct Nr3Tables {
     const uint8_t *wblk;
-    const uint32_t *sdir;
     const uint8_t *ssym;
+    const uint16_t *scdf;
 };
 constexpr uint32_t kPairs = 37;                                        // contexts per srel
 constexpr uint32_t kWContexts = 7u * kPairs;                           // 259
 constexpr uint32_t kWL1Bytes = (kWContexts * 8u + 15u) & ~15u;         // 2,080
 constexpr uint32_t kWBlockBytes = kWL1Bytes + kWContexts * 32u;        // 10,368 per matrix
 constexpr size_t kWTableBytes = 3ull * kWBlockBytes;
-constexpr size_t kSdirBytes = 3ull * kTotal * 4u;
 constexpr size_t kSsymBytes = 3ull * kTotal;
-constexpr size_t kTableBytes = kWTableBytes + kSdirBytes + kSsymBytes;
+constexpr uint32_t kScdfBytes = 528;   // 257 u16, padded to a multiple of 16 B
+constexpr size_t kTableBytes = kWTableBytes + kSsymBytes + 3ull * kScdfBytes;
 
 // One record of a launch, in device memory.
 struct Nr3Record {
@@ -77,7 +77,7 @@ struct CommitJob {
     const uint32_t *error;
 };
 
-constexpr int kScaleThreads = 64;
+constexpr int kScaleThreads = 128;
 constexpr int kWeightThreadsMax = 256;   // weight CTAs have 128 or 256 threads (WEXB_WEIGHT_THREADS)
 
 cudaError_t launch_nr3_scales(const Nr3Record *recs, const Nr3Task *tasks, uint32_t ntasks, cudaStream_t st);

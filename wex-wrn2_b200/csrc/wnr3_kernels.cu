@@ -39,16 +39,16 @@ __global__ void __launch_bounds__(kScaleThreads) nr3_scales(const Nr3Record *__r
                                                             const Nr3Task *__restrict__ tasks) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar;
-    uint32_t *sdir = reinterpret_cast<uint32_t *>(smem);
-    uint8_t *ssym = smem + kTotal * 4u;
-    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kTotal * 5u);
+    uint8_t *ssym = smem;
+    uint16_t *scdf = reinterpret_cast<uint16_t *>(smem + kTotal);
+    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kTotal + kScdfBytes);
     const Nr3Task task = tasks[blockIdx.x];
     const Nr3Record &R = recs[task.rec];
     const uint32_t m = task.matrix;
     {
-        void *dst[2] = {sdir, ssym};
-        const void *src[2] = {R.t.sdir + (size_t)m * kTotal, R.t.ssym + (size_t)m * kTotal};
-        const uint32_t bytes[2] = {kTotal * 4u, kTotal};
+        void *dst[2] = {ssym, scdf};
+        const void *src[2] = {R.t.ssym + (size_t)m * kTotal, reinterpret_cast<const uint8_t *>(R.t.scdf) + (size_t)m * kScdfBytes};
+        const uint32_t bytes[2] = {kTotal, kScdfBytes};
         if (!stage_tables(&bar, dst, src, bytes, 2)) {
             if (threadIdx.x == 0) atomicOr(R.error, kErrTimeout);
             return;
@@ -72,9 +72,9 @@ __global__ void __launch_bounds__(kScaleThreads) nr3_scales(const Nr3Record *__r
             uint32_t word = 0;
 #pragma unroll
             for (uint32_t k = 0; k < 4; ++k) {
-                const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), e = sdir[slot];
-                word |= (uint32_t)ssym[slot] << (8u * k);
-                x = (e >> 14) * (x >> kPrec) + (e & 0x3fffu);
+                const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), y = ssym[slot], start = scdf[y];
+                word |= y << (8u * k);
+                x = (scdf[y + 1] - start) * (x >> kPrec) + slot - start;
                 x = rd.renorm(x, two);
             }
             if (nr3) h = mm3_block(h, word);
@@ -86,10 +86,10 @@ __global__ void __launch_bounds__(kScaleThreads) nr3_scales(const Nr3Record *__r
         rd.refill();
         uint32_t word = 0, held = 0;
         for (uint32_t i = full; i < count; ++i) {
-            const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), e = sdir[slot], s = ssym[slot];
+            const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), s = ssym[slot], start = scdf[s];
             out[i] = (uint8_t)s;
             word |= s << (8u * held);
-            x = (e >> 14) * (x >> kPrec) + (e & 0x3fffu);
+            x = (scdf[s + 1] - start) * (x >> kPrec) + slot - start;
             x = rd.renorm(x, two);
             if (++held == 4) { if (nr3) h = mm3_block(h, word); word = 0; held = 0; }
         }
@@ -264,7 +264,7 @@ __global__ void commit_regions(const CommitJob *__restrict__ jobs) {
     }
 }
 
-constexpr size_t scale_smem(int threads) { return kTotal * 5u + (size_t)kRingWords * 4u * threads; }
+constexpr size_t scale_smem(int threads) { return kTotal + kScdfBytes + (size_t)kRingWords * 4u * threads; }
 constexpr size_t weight_smem(int threads) { return kWBlockBytes + (size_t)(kRingWords + 1u) * 4u * threads; }
 
 }  // namespace
