@@ -101,6 +101,13 @@ __global__ void __launch_bounds__(kScaleThreads) nr3_scales(const Nr3Record *__r
     else if (x != expect) atomicOr(R.error, nr3 ? kErrHash : kErrStruct);
 }
 
+// a - b as a multiply-add on the FMA pipe (the integer ALU pipe is this kernel's limit)
+__device__ __forceinline__ uint32_t sub_fma(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(b), "r"(0xffffffffu), "r"(a));
+    return d;
+}
+
 // ---- kernel B: weight streams -----------------------------------------------------------------
 // A lane's payload ring for the weight kernel: word w of the stream (counted from the stream's
 // first word) lives in slot w % 32, slot 32 repeats slot 0, so the two words under any read
@@ -204,11 +211,11 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const N
             const uint2 c = l1[idx];
             const uint32_t slot = x & (kTotal - 1u), gs = slot * 0x10001u + 0x80008000u;
             // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]
-            const uint32_t d1 = gs - c.y;
-            const uint32_t q = __popc(((gs - c.x) & 0x80008000u) | ((d1 >> 1) & 0x4000u));
+            const uint32_t d1 = sub_fma(gs, c.y);
+            const uint32_t q = __popc((sub_fma(gs, c.x) & 0x80008000u) | ((d1 >> 1) & 0x4000u));
             const uint2 row = l2[4u * idx + q];   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
             // r = [cdf[4q+1] <= slot] + [cdf[4q+2] <= slot] + [cdf[4q+3] <= slot]
-            const uint32_t r = __popc(((gs - row.y) & 0x80008000u) | ((gs - row.x) >> 31));
+            const uint32_t r = __popc((sub_fma(gs, row.y) & 0x80008000u) | (sub_fma(gs, row.x) >> 31));
             // cdf[4q+4] in bits 0..15: field q of cdf[4], cdf[8], cdf[12], 2^14 (bytes 2q, 2q + 1)
             const uint32_t bound = __byte_perm(c.x, c.y, 0x10u + 0x22u * q);
             // start | end << 16 = fields r, r + 1 of cdf[4q .. 4q+3], bound (only its low half reaches pair)
