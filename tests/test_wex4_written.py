@@ -168,3 +168,46 @@ def test_gpu_check_decodes_codec8_on_request():
     assert L.wex4_check(bad, len(bad), 7, None) == -14
     bad = _damaged(data, 7, False)
     assert L.wex4_check(bad, len(bad), 7, None) == -3
+
+
+def test_bench_containers_are_valid_for_the_reference():
+    """The containers bench.py times (tiny-file, and a 12-record prefix of a mixed step) pass the
+    reference's validation; the tiny one decodes to the digest the bench verifies against."""
+    import os
+    import sys
+    R = ref()
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    cfg = bench.CONFIGS['tiny-file']
+    data, decoded, counts, vdata, vdigest = bench.build_container(cfg, bench.container_owners(cfg, 0, 1, 1), 4)
+    assert counts == {0: 1, 5: 8, 8: 0}
+    f = oracle.Wex4File(data)
+    assert R.wex4_validate(f.page, f.file_bytes, f.index, len(f.index)) == 0
+    d = ctypes.create_string_buffer(32)
+    assert R.wex4_check(vdata, len(vdata), 3, d) == 0 and d.raw == vdigest
+    cfg = dict(bench.CONFIGS['mixed'], hidden=1024, ffn=512)   # the mixed recipe at a small shape
+    owners = bench.container_owners(cfg, 0, 1, 2)[:12]
+    data, decoded, counts, vdata, vdigest = bench.build_container(cfg, owners, 4)
+    f = oracle.Wex4File(data)
+    assert R.wex4_validate(f.page, f.file_bytes, f.index, len(f.index)) == 0
+    assert R.wex4_check(data, len(data), 1, None) == 0
+    assert sum(counts.values()) == 12
+
+
+@pytest.mark.gpu
+def test_gpu_check_of_a_bench_mixed_container():
+    """A small-shape mixed step (RAW, WNR4 kind MX and WNR3 canonical-zero records) checked and decoded on
+    the GPU with codec 8 on: the content digest of its source slabs, and a throughput-pass check (no
+    digest) that passes too."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    L = lib()
+    cfg = dict(bench.CONFIGS['mixed'], hidden=1024, ffn=512)
+    owners = bench.container_owners(cfg, 0, 1, 3)[:12]
+    data, decoded, counts, vdata, vdigest = bench.build_container(cfg, owners, 4)
+    assert counts[0] + counts[5] + counts[8] == 12 and counts[8] > 0
+    d = ctypes.create_string_buffer(32)
+    assert L.wex4_check(vdata, len(vdata), 7, d) == 0 and d.raw == vdigest
+    assert L.wex4_check(data, len(data), 15, None) == 0
