@@ -58,6 +58,10 @@ CONFIGS = {
                       container=True, raw=(8,), wnr4_frac=0.0),
     'mixed': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
                   container=True, raw_frac=0.10, wnr4_frac=0.30),
+    # expert misses served from a container file: every step reads `misses` distinct experts of the rank's
+    # file (a seeded permutation, as bench/wex_io.c draws them) and decodes them into HBM (wexb_file_*)
+    'file': dict(hidden=2048, ffn=768, layers=8, experts=128, batch=8, cz=False, sigma=(0.01, 0.04), neg_zero=0.0,
+                 file=True, misses=256),
 }
 SEED = 20261201
 MEASURED_PEAKS = os.path.join(ROOT, 'MEASURED_PEAKS.json')
@@ -419,6 +423,8 @@ def run_reference(args, cfg):
         return run_reference_container(args, cfg)
     if cfg.get('wnr4'):
         return run_reference_wnr4(args, cfg)
+    if cfg.get('file'):
+        return run_reference_file(args, cfg)
     cores = os.cpu_count() or 1
     layers = args.layers or cfg['layers']
     trace = routing_trace(cfg, args.warmup + args.steps, 0, 1, layers)
@@ -570,6 +576,233 @@ def run_wnr4(args, cfg):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+    return 0
+
+
+# ---- expert misses from a container file (config "file") ------------------------------------------------
+def file_dir():
+    return os.environ.get('WEXB_FILE_DIR') or None
+
+
+def write_expert_file(cfg, rank, world, threads):
+    """This rank's container file: every expert of its shard (expert id mod world size) of cfg['layers']
+    layers as WNR3 records under one WNM2 model. Returns (path, owners, experts, model blob)."""
+    import tempfile
+    import wex4file
+    owners = [(l, e) for l in range(cfg['layers']) for e in range(rank, cfg['experts'], world)]
+    blob, experts = build_pool(cfg, owners, threads)
+    recs = [wex4file.expert_record(e, 0, value_exact=cfg['cz']) for e in experts]
+    data = wex4file.write(recs, [(wex4file.BLOB_WNM2, fnv1a(blob), blob)], grid=(cfg['layers'], cfg['experts']),
+                          value_exact=cfg['cz'])
+    del recs
+    fd, path = tempfile.mkstemp(prefix=f'wexb-experts-r{rank}-', suffix='.wex4', dir=file_dir())
+    with os.fdopen(fd, 'wb') as f:
+        f.write(data)
+        f.flush()
+        os.fsync(f.fileno())
+    return path, owners, experts, blob
+
+
+def file_record_offsets(path):
+    """{(layer, expert): offset} of the expert records, from the container's record table."""
+    import struct
+    with open(path, 'rb') as fh:
+        head = fh.read(4096)
+        index_offset, = struct.unpack_from('<Q', head, 32)
+        nblobs, nrecords = struct.unpack_from('<II', head, 48)
+        fh.seek(index_offset + 64 * nblobs)
+        rows = fh.read(72 * nrecords)
+    out = {}
+    for r in range(nrecords):
+        offset, stored, decoded, codec, flags, blob, owner = struct.unpack_from('<QIIHHII', rows, 72 * r)
+        if flags & 2:
+            out[(owner >> 16, owner & 0xffff)] = offset
+    return out
+
+
+def miss_keys(owners, misses, step):
+    """The experts one step reads: `misses` distinct records of the file in a seeded random order."""
+    perm = np.random.default_rng(SEED + 7919 * step).permutation(len(owners))[:misses]
+    return [owners[int(i)] for i in perm]
+
+
+def open_expert_file(wexcuda, path):
+    """(file, direct): O_DIRECT when the filesystem allows it, else through the page cache."""
+    try:
+        return wexcuda.ExpertFile(path, direct=True), True
+    except OSError as e:
+        if e.errno != 1:
+            raise
+        return wexcuda.ExpertFile(path, direct=False), False
+
+
+def run_file(args, cfg):
+    import torch
+    import wexcuda
+    world, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    threads = max(1, (os.cpu_count() or 8) // max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world))))
+    t0 = time.time()
+    path, owners, experts, _ = write_expert_file(cfg, rank, world, threads)
+    log(f'[rank {rank}] file of {len(owners)} records ({os.path.getsize(path) / 1e9:.2f} GB) written in '
+        f'{time.time() - t0:.1f} s at {path}')
+    by_owner = {(e.layer, e.index): e for e in experts}
+    raw = len(experts[0].expected)
+    N = min(cfg['misses'], len(owners))
+    steps = [miss_keys(owners, N, s) for s in range(args.warmup + args.steps)]
+    last = steps[-1]
+    expected = {k: hashlib.sha256(by_owner[k].expected).digest() for k in (last[0], last[-1])}
+    stored = [sum(len(by_owner[k].record) for k in keys) for keys in steps]
+    del experts, by_owner
+    f, direct = open_expert_file(wexcuda, path)
+    dst = torch.empty((N, raw), dtype=torch.uint8, device='cuda')
+    import synth
+    entry = synth.expert_entry(cfg['hidden'], cfg['ffn'])
+    soff = [int.from_bytes(entry[44 + 4 * m:48 + 4 * m], 'little') for m in range(3)]
+    woff = [int.from_bytes(entry[56 + 4 * m:60 + 4 * m], 'little') for m in range(3)]
+    ds = [dst.data_ptr() + j * raw + soff[m] for j in range(N) for m in range(3)]
+    dw = [dst.data_ptr() + j * raw + woff[m] for j in range(N) for m in range(3)]
+
+    def timed(fn, keys):
+        if not direct:
+            f.evict()
+        barrier(world)
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        fn(keys)
+        torch.cuda.synchronize()
+        return max_over_ranks(time.perf_counter() - t, world)
+
+    def decode(keys):
+        bad, st = f.decode(keys, local, ds, dw)
+        assert bad == 0, st
+
+    def read(keys):
+        bad, st, got = f.read(keys)
+        assert bad == 0, st
+    for s in range(args.warmup):
+        timed(read, steps[s])
+        timed(decode, steps[s])
+    h2d_gbs = measure_h2d(torch)
+    clocks = Clocks(local)
+    clocks.start()
+    t_dec = [timed(decode, steps[args.warmup + s]) for s in range(args.steps)]
+    clk = clocks.stop()
+    t_read = [timed(read, steps[args.warmup + s]) for s in range(args.steps)]
+    got = {k: hashlib.sha256(bytes(dst[j].cpu().numpy())).digest() for j, k in ((0, last[0]), (N - 1, last[-1]))}
+    assert got == expected, 'decoded bytes differ from the source'
+    dec_all, stored_all = sum_over_ranks([N * raw * args.steps, sum(stored[args.warmup:])], world)
+    sec, rsec = sum(t_dec), sum(t_read)
+    value = dec_all / sec / 1e9
+    read_gbs = stored_all / rsec / 1e9 / world
+    achieved = stored_all / sec / 1e9 / world
+    line = {
+        'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': round(value, 3), 'unit': 'GB/s', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(1e3 * sec / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'experts_per_s': round(N * world * args.steps / sec, 1),
+        'config': {'workload': f'file: expert misses from a WEX4 container file, {N} distinct WNR3 MXFP4 experts per '
+                               f'step in a seeded random order (hidden {cfg["hidden"]}, FFN {cfg["ffn"]}), of a file of '
+                               f'{len(owners)} experts per rank ({cfg["layers"]} layers, expert id mod world size), '
+                               f'read, uploaded and decoded by wexb_file_decode',
+                   'reads': 'O_DIRECT' if direct else 'page cache, evicted before every step',
+                   'readers': 8, 'placement': 'expert id mod world size',
+                   'l2': 'inputs larger than L2 (126 MB) between steps'},
+        'e2e': {'value': round(value, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': int(sum(stored[args.warmup:]) / args.steps),
+                'd2h_bytes_per_step': 4 * N, 'api': 'wexb_file_decode (file to HBM)'},
+        'roofline': {'bound': 'storage read', 'achieved': round(achieved, 3), 'peak': round(read_gbs, 3),
+                     'unit': 'GB/s (stored bytes per GPU)', 'frac': round(achieved / read_gbs, 4),
+                     'peak_source': 'measured here: the same records through wexb_file_read (reads alone, same '
+                                    'readers and ring), the slowest rank', 'h2d_gbs': round(h2d_gbs, 2)},
+        'gpu_launches': 3 * -(-N // 8), 'clocks': clk, 'verified_records': 2,
+    }
+    f.close()
+    os.remove(path)
+    if rank == 0:
+        if not args.no_cpu_baseline and world == 1:
+            line['cpu_baseline'] = reference_file_miss_rate(args, cfg, None, seconds=args.cpu_seconds)
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def reference_file_miss_rate(args, cfg, built, seconds):
+    """The reference's miss path on the host cores: each thread preads one whole record (O_DIRECT when the
+    filesystem allows it, as c/expert_store_wex.c opens its file) and decodes it with the reference's CPU
+    decoder (oracle/_ref/wex_nr3_tools.so), until `seconds` of work. built: write_expert_file's result, or
+    None to write a file of the config's first layer."""
+    sys.path.insert(0, os.path.join(ROOT, 'oracle'))
+    import ctypes
+    import mmap
+    import oracle
+    L = oracle.ref_lib('wex_nr3_tools')
+    if L is None:
+        raise RuntimeError('oracle/_ref/wex_nr3_tools.so is missing: build it with `make -C oracle ref`')
+    cores = os.cpu_count() or 1
+    own = built is None
+    if own:
+        built = write_expert_file(dict(cfg, layers=1), 0, 1, cores)
+    path, owners, experts, blob = built
+    by_owner = {(e.layer, e.index): e for e in experts}
+    offsets = file_record_offsets(path)
+    try:
+        fd, direct = os.open(path, os.O_RDONLY | os.O_DIRECT), True
+    except OSError:
+        fd, direct = os.open(path, os.O_RDONLY), False
+    largest = max(len(e.record) for e in experts)
+    bufs = [mmap.mmap(-1, largest) for _ in range(cores)]   # page-aligned, as O_DIRECT needs
+    outs = [ctypes.create_string_buffer(experts[0].raw) for _ in range(cores)]
+
+    def one(i, key):
+        e, b = by_owner[key], bufs[i % cores]
+        if os.preadv(fd, [b], offsets[key]) < len(e.record):
+            raise RuntimeError('short read')
+        rec = (ctypes.c_char * len(e.record)).from_buffer(b)
+        st = L.wex_nr3_decode(blob, e.entry, rec, e.layer, e.index, outs[i % cores])
+        del rec
+        if st != 0:
+            raise RuntimeError('reference decoder refused a record')
+        return e.raw
+    t0, n, nbytes, s = time.perf_counter(), 0, 0, 0
+    with ThreadPoolExecutor(cores) as pool:
+        while time.perf_counter() - t0 < seconds:
+            keys = miss_keys(owners, cores, s)
+            s += 1
+            nbytes += sum(pool.map(one, range(len(keys)), keys))
+            n += len(keys)
+    dt = time.perf_counter() - t0
+    os.close(fd)
+    if own:
+        os.remove(path)
+    return {'value': round(nbytes / dt / 1e9, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
+            'sample': f'{n} expert misses ({nbytes / 1e9:.2f} GB decoded) in {dt:.1f} s: one pread of the whole '
+                      f'record ({"O_DIRECT" if direct else "page cache"}) then the reference wex_nr2_decode, one '
+                      f'record per host thread'}
+
+
+def run_reference_file(args, cfg):
+    """The reference arm of the file config: rank 0 writes the same file and serves each step's misses with
+    the reference's path (pread, then its CPU decoder), on all host cores; each step a bounded sample."""
+    cores = os.cpu_count() or 1
+    built = write_expert_file(cfg, 0, 1, cores)
+    N = min(cfg['misses'], len(built[1]))
+    raw = built[2][0].raw
+    rate = reference_file_miss_rate(args, cfg, built, seconds=args.cpu_seconds)
+    os.remove(built[0])
+    value = rate['value']
+    line = {
+        'impl': 'reference', 'metric': 'decoded MXFP4 expert GB/s into HBM', 'value': value, 'unit': 'GB/s',
+        'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(1e3 * N * raw / (value * 1e9), 3),
+        'experts_per_s': round(value * 1e9 / raw, 2), 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'config': {'workload': f'file: expert misses from a WEX4 container file, {N} distinct WNR3 MXFP4 experts per '
+                               f'step (hidden {cfg["hidden"]}, FFN {cfg["ffn"]})'},
+        'cpu_baseline': rate,
+        'e2e': {'value': value, 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line))
     return 0
 
 
@@ -1040,6 +1273,8 @@ def main():
         return run_container(args, cfg)
     if cfg.get('wnr4'):
         return run_wnr4(args, cfg)
+    if cfg.get('file'):
+        return run_file(args, cfg)
     return run_gpu(args, cfg)
 
 

@@ -76,6 +76,43 @@ int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned char *re
  * at scale 0, 8 canonical zero, 16 bounded wait expired); 0 if none failed. */
 unsigned int wexb_last_error_bits(void);
 
+/* Expert records read from a WEX4 container file: the step before the upload. The reference's expert
+ * store reads each record with one pread (O_DIRECT where it can) into a pageable slab and decodes it
+ * there (c/expert_store_wex.c:92-121, :305-337; its read paths are timed by bench/wex_io.c). Here the
+ * reads run on a pool of reader threads, in page-aligned pieces of at most 2 MiB, into a ring of
+ * page-locked buffers of 8 records each; each batch is uploaded and decoded (wexb_batch_submit) while
+ * the next ones are read. A WexbFile serves one call at a time. */
+typedef struct WexbFile WexbFile;
+#define WEXB_FILE_DIRECT 1u   /* open with O_DIRECT: reads bypass the page cache */
+
+/* Opens `path`: reads and validates the header page and the index (the WEX4 rules of wex4_validate),
+ * reads every WNM2 model blob, checks it against its SHA-256 and registers it (wex_cuda_register_model).
+ * readers: reader threads, 0 = 8, at most 64. Returns 0 and *out; -1 for bad arguments or a container
+ * that fails validation; 1 when the file cannot be opened or read (with WEXB_FILE_DIRECT: also when
+ * the filesystem refuses O_DIRECT) or memory runs out. */
+int wexb_file_open(const char *path, unsigned int flags, int readers, WexbFile **out);
+/* The expert grid of the header, the number of expert records, the largest stored record (page-aligned). */
+int wexb_file_info(const WexbFile *f, unsigned int *layers, unsigned int *experts, unsigned int *records,
+                   unsigned long long *max_stored);
+/* Drops the file's pages from the page cache (POSIX_FADV_DONTNEED): 0, or 1 if refused. */
+int wexb_file_evict(WexbFile *f);
+/* Reads the stored records of experts (layer[i], expert[i]) through the ring and discards them: the
+ * read stage alone. check != 0: each record's SHA-256 is checked against the index on the host.
+ * status[i]: 0 read, -1 no such expert or (check) a SHA-256 mismatch, 1 the read failed. *bytes (may
+ * be NULL): stored bytes read. Returns the number of non-zero statuses, -1 for bad arguments. */
+int wexb_file_read(WexbFile *f, int n, const unsigned int *layer, const unsigned int *expert, int check,
+                   int *status, unsigned long long *bytes);
+/* Reads, uploads and decodes experts (layer[i], expert[i]) into device buffers, as
+ * wex_cuda_decode_batch_to_device does from host memory: dst_scale[3i + m] and dst_weight[3i + m] for
+ * matrix m, written only when status[i] is 0. WNR3 records are decoded on `device`; RAW records are
+ * copied region by region. status[i]: 0 ok; -1 no such expert, or a record that fails its checks (the
+ * record header against the index, the decode's own checks); 1 unavailable (read failed, model not
+ * registered, CUDA error: the caller may try again). Returns the number of non-zero statuses, -1 for
+ * bad arguments. */
+int wexb_file_decode(WexbFile *f, int device, int n, const unsigned int *layer, const unsigned int *expert,
+                     unsigned char *const *dst_scale, unsigned char *const *dst_weight, int *status);
+void wexb_file_close(WexbFile *f);
+
 #ifdef __cplusplus
 }
 #endif

@@ -388,6 +388,23 @@ WEXB_API int wexb_batch_wait(int ticket, int *status) {
     return bad;
 }
 
+namespace wexb {
+bool batch_uploads_wait(int t) {
+    cudaEvent_t e = nullptr;
+    int device = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_calls_mu);
+        const Call *c = nullptr;
+        for (const auto &q : g_calls) if (q.first == t) { c = q.second; break; }
+        if (!c) return false;
+        if (!c->w) return true;   // nothing was queued
+        e = c->w->uploads_done; device = c->device;
+    }
+    if (cudaSetDevice(device) != cudaSuccess || cudaEventSynchronize(e) != cudaSuccess) { (void)cudaGetLastError(); return false; }
+    return true;
+}
+}  // namespace wexb
+
 // ---- resident records --------------------------------------------------------------------------
 struct WexbResident {
     int device = -1;

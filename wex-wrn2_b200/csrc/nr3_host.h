@@ -60,10 +60,15 @@ void plan_descriptor(const Plan &p, const Nr3Tables &t, const uint8_t *drec, con
 // `wthreads` streams.
 void plan_tasks(const Plan &p, uint32_t rec, int wthreads, std::vector<Nr3Task> &stasks, std::vector<Nr3Task> &wtasks);
 
-// Weight CTA size: WEXB_WEIGHT_THREADS (32..256, multiple of 32), default 128.
+// Weight CTA size: WEXB_WEIGHT_THREADS (128 or 256), default 256.
 int weight_threads();
 // Reports an integrity failure once per process (c/tools/wex_cuda_bridge.cu:117-122).
 void report_error_bits(uint32_t bits);
 uint32_t last_error_bits();
+
+// Queued batches (helper_abi.cpp): waits until the host records of ticket `t` (wexb_batch_submit) have
+// been copied to the device, so their host memory may be reused before the wait for the decode. False
+// for an unknown ticket or a CUDA error.
+bool batch_uploads_wait(int t);
 
 }  // namespace wexb

@@ -15,6 +15,7 @@
 #include "container.cuh"
 #include "nr3_host.h"
 #include "sha256.cuh"
+#include "wex4_index.h"
 #include "wex4_tools.h"
 #include "wbp1_host.h"
 #include "wnr4_host.h"
@@ -642,6 +643,47 @@ int current_device() {
 }
 
 }  // namespace
+
+// ---- the expert records of an index, for file readers (wex4_index.h) --------------------------------
+int file_header(const uint8_t *page, uint64_t file_bytes, FileIndex *out) {
+    Header h;
+    if (!out) return E_ARG;
+    const int st = parse_header(page, file_bytes, &h);
+    if (st) return st;
+    out->file_bytes = file_bytes; out->index_offset = h.index_offset; out->index_len = page_align(h.index_bytes);
+    out->layers = h.layers; out->experts = h.experts;
+    return OK;
+}
+
+int file_index(const uint8_t *page, const uint8_t *index, FileIndex *out) {
+    View v;
+    if (!out) return E_ARG;
+    int st = view_of(page, out->file_bytes, index, (size_t)out->index_len, &v);
+    if (st) return st;
+    out->records.clear(); out->models.clear();
+    for (uint32_t i = 0; i < v.h.blobs; ++i) {
+        const Blob b = v.blob(i);
+        if (b.kind != kBlobWnm2) continue;
+        FileModel m{b.offset, b.bytes, b.id, {}};
+        std::memcpy(m.sha, b.sha, 32);
+        out->models.push_back(m);
+    }
+    for (uint32_t r = 0; r < v.h.records; ++r) {
+        const Record rec = v.record(r);
+        if (!(rec.flags & kRecExpert)) continue;
+        FileExpert f{};
+        if ((st = expert_entry(v, r, &f.entry)) != OK) return st;
+        if (rec.codec != kCodecRaw && rec.codec != kCodecWnr3) return E_UNSUPPORTED;
+        f.owner = rec.owner; f.codec = rec.codec; f.stored = rec.stored; f.value_exact = (rec.flags & kRecValueExact) != 0;
+        f.model = rec.codec == kCodecWnr3 ? v.blob(rec.blob - 1).id : 0;
+        std::memcpy(f.sha, rec.sha, 32);
+        out->records.push_back(f);
+    }
+    return OK;
+}
+
+void host_sha256(const uint8_t *p, size_t n, uint8_t out[32]) { sha256(p, n, out); }
+
 }  // namespace wexb
 
 using namespace wexb;
@@ -694,7 +736,7 @@ WEXB_API int wex4_decode_record_buf(const unsigned char *page, uint64_t file_byt
     Job &j = jobs[0];
     j.r = r; j.rec = rec; j.stored = stored;
     j.expect_sha = check_sha ? rec.sha : nullptr;
-    // WBP1 (codec 6) is not built here; codec 8 and unknown codecs are unsupported, as in the reference
+    // codec 8 and unknown codecs are unsupported, as in the reference
     if (rec.codec == kCodecWnr3) j.pre = prepare_wnr3(v, j, model_id, device);
     else if (rec.codec == kCodecWbp1) j.pre = prepare_wbp1(j, device);
     else if (rec.codec != kCodecRaw) j.pre = E_UNSUPPORTED;

@@ -1,6 +1,6 @@
 """ctypes binding of libwexb200.so: the CUDA helper ABI (include/wex_cuda_helper.h), the engine API
 (include/wex_decode.h), the WEX4 tools ABI (include/wex4_tools.h), the WNR4 ABI (include/wnr4_cuda.h)
-and the resident-record additions (include/wexb200.h).
+and the B200 additions (include/wexb200.h: queued batches, resident records, file reads).
 
 Device buffers are plain integers (device pointers: torch tensors' data_ptr() work, any runtime of
 the process shares the device's primary context). Host buffers are numpy uint8 arrays or bytes.
@@ -52,6 +52,12 @@ def lib():
         L.wexb_resident_profile.argtypes = [P, I]
         L.wexb_resident_kernel_ms.argtypes = [P, P]
         L.wexb_resident_destroy.argtypes = [P]; L.wexb_resident_destroy.restype = None
+        L.wexb_file_open.argtypes = [ctypes.c_char_p, ctypes.c_uint, I, P]
+        L.wexb_file_info.argtypes = [P, P, P, P, P]
+        L.wexb_file_evict.argtypes = [P]
+        L.wexb_file_read.argtypes = [P, I, P, P, I, P, P]
+        L.wexb_file_decode.argtypes = [P, I, I, P, P, P, P, P]
+        L.wexb_file_close.argtypes = [P]; L.wexb_file_close.restype = None
         _lib = L
     return _lib
 
@@ -197,6 +203,63 @@ class Resident:
         if self.handle:
             lib().wexb_resident_destroy(self.handle)
             self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+FILE_DIRECT = 1
+
+
+class ExpertFile:
+    """A WEX4 container file opened for expert reads (wexb_file_*): records read by a pool of reader
+    threads into page-locked buffers, then uploaded and decoded batch by batch."""
+
+    def __init__(self, path, direct=False, readers=0):
+        h = ctypes.c_void_p()
+        rc = lib().wexb_file_open(os.fsencode(path), FILE_DIRECT if direct else 0, readers, ctypes.byref(h))
+        if rc:
+            raise OSError(rc, f'wexb_file_open: {rc}')
+        self._h = h
+
+    def info(self):
+        """(layers, experts, expert records, largest stored record)."""
+        v = [ctypes.c_uint(), ctypes.c_uint(), ctypes.c_uint(), ctypes.c_ulonglong()]
+        lib().wexb_file_info(self._h, *[ctypes.byref(x) for x in v])
+        return tuple(x.value for x in v)
+
+    def evict(self):
+        return lib().wexb_file_evict(self._h)
+
+    @staticmethod
+    def _keys(keys):
+        n = len(keys)
+        lay = (ctypes.c_uint * max(n, 1))(*[k[0] for k in keys])
+        exp = (ctypes.c_uint * max(n, 1))(*[k[1] for k in keys])
+        return n, lay, exp
+
+    def read(self, keys, check=False):
+        """Read stage only. keys: (layer, expert) pairs. (failures, statuses, stored bytes)."""
+        n, lay, exp = self._keys(keys)
+        status = (ctypes.c_int * max(n, 1))()
+        got = ctypes.c_ulonglong()
+        bad = lib().wexb_file_read(self._h, n, lay, exp, 1 if check else 0, status, ctypes.byref(got))
+        return bad, list(status)[:n], got.value
+
+    def decode(self, keys, device, dst_scale, dst_weight):
+        """keys: (layer, expert) pairs; dst_scale / dst_weight: 3 * n device pointers. (failures, statuses)."""
+        n, lay, exp = self._keys(keys)
+        status = (ctypes.c_int * max(n, 1))()
+        bad = lib().wexb_file_decode(self._h, device, n, lay, exp, _ptrs(dst_scale), _ptrs(dst_weight), status)
+        return bad, list(status)[:n]
+
+    def close(self):
+        if self._h:
+            lib().wexb_file_close(self._h)
+            self._h = None
 
     def __del__(self):
         try:
