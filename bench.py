@@ -62,6 +62,9 @@ CONFIGS = {
     # file (a seeded permutation, as bench/wex_io.c draws them) and decodes them into HBM (wexb_file_*)
     'file': dict(hidden=2048, ffn=768, layers=8, experts=128, batch=8, cz=False, sigma=(0.01, 0.04), neg_zero=0.0,
                  file=True, misses=256),
+    # the writer side: 64 coded mid experts counted (model training) and encoded as WNR3 records per step
+    'encode': dict(hidden=2048, ffn=768, layers=8, experts=8, batch=64, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
+                   encode=True),
 }
 SEED = 20261201
 MEASURED_PEAKS = os.path.join(ROOT, 'MEASURED_PEAKS.json')
@@ -425,6 +428,8 @@ def run_reference(args, cfg):
         return run_reference_wnr4(args, cfg)
     if cfg.get('file'):
         return run_reference_file(args, cfg)
+    if cfg.get('encode'):
+        return run_reference_encode(args, cfg)
     cores = os.cpu_count() or 1
     layers = args.layers or cfg['layers']
     trace = routing_trace(cfg, args.warmup + args.steps, 0, 1, layers)
@@ -799,6 +804,147 @@ def run_reference_file(args, cfg):
         'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
         'config': {'workload': f'file: expert misses from a WEX4 container file, {N} distinct WNR3 MXFP4 experts per '
                                f'step (hidden {cfg["hidden"]}, FFN {cfg["ffn"]})'},
+        'cpu_baseline': rate,
+        'e2e': {'value': value, 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ---- the writer side (config "encode") ---------------------------------------------------------------
+def encode_pool(cfg, threads):
+    """The coded experts of the encode config (layers x experts, one sigma per layer) and the model
+    trained on all of them by the writer tools."""
+    import synth
+    sig = layer_sigmas(cfg)
+    owners = [(l, e) for l in range(cfg['layers']) for e in range(cfg['experts'])]
+    with ThreadPoolExecutor(threads) as pool:
+        ex = list(pool.map(lambda o: synth.Expert(cfg['hidden'], cfg['ffn'], o[0], o[1], SEED * 17 + o[0] * 4099 + o[1],
+                                                  sig[o[0]], cfg['cz'], 0, cfg['neg_zero']), owners))
+    blob = synth.train_model([(e.entry, e.coded) for e in ex])
+    return ex, blob
+
+
+def run_encode(args, cfg):
+    """Each step counts the training symbols of the step's experts (wexb_count_batch) and encodes them as
+    WNR3 records (wexb_encode_batch, chunks 2048:512), from host memory and back: the writer's work for
+    one container of `batch` experts."""
+    import torch
+    import synth
+    import wexcuda
+    world, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    threads = max(1, (os.cpu_count() or 8) // max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world))))
+    t0 = time.time()
+    ex, blob = encode_pool(cfg, threads)
+    log(f'[rank {rank}] {len(ex)} coded experts in {time.time() - t0:.1f} s')
+    # inputs and outputs in page-locked host memory, as a writer would stage them
+    size = len(ex[0].coded)
+    host_in = np.empty(len(ex) * size, np.uint8)
+    host_out = np.empty(len(ex) * size, np.uint8)   # a record is smaller than its slab or stored RAW
+    for i, e in enumerate(ex):
+        host_in[i * size:(i + 1) * size] = np.frombuffer(e.coded, np.uint8)
+    assert wexcuda.host_register(host_in) == 0 and wexcuda.host_register(host_out) == 0
+    coded = [host_in[i * size:(i + 1) * size] for i in range(len(ex))]
+    outs = [host_out[i * size:(i + 1) * size] for i in range(len(ex))]
+    entries, flags, owners = [e.entry for e in ex], [e.flags for e in ex], [e.owner for e in ex]
+    src = len(host_in)
+    check = [synth.encode(blob, ex[i].entry, ex[i].coded, ex[i].flags, ex[i].owner)[1] for i in (0, len(ex) - 1)]
+
+    def step():
+        st, wc, sc = wexcuda.count_batch(entries, coded, True, local)
+        assert st == [0] * len(ex)
+        res = wexcuda.encode_batch(blob, entries, coded, flags, owners, True, 2048, 512, local, outs=outs)
+        assert all(r[0] in (0, 1) for r in res)
+        return res
+    for _ in range(args.warmup):
+        step()
+    clocks = Clocks(local)
+    clocks.start()
+    times = []
+    for _ in range(args.steps):
+        barrier(world)
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        res = step()
+        torch.cuda.synchronize()
+        times.append(max_over_ranks(time.perf_counter() - t, world))
+    clk = clocks.stop()
+    got = [outs[i][:res[i][3]].tobytes() for i in (0, len(ex) - 1)]
+    assert got == check, 'GPU records differ from the CPU encoder'
+    out_bytes = sum(r[3] for r in res if r[0] == 0)
+    sec = sum(times)
+    value = src * world * args.steps / sec / 1e9
+    line = {
+        'metric': 'coded MXFP4 expert GB/s counted and encoded into WNR3 records', 'value': round(value, 3),
+        'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': round(1e3 * sec / args.steps, 3), 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'config': {'workload': f'encode: {len(ex)} coded MXFP4 experts per rank (hidden {cfg["hidden"]}, FFN '
+                               f'{cfg["ffn"]}, canonical zero), training counts then WNR3 records (chunks 2048:512) '
+                               f'under one WNM2 model, from host memory and back',
+                   'l2': 'inputs larger than L2 (126 MB) between steps'},
+        'e2e': {'value': round(value, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': 2 * src, 'd2h_bytes_per_step': out_bytes,
+                'api': 'wexb_count_batch + wexb_encode_batch'},
+        'gpu_launches': 1 + 3, 'clocks': clk, 'verified_records': 2,
+    }
+    if rank == 0:
+        if not args.no_cpu_baseline and world == 1:
+            line['cpu_baseline'] = reference_encode_rate(ex, blob, args.cpu_seconds)
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def reference_encode_rate(ex, blob, seconds):
+    """The reference's writer on the host cores: its counts (wex_nr3_count_expert) and its encoder
+    (wex_nr3_encode_record) from oracle/_ref/wex_nr3_tools.so, one expert per thread, until `seconds`."""
+    sys.path.insert(0, os.path.join(ROOT, 'oracle'))
+    import ctypes
+    import oracle
+    L = oracle.ref_lib('wex_nr3_tools')
+    if L is None:
+        raise RuntimeError('oracle/_ref/wex_nr3_tools.so is missing: build it with `make -C oracle ref`')
+    cores = os.cpu_count() or 1
+    cap = 4 * len(ex[0].coded) + 65536
+    outs = [ctypes.create_string_buffer(cap) for _ in range(cores)]
+
+    def one(i):
+        e = ex[i % len(ex)]
+        wc = np.zeros(3 * 567 * 16, np.uint64)
+        sc = np.zeros(3 * 256, np.uint64)
+        if L.wex_nr3_count_expert(e.entry, e.coded, wc.ctypes.data, sc.ctypes.data) != 0:
+            raise RuntimeError('reference counts refused an expert')
+        used, total = ctypes.c_size_t(), ctypes.c_size_t()
+        if L.wex_nr3_encode_record(blob, e.entry, e.coded, e.flags, e.owner, 2048, 512, outs[i % cores], cap,
+                                   ctypes.byref(used), ctypes.byref(total)) < 0:
+            raise RuntimeError('reference encoder refused an expert')
+        return len(e.coded)
+    t0, n, nbytes = time.perf_counter(), 0, 0
+    with ThreadPoolExecutor(cores) as pool:
+        while time.perf_counter() - t0 < seconds:
+            nbytes += sum(pool.map(one, range(n, n + cores)))
+            n += cores
+    dt = time.perf_counter() - t0
+    return {'value': round(nbytes / dt / 1e9, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
+            'sample': f'{n} experts counted and encoded in {dt:.1f} s, one expert per host thread (reference '
+                      f'wex_nr3_count_expert + wex_nr3_encode_record)'}
+
+
+def run_reference_encode(args, cfg):
+    ex, blob = encode_pool(cfg, os.cpu_count() or 1)
+    rate = reference_encode_rate(ex, blob, args.cpu_seconds)
+    value = rate['value']
+    src = len(ex[0].coded)
+    line = {
+        'impl': 'reference', 'metric': 'coded MXFP4 expert GB/s counted and encoded into WNR3 records', 'value': value,
+        'unit': 'GB/s', 'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': round(1e3 * src * len(ex) / (value * 1e9), 3), 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'u8', 'data': 'synthetic',
+        'config': {'workload': f'encode: {len(ex)} coded MXFP4 experts (hidden {cfg["hidden"]}, FFN {cfg["ffn"]}, '
+                               f'canonical zero), training counts then WNR3 records (chunks 2048:512)'},
         'cpu_baseline': rate,
         'e2e': {'value': value, 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
@@ -1275,6 +1421,8 @@ def main():
         return run_wnr4(args, cfg)
     if cfg.get('file'):
         return run_file(args, cfg)
+    if cfg.get('encode'):
+        return run_encode(args, cfg)
     return run_gpu(args, cfg)
 
 

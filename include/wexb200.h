@@ -113,6 +113,30 @@ int wexb_file_decode(WexbFile *f, int device, int n, const unsigned int *layer, 
                      unsigned char *const *dst_scale, unsigned char *const *dst_weight, int *status);
 void wexb_file_close(WexbFile *f);
 
+/* The writer side on the GPU. The reference writes records on the CPU, one at a time
+ * (c/tools/wex_nr3_tools.c:87-120 -> wex_nr3_encode, c/wex_neural_rans.h:615-749), after counting
+ * its training experts (c/wex_neural_rans.h:579-613). These run every stream of every record of a call
+ * at once and give the same bytes.
+ *
+ * Encodes n coded experts (the canonical-zero / ceil-form domain: canonical slab layout of entries[i],
+ * in host memory) as WNR3 records (nr3 = 1; flags[i] = the record flags, owners[i] = layer << 16 |
+ * expert) or WNR2 records (nr3 = 0; flags and owners 0) with the chunk pair wchunk:schunk under the
+ * WNM2 model `blob`. status[i]: 0 encoded (out[i] holds total[i] bytes: used[i] bytes of record, then
+ * zero padding to 4096); 1 the record would not be smaller than the 4096-aligned raw slab (the writer
+ * stores the expert RAW; out[i] untouched, used / total still given); -1 invalid (entry layout, chunk
+ * sizes, flags, a -0 nibble in a canonical-zero record, a record larger than cap[i]); -2 CUDA
+ * unavailable. Returns the number of non-zero statuses, -1 for bad arguments. */
+int wexb_encode_batch(int n, const WexEntry *const *entries, const unsigned char *const *coded,
+                      const unsigned int *flags, const unsigned int *owners, int nr3, unsigned int wchunk,
+                      unsigned int schunk, const unsigned char *blob, size_t blob_bytes, int device,
+                      unsigned char *const *out, const size_t *cap, size_t *used, size_t *total, int *status);
+/* Adds the training counts of n coded experts to wc[3][567][16] (weight symbols per matrix and
+ * context) and sc[3][256] (scale values per matrix), contexts taken against the rule-g anchors (nr3 =
+ * 1) or the lower medians (nr3 = 0). status[i]: 0 counted, -1 invalid entry, -2 CUDA unavailable (then
+ * nothing is added). Returns the number of non-zero statuses, -1 for bad arguments. */
+int wexb_count_batch(int n, const WexEntry *const *entries, const unsigned char *const *coded, int nr3, int device,
+                     unsigned long long *wc, unsigned long long *sc, int *status);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,8 @@ def lib():
         L.wexb_file_read.argtypes = [P, I, P, P, I, P, P]
         L.wexb_file_decode.argtypes = [P, I, I, P, P, P, P, P]
         L.wexb_file_close.argtypes = [P]; L.wexb_file_close.restype = None
+        L.wexb_encode_batch.argtypes = [I, P, P, P, P, I, ctypes.c_uint, ctypes.c_uint, P, SZ, I, P, P, P, P, P]
+        L.wexb_count_batch.argtypes = [I, P, P, I, I, P, P, P]
         _lib = L
     return _lib
 
@@ -266,3 +268,38 @@ class ExpertFile:
             self.close()
         except Exception:
             pass
+
+
+def encode_batch(blob, entries, coded, flags, owners, nr3=True, wchunk=2048, schunk=512, device=0, caps=None,
+                 outs=None):
+    """Records encoded on the GPU (wexb_encode_batch): a list of (status, record, used, total); status 0
+    encoded, 1 store RAW, -1 invalid, -2 CUDA unavailable. outs: writable host buffers (numpy uint8) to
+    encode into, whose sizes are the caps; then record is None and the caller reads outs[i][:total]."""
+    n = len(entries)
+    ep, keep_e = _entries(entries)
+    srcs = [_buf(c) for c in coded]
+    given = outs is not None
+    if not given:
+        outs = [np.empty(c, np.uint8) for c in (caps or [4 * len(c) + 65536 for c in coded])]
+    dsts = [_buf(o) for o in outs]
+    U = ctypes.c_uint * max(n, 1)
+    used, total = (SZ * max(n, 1))(), (SZ * max(n, 1))()
+    status = (ctypes.c_int * max(n, 1))()
+    b = bytes(blob)
+    lib().wexb_encode_batch(n, ep, _ptrs([x[0] for x in srcs]), U(*flags), U(*owners), 1 if nr3 else 0, wchunk, schunk,
+                            b, len(b), device, _ptrs([d[0] for d in dsts]), (SZ * max(n, 1))(*[len(o) for o in outs]),
+                            used, total, status)
+    return [(status[i], None if given or status[i] else outs[i][:total[i]].tobytes(), used[i], total[i])
+            for i in range(n)]
+
+
+def count_batch(entries, coded, nr3=True, device=0):
+    """(statuses, wc, sc): training counts on the GPU (wexb_count_batch), numpy uint64 [3*567*16], [3*256]."""
+    n = len(entries)
+    ep, keep_e = _entries(entries)
+    srcs = [_buf(c) for c in coded]
+    wc, sc = np.zeros(3 * 567 * 16, np.uint64), np.zeros(3 * 256, np.uint64)
+    status = (ctypes.c_int * max(n, 1))()
+    lib().wexb_count_batch(n, ep, _ptrs([x[0] for x in srcs]), 1 if nr3 else 0, device, wc.ctypes.data, sc.ctypes.data,
+                           status)
+    return list(status)[:n], wc, sc
