@@ -886,7 +886,7 @@ def run_encode(args, cfg):
                    'l2': 'inputs larger than L2 (126 MB) between steps'},
         'e2e': {'value': round(value, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': 2 * src, 'd2h_bytes_per_step': out_bytes,
                 'api': 'wexb_count_batch + wexb_encode_batch'},
-        'gpu_launches': 1 + 3, 'clocks': clk, 'verified_records': 2,
+        'gpu_launches': 2 + 4, 'clocks': clk, 'verified_records': 2,
     }
     if rank == 0:
         if not args.no_cpu_baseline and world == 1:
