@@ -1119,15 +1119,21 @@ def measure_h2d(torch, mib=256, reps=5):
     return best
 
 
-def profile_traffic_per_record(config):
-    """DRAM bytes per record of the weight kernel from its committed ncu summary, if there is one."""
+def profile_value(config, key):
+    """A figure of the weight kernel's committed ncu summary (a `key: value` line), if there is one."""
     path = os.path.join(ROOT, 'profiles', f'nr3_weights_{config}.md')
     if not os.path.exists(path):
         return None
     for line in open(path):
-        if line.startswith('traffic_bytes_per_record:'):
-            return int(line.split(':')[1])
+        if line.startswith(key + ':'):
+            return float(line.split(':')[1])
     return None
+
+
+def profile_traffic_per_record(config):
+    """DRAM bytes per record of the weight kernel from its committed ncu summary, if there is one."""
+    v = profile_value(config, 'traffic_bytes_per_record')
+    return int(v) if v else None
 
 
 def config_desc(args, cfg, records):
@@ -1324,6 +1330,20 @@ def run_gpu(args, cfg):
     hbm_peak = peaks.get('hbm_gbs', 6650.0)
     achieved = alg / (wk_ms / 1e3) / 1e9 if wk_ms else None
     traffic_rec = profile_traffic_per_record(args.config)
+    # the kernel's compute roofline: warp-instructions issued (the ncu count per warp and symbol of the
+    # committed profile x the launch's weight symbols / 32) over the event-timed duration, against the
+    # issue rate of every scheduler (4 per SM, one warp-instruction a cycle) at the sampled SM clock
+    ipws = profile_value(args.config, 'warp_instructions_per_warp_symbol')
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    issue = None
+    if ipws and wk_ms and clk.get('sm_mhz'):
+        winstr = 2 * wbytes / args.steps / 32 * ipws
+        peak_issue = sms * 4 * clk['sm_mhz'] * 1e6
+        issue = {'bound': 'warp-instruction issue', 'achieved': round(winstr / (wk_ms / 1e3) / 1e12, 4),
+                 'peak': round(peak_issue / 1e12, 4), 'unit': 'T warp-instructions/s',
+                 'frac': round(winstr / (wk_ms / 1e3) / peak_issue, 4),
+                 'source': f'{ipws} warp-instructions per warp-symbol (ncu, committed profile) x weight symbols '
+                           f'/ 32; {sms} SMs x 4 schedulers at the median sampled SM clock'}
     h2d_per_step = stored // args.steps + 0
     # rooflines of the two paths (per GPU): the resident decode against HBM (records read, slabs written
     # by the decoder and again by the commit copy), the end-to-end path against the measured H2D link
@@ -1364,7 +1384,8 @@ def run_gpu(args, cfg):
                                        'launch, scaled to this launch' if traffic_rec else None,
                      'kernel_ms': round(wk_ms, 4) if wk_ms else None,
                      'alg_bytes_per_launch': int(alg),
-                     'step_kernel_ms': [round(statistics.mean(m[i] for m in kernel_ms if m), 4) for i in range(3)]},
+                     'step_kernel_ms': [round(statistics.mean(m[i] for m in kernel_ms if m), 4) for i in range(3)],
+                     'issue': issue},
         'gpu_launches': launches,
         'clocks': clk,
         'verified_records': verified,
