@@ -148,20 +148,17 @@ struct WeightReader {
         cp_commit();
         cp_wait<1>();
     }
-    // The next two payload bytes as a big-endian pair in bits 16..31. Past the stream's end the
-    // ring holds stale words: consuming them is caught by the final position check.
-    __device__ __forceinline__ uint32_t peek() const {
+    // The next four payload bytes, big-endian: enough for two symbols, each of which takes at most two.
+    // Past the stream's end the ring holds stale words: consuming them is caught by the final position
+    // check.
+    __device__ __forceinline__ uint32_t peek4() const {
         const uint32_t *p = ring + ((bit >> 5) & 31u) * kThreads;
-        return __byte_perm(__funnelshift_r(p[0], p[kThreads], bit), 0, 0x0144);
+        return __byte_perm(__funnelshift_r(p[0], p[kThreads], bit), 0, 0x0123);
     }
     __device__ __forceinline__ void drain() const { cp_wait<0>(); }
-    // x in [2^9, 2^31) after a symbol: shift in 0, 1 or 2 bytes until x >= 2^23.
-    __device__ __forceinline__ uint32_t renorm(uint32_t x, uint32_t two) {
-        const uint32_t bits = ((uint32_t)__clz(x) - 1u) & 24u;
-        bit += bits;
-        return __funnelshift_l(two, x, bits);
-    }
 };
+// x in [2^9, 2^31) after a symbol: the bits (0, 8 or 16) to shift in until x >= 2^23.
+__device__ __forceinline__ uint32_t renorm_bits(uint32_t x) { return ((uint32_t)__clz(x) - 1u) & 24u; }
 
 template <int kThreads>
 __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const Nr3Record *__restrict__ recs,
@@ -204,10 +201,9 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const N
         const uint2 *l1 = level1 + srel;
         const uint2 *l2 = level2 + 4u * srel;
         uint32_t idx = kPairs - 1u, top = 0, w[4] = {0, 0, 0, 0};   // the block-start context
-#pragma unroll
-        for (uint32_t k = 0; k < 32; ++k) {
-            if (k == 0 || k == 16) rd.refill();
-            const uint32_t two = rd.peek();
+        // one symbol: its quartile and rank from the two 8-byte rows of context idx, the state update,
+        // then the next context (pair index top (top + 1) / 2 + mag)
+        auto step = [&](uint32_t k) {
             const uint2 c = l1[idx];
             const uint32_t slot = x & (kTotal - 1u), gs = slot * 0x10001u + 0x80008000u;
             // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]
@@ -224,11 +220,23 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) nr3_weights(const N
             const uint32_t start = pair & 0xffffu, freq = (pair >> 16) - start;
             x = freq * (x >> kPrec) + slot - start;
             const uint32_t sym = 4u * q + r;
-            x = rd.renorm(x, two);
             w[k / 8u] += sym << (4u * (k % 8u));
             const uint32_t mag = sym & 7u;
             top = max(top, mag);
             idx = ((top * top + top) >> 1) + mag;
+        };
+#pragma unroll
+        for (uint32_t k = 0; k < 32; k += 2) {
+            if (k == 0 || k == 16) rd.refill();
+            uint32_t win = rd.peek4();   // the bytes of both symbols of the pair
+            step(k);
+            const uint32_t b1 = renorm_bits(x);
+            x = __funnelshift_l(win, x, b1);
+            win <<= b1;
+            step(k + 1);
+            const uint32_t b2 = renorm_bits(x);
+            x = __funnelshift_l(win, x, b2);
+            rd.bit += b1 + b2;
         }
         if (nr3) {   // hash and checks on the coded nibbles, then the ceil inverse
             h = mm3_block(mm3_block(mm3_block(mm3_block(h, w[0]), w[1]), w[2]), w[3]);
