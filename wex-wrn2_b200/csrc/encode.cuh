@@ -46,8 +46,10 @@ struct CountTask {
 // scale CDFs), in device memory.
 // Both launches first set every record's three anchors from its scales (rule g for WNR3, the lower
 // median for WNR2: c/wex_neural_rans.h:399-405, :526-534).
-cudaError_t launch_encode(const uint8_t *dblob, EncRecord *recs, uint32_t nrec, const EncTask *tasks,
-                          uint32_t ntasks, uint32_t total_streams, const uint32_t *stream_rec, cudaStream_t st);
+// One group of an encode launch: records [first, first + nrec) of recs, their tasks (whose rec fields index
+// recs) and their streams (stream_rec: pairs of record index into recs and stream g).
+cudaError_t launch_encode(const uint8_t *dblob, EncRecord *recs, uint32_t first, uint32_t nrec, const EncTask *tasks,
+                          uint32_t ntasks, const uint32_t *stream_rec, uint32_t nstreams, cudaStream_t st);
 cudaError_t launch_count(EncRecord *recs, uint32_t nrec, const CountTask *tasks, uint32_t ntasks, unsigned long long *wc,
                          unsigned long long *sc, cudaStream_t st);
 

@@ -61,8 +61,17 @@ struct EncSpace {
     std::mutex mu;
     DevBuf slabs, scratch, outs, meta, blob;
     PinBuf hmeta;
-    cudaStream_t st = nullptr;
+    cudaStream_t st[2] = {}, down = nullptr;   // uploads and kernels of groups in turn; downloads
+    cudaEvent_t meta_done = nullptr, verdicts[2] = {};
+    bool ready() {
+        for (cudaStream_t *s : {&st[0], &st[1], &down})
+            if (!*s && cudaStreamCreateWithFlags(s, cudaStreamNonBlocking) != cudaSuccess) return false;
+        for (cudaEvent_t *e : {&meta_done, &verdicts[0], &verdicts[1]})
+            if (!*e && cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return false;
+        return true;
+    }
 };
+constexpr size_t kGroup = 8;   // records per pipelined group of an encode launch
 EncSpace g_enc[kMaxDevices];
 
 template <class T> T *carve(uint8_t *&p, size_t n) {
@@ -108,9 +117,8 @@ WEXB_API int wexb_encode_batch(int n, const WexEntry *const *entries, const unsi
     EncSpace &S = g_enc[device];
     std::lock_guard<std::mutex> lock(S.mu);
     const size_t slot = align_up(2 * (size_t)std::max(wchunk, schunk) + 16, 16);
-    bool cuda_ok = (S.st || cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) == cudaSuccess) &&
-                   S.blob.grow(blob_bytes) &&
-                   cudaMemcpyAsync(S.blob.p, blob, blob_bytes, cudaMemcpyHostToDevice, S.st) == cudaSuccess;
+    bool cuda_ok = S.ready() && S.blob.grow(blob_bytes) &&
+                   cudaMemcpyAsync(S.blob.p, blob, blob_bytes, cudaMemcpyHostToDevice, S.st[0]) == cudaSuccess;
     size_t at = 0;
     while (cuda_ok && at < jobs.size()) {
         // one launch: as many records as fit kLaunchBytes (at least one)
@@ -128,7 +136,9 @@ WEXB_API int wexb_encode_batch(int n, const WexEntry *const *entries, const unsi
         }
         // metadata: records, tasks, stream map, lengths and offsets, error words, results
         std::vector<EncTask> tasks;
+        std::vector<size_t> task_at(k + 1);
         for (size_t q = 0; q < k; ++q) {
+            task_at[q] = tasks.size();
             const Job &j = jobs[at + q];
             for (uint32_t m = 0; m < 3; ++m) {
                 const uint32_t ss = (j.L.scount[m] + schunk - 1) / schunk, ws = (j.L.wcount[m] + wchunk - 1) / wchunk;
@@ -136,6 +146,7 @@ WEXB_API int wexb_encode_batch(int n, const WexEntry *const *entries, const unsi
                 for (uint32_t f = 0; f < ws; f += kEncThreads) tasks.push_back({(uint32_t)q, m, 0, f, std::min<uint32_t>(kEncThreads, ws - f)});
             }
         }
+        task_at[k] = tasks.size();
         const size_t meta_bytes = align_up(k * sizeof(EncRecord), 256) + align_up(tasks.size() * sizeof(EncTask), 256) +
                                   align_up(streams * 8, 256) + align_up(streams * 8, 256) + align_up(k * 4, 256) +
                                   align_up(k * 24, 256);
@@ -180,24 +191,44 @@ WEXB_API int wexb_encode_batch(int n, const WexEntry *const *entries, const unsi
             herr[q] = 0;
             for (uint32_t g = 0; g < j.streams; ++g) { hmap[2 * (lens_at[q] + g)] = (uint32_t)q; hmap[2 * (lens_at[q] + g) + 1] = g; }
         }
-        cuda_ok = cudaMemcpyAsync(S.meta.p, S.hmeta.p, meta_bytes, cudaMemcpyHostToDevice, S.st) == cudaSuccess;
-        for (size_t q = 0; cuda_ok && q < k; ++q)
-            cuda_ok = cudaMemcpyAsync(S.slabs.p + slab_at[q], coded[jobs[at + q].i], jobs[at + q].L.raw, cudaMemcpyHostToDevice,
-                                      S.st) == cudaSuccess;
-        cuda_ok = cuda_ok && launch_encode(S.blob.p, drec, (uint32_t)k, dtask, (uint32_t)tasks.size(), (uint32_t)streams,
-                                           dmap, S.st) == cudaSuccess &&
-                  cudaMemcpyAsync(hres, dres, 24 * k, cudaMemcpyDeviceToHost, S.st) == cudaSuccess &&
-                  cudaStreamSynchronize(S.st) == cudaSuccess;
-        for (size_t q = 0; cuda_ok && q < k; ++q) {
-            const Job &j = jobs[at + q];
-            const int64_t st = (int64_t)hres[3 * q];
-            status[j.i] = (int)st;
-            used[j.i] = (size_t)hres[3 * q + 1];
-            total[j.i] = (size_t)hres[3 * q + 2];
-            if (st == 0)
-                cuda_ok = cudaMemcpyAsync(out[j.i], S.outs.p + out_at[q], total[j.i], cudaMemcpyDeviceToHost, S.st) == cudaSuccess;
+        // The metadata first. Then groups of kGroup records on the two streams in turn: uploads, kernels and
+        // verdicts. A group's records come back, on the download stream, once its verdicts are read, while
+        // the next groups upload and encode: uploads, kernels and downloads overlap.
+        cuda_ok = cudaMemcpyAsync(S.meta.p, S.hmeta.p, meta_bytes, cudaMemcpyHostToDevice, S.st[0]) == cudaSuccess &&
+                  cudaEventRecord(S.meta_done, S.st[0]) == cudaSuccess &&
+                  cudaStreamWaitEvent(S.st[1], S.meta_done, 0) == cudaSuccess;
+        const size_t groups = (k + kGroup - 1) / kGroup;
+        auto fetch = [&](size_t gi) {   // group gi's verdicts, then its records' copies back
+            if (cudaEventSynchronize(S.verdicts[gi & 1]) != cudaSuccess) return false;
+            for (size_t q = gi * kGroup; q < std::min(k, (gi + 1) * kGroup); ++q) {
+                const Job &j = jobs[at + q];
+                const int64_t st = (int64_t)hres[3 * q];
+                status[j.i] = (int)st;
+                used[j.i] = (size_t)hres[3 * q + 1];
+                total[j.i] = (size_t)hres[3 * q + 2];
+                if (st == 0 && cudaMemcpyAsync(out[j.i], S.outs.p + out_at[q], total[j.i], cudaMemcpyDeviceToHost,
+                                               S.down) != cudaSuccess)
+                    return false;
+            }
+            return true;
+        };
+        for (size_t gi = 0; cuda_ok && gi < groups; ++gi) {
+            const size_t q0 = gi * kGroup, q1 = std::min(k, q0 + kGroup);
+            cudaStream_t sg = S.st[gi & 1];
+            for (size_t q = q0; cuda_ok && q < q1; ++q)
+                cuda_ok = cudaMemcpyAsync(S.slabs.p + slab_at[q], coded[jobs[at + q].i], jobs[at + q].L.raw,
+                                          cudaMemcpyHostToDevice, sg) == cudaSuccess;
+            const size_t s0 = lens_at[q0], s1 = q1 < k ? lens_at[q1] : streams;
+            cuda_ok = cuda_ok &&
+                      launch_encode(S.blob.p, drec, (uint32_t)q0, (uint32_t)(q1 - q0), dtask + task_at[q0],
+                                    (uint32_t)(task_at[q1] - task_at[q0]), dmap + 2 * s0, (uint32_t)(s1 - s0), sg) == cudaSuccess &&
+                      cudaMemcpyAsync(hres + 3 * q0, dres + 3 * q0, 24 * (q1 - q0), cudaMemcpyDeviceToHost, sg) == cudaSuccess &&
+                      cudaEventRecord(S.verdicts[gi & 1], sg) == cudaSuccess;
+            if (cuda_ok && gi) cuda_ok = fetch(gi - 1);
         }
-        cuda_ok = cuda_ok && cudaStreamSynchronize(S.st) == cudaSuccess;
+        if (cuda_ok && groups) cuda_ok = fetch(groups - 1);
+        cuda_ok = cuda_ok && cudaStreamSynchronize(S.st[0]) == cudaSuccess && cudaStreamSynchronize(S.st[1]) == cudaSuccess &&
+                  cudaStreamSynchronize(S.down) == cudaSuccess;
         if (!cuda_ok)
             for (size_t q = 0; q < k; ++q) status[jobs[at + q].i] = -2;
         at = end;
@@ -231,8 +262,7 @@ WEXB_API int wexb_count_batch(int n, const WexEntry *const *entries, const unsig
     EncSpace &S = g_enc[device];
     std::lock_guard<std::mutex> lock(S.mu);
     const size_t counters = (3 * kEncContexts * 16 + 3 * 256) * sizeof(unsigned long long);
-    bool ok = (S.st || cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking) == cudaSuccess) && S.outs.grow(counters) &&
-              cudaMemsetAsync(S.outs.p, 0, counters, S.st) == cudaSuccess;
+    bool ok = S.ready() && S.outs.grow(counters) && cudaMemsetAsync(S.outs.p, 0, counters, S.st[0]) == cudaSuccess;
     unsigned long long *dwc = reinterpret_cast<unsigned long long *>(S.outs.p), *dsc = dwc + 3 * kEncContexts * 16;
     size_t at = 0;
     while (ok && at < jobs.size()) {
@@ -273,12 +303,12 @@ WEXB_API int wexb_count_batch(int n, const WexEntry *const *entries, const unsig
             }
             R.nr3 = nr3 ? 1 : 0;
         }
-        ok = cudaMemcpyAsync(S.meta.p, S.hmeta.p, meta_bytes, cudaMemcpyHostToDevice, S.st) == cudaSuccess;
+        ok = cudaMemcpyAsync(S.meta.p, S.hmeta.p, meta_bytes, cudaMemcpyHostToDevice, S.st[0]) == cudaSuccess;
         for (size_t q = 0; ok && q < k; ++q)
             ok = cudaMemcpyAsync(S.slabs.p + slab_at[q], coded[jobs[at + q].i], jobs[at + q].L.raw, cudaMemcpyHostToDevice,
-                                 S.st) == cudaSuccess;
-        ok = ok && launch_count(drec, (uint32_t)k, dtask, (uint32_t)tasks.size(), dwc, dsc, S.st) == cudaSuccess &&
-             cudaStreamSynchronize(S.st) == cudaSuccess;   // the slabs and metadata are reused by the next launch
+                                 S.st[0]) == cudaSuccess;
+        ok = ok && launch_count(drec, (uint32_t)k, dtask, (uint32_t)tasks.size(), dwc, dsc, S.st[0]) == cudaSuccess &&
+             cudaStreamSynchronize(S.st[0]) == cudaSuccess;   // the slabs and metadata are reused by the next launch
         at = end;
     }
     std::vector<unsigned long long> hwc(3 * kEncContexts * 16), hsc(3 * 256);

@@ -265,14 +265,14 @@ __global__ void __launch_bounds__(256) enc_count(const EncRecord *recs, const Co
 
 }  // namespace
 
-cudaError_t launch_encode(const uint8_t *dblob, EncRecord *recs, uint32_t nrec, const EncTask *tasks,
-                          uint32_t ntasks, uint32_t total_streams, const uint32_t *stream_rec, cudaStream_t st) {
+cudaError_t launch_encode(const uint8_t *dblob, EncRecord *recs, uint32_t first, uint32_t nrec, const EncTask *tasks,
+                          uint32_t ntasks, const uint32_t *stream_rec, uint32_t nstreams, cudaStream_t st) {
     if (!nrec) return cudaSuccess;
-    enc_anchor<<<3 * nrec, 256, 0, st>>>(recs);
+    enc_anchor<<<3 * nrec, 256, 0, st>>>(recs + first);
     enc_streams<<<ntasks, kEncThreads, 0, st>>>(dblob, recs, tasks);
-    enc_scan<<<nrec, 1024, 0, st>>>(recs);
+    enc_scan<<<nrec, 1024, 0, st>>>(recs + first);
     const uint32_t warps_per_cta = 256 / 32;
-    enc_pack<<<(total_streams + warps_per_cta - 1) / warps_per_cta, 256, 0, st>>>(recs, stream_rec, total_streams);
+    enc_pack<<<(nstreams + warps_per_cta - 1) / warps_per_cta, 256, 0, st>>>(recs, stream_rec, nstreams);
     return cudaGetLastError();
 }
 
