@@ -71,7 +71,7 @@ struct EncSpace {
         return true;
     }
 };
-constexpr size_t kGroup = 8;   // records per pipelined group of an encode launch
+constexpr size_t kGroup = 16;   // records per pipelined group of an encode launch
 EncSpace g_enc[kMaxDevices];
 
 template <class T> T *carve(uint8_t *&p, size_t n) {

@@ -61,7 +61,18 @@ __global__ void __launch_bounds__(256) enc_anchor(EncRecord *recs) {
     const uint8_t *s = R.coded + R.soff[m];
     hist[threadIdx.x] = 0;
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&hist[s[i]], 1u);
+    uint32_t i0 = 0;
+    if (!(reinterpret_cast<uintptr_t>(s) & 15u)) {   // 16 scales a load
+        const uint4 *v = reinterpret_cast<const uint4 *>(s);
+        for (uint32_t i = threadIdx.x; i < n / 16; i += blockDim.x) {
+            const uint4 q = v[i];
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int k = 0; k < 16; ++k) atomicAdd(&hist[(w[k >> 2] >> (8 * (k & 3))) & 0xffu], 1u);
+        }
+        i0 = n & ~15u;
+    }
+    for (uint32_t i = i0 + threadIdx.x; i < n; i += blockDim.x) atomicAdd(&hist[s[i]], 1u);
     __syncthreads();
     if (threadIdx.x) return;
     uint32_t best = 0;
