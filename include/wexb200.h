@@ -5,7 +5,8 @@
  * Resident records: an engine that keeps compressed experts in HBM uploads and validates them once
  * (wexb_resident_create) and then decodes any subset straight from device memory into its own
  * device buffers, asynchronously on its own stream (wexb_resident_decode + wexb_resident_wait).
- * One decode of a resident set is in flight at a time. */
+ * Two decodes of a resident set may be queued at once, so the host plans the next one while the GPU
+ * runs the previous one; a wait returns the oldest queued decode. */
 #ifndef WEXB_WEXB200_H
 #define WEXB_WEXB200_H
 #include "wex_entry.h"
@@ -42,15 +43,17 @@ int wexb_resident_create(int n, const WexEntry *const *entries, const unsigned c
 size_t wexb_resident_bytes(const WexbResident *r);
 /* Queue the decode of resident records index[0 .. k) on `stream` (a cudaStream_t, NULL = the set's own
  * stream): record index[j]'s matrix m goes to dst_scale[3j + m] / dst_weight[3j + m] (device), each
- * written only if that record decoded cleanly. Returns 0 queued, -1 bad arguments (nothing queued),
- * 1 CUDA error. */
+ * written only if that record decoded cleanly. With two decodes already queued, the oldest is waited
+ * for first and its statuses are dropped. Returns 0 queued, -1 bad arguments (nothing queued), 1 CUDA
+ * error. */
 int wexb_resident_decode(WexbResident *r, int k, const int *index, unsigned char *const *dst_scale,
                          unsigned char *const *dst_weight, void *stream);
-/* Wait for the queued decode; status[j] of record index[j]: 0 written, -1 failed its checks
- * (destination untouched), 1 CUDA error. Returns the number of non-zero statuses. */
+/* Wait for the oldest queued decode; status[j] of its record index[j]: 0 written, -1 failed its checks
+ * (destination untouched), 1 CUDA error. Returns the number of non-zero statuses, -1 when nothing is
+ * queued. */
 int wexb_resident_wait(WexbResident *r, int *status);
-/* 1: bracket each kernel of the following decodes with CUDA events on its stream; 0: stop. Returns 0,
- * or 1 when the events cannot be created. */
+/* 1: bracket each kernel of the following decodes with CUDA events on its stream; 0: stop. Returns 0
+ * (a decode returns 1 when its events cannot be created). */
 int wexb_resident_profile(WexbResident *r, int on);
 /* Milliseconds of the scale, weight and commit kernels of the last waited decode (profiling on):
  * 0, or -1 when there is nothing to report. */

@@ -286,6 +286,38 @@ def test_resident_decode(torch_cuda, tiny):
     res.close()
 
 
+def test_resident_two_decodes_queued(torch_cuda, tiny):
+    """Two decodes of one resident set queued at once (different subsets and destinations): each wait
+    returns the oldest decode's statuses; a third decode with two queued drops the oldest's statuses;
+    a wait with nothing queued returns -1."""
+    blob, ex = tiny
+    res = wexcuda.Resident([e.entry for e in ex], [e.record for e in ex], 0)
+    res.profile(True)
+    a, b, c = [1, 2], [0, 1, 2], [2]
+    ta, sa, wa = _dst(torch_cuda, ex[0].entry, len(a))
+    tb, sb, wb = _dst(torch_cuda, ex[0].entry, len(b))
+    tc, sc, wc = _dst(torch_cuda, ex[0].entry, len(c))
+    L = wexcuda.lib()
+    status = (ctypes.c_int * 3)()
+
+    def queue(index, sp, wp):
+        idx = (ctypes.c_int * len(index))(*index)
+        return L.wexb_resident_decode(res.handle, len(index), idx, wexcuda._ptrs(sp), wexcuda._ptrs(wp), None)
+    assert queue(a, sa, wa) == 0 and queue(b, sb, wb) == 0
+    assert L.wexb_resident_wait(res.handle, status) == 0 and list(status)[:2] == [0, 0]   # a
+    ms = (ctypes.c_float * 3)()
+    assert L.wexb_resident_kernel_ms(res.handle, ms) == 0 and all(v > 0 for v in ms)
+    assert queue(c, sc, wc) == 0                       # b and c queued
+    assert queue(a, sa, wa) == 0                       # b waited for and dropped; c and a queued
+    assert L.wexb_resident_wait(res.handle, status) == 0 and list(status)[:1] == [0]        # c
+    assert L.wexb_resident_wait(res.handle, status) == 0 and list(status)[:2] == [0, 0]     # a
+    assert L.wexb_resident_wait(res.handle, status) == -1
+    for ts, index in ((ta, a), (tb, b), (tc, c)):
+        for j, x in enumerate(index):
+            assert _slab(ts, j) == ex[x].expected
+    res.close()
+
+
 def test_queued_batches(torch_cuda, tiny):
     """wexb_batch_submit / wexb_batch_wait: several batches in flight, one with a damaged and an
     unavailable record; each wait gives the statuses of the synchronous call; tickets are single-use."""

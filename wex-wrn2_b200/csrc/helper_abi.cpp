@@ -406,20 +406,30 @@ bool batch_uploads_wait(int t) {
 }  // namespace wexb
 
 // ---- resident records --------------------------------------------------------------------------
+// One queued decode of a resident set: its metadata (host and device), scratch, events and statuses.
+struct ResSlot {
+    DevBuf dscratch, dmeta;
+    PinBuf hmeta;
+    MetaLayout L;
+    cudaEvent_t done = nullptr;
+    cudaEvent_t marks[4] = {};
+    bool timed = false;
+    int k = 0;
+};
+// Two decodes may be queued at once: the host plans the next one while the GPU runs the previous one.
 struct WexbResident {
     int device = -1;
     cudaStream_t own = nullptr;
-    cudaEvent_t done = nullptr;
     std::vector<Plan> plans;          // lengths pointers cleared: the records live on the device
     std::vector<Nr3Tables> tabs;
     std::vector<size_t> rec_off, off_off;
-    DevBuf store, dscratch, dmeta;    // store: records, then offset tables
-    PinBuf hmeta;
+    DevBuf store;                     // records, then offset tables
     size_t offs_at = 0, bytes = 0;
-    bool queued = false, profiling = false, timed = false;
-    int last_k = 0, launches = 0;
-    cudaEvent_t marks[4] = {};
-    MetaLayout L;
+    bool profiling = false;
+    int launches = 0;
+    ResSlot slot[2];
+    int head = 0, queued = 0;         // the oldest queued decode's slot, and how many are queued
+    int waited = -1;                  // the slot of the last waited decode (kernel times)
 };
 
 WEXB_API unsigned int wexb_abi(void) { return 1u; }
@@ -459,7 +469,8 @@ WEXB_API int wexb_resident_create(int n, const WexEntry *const *entries, const u
     r->offs_at = align_up(rec_bytes, 256);
     r->bytes = r->offs_at + noffs * 4;
     bool ok = cudaStreamCreateWithFlags(&r->own, cudaStreamNonBlocking) == cudaSuccess &&
-              cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming) == cudaSuccess && r->store.grow(r->bytes);
+              cudaEventCreateWithFlags(&r->slot[0].done, cudaEventDisableTiming) == cudaSuccess &&
+              cudaEventCreateWithFlags(&r->slot[1].done, cudaEventDisableTiming) == cudaSuccess && r->store.grow(r->bytes);
     for (int i = 0, j = 0; ok && i < n; ++i) {
         if (status[i]) continue;
         ok = cudaMemcpy(r->store.p + r->rec_off[(size_t)j], records[i], r->plans[(size_t)j].total, cudaMemcpyHostToDevice) == cudaSuccess &&
@@ -480,6 +491,28 @@ WEXB_API int wexb_resident_create(int n, const WexEntry *const *entries, const u
 
 WEXB_API size_t wexb_resident_bytes(const WexbResident *r) { return r ? r->bytes : 0; }
 
+namespace {
+// Waits for the oldest queued decode of r and releases its slot: its statuses (may be NULL), or
+// nullptr-safe counts. Returns the number of non-zero statuses.
+int resident_retire(WexbResident *r, int *status) {
+    ResSlot &q = r->slot[r->head];
+    const bool ok = cudaSetDevice(r->device) == cudaSuccess && cudaEventSynchronize(q.done) == cudaSuccess;
+    if (!ok) (void)cudaGetLastError();
+    const uint32_t *herrs = reinterpret_cast<const uint32_t *>(q.hmeta.p + q.L.errs);
+    int bad = 0;
+    for (int j = 0; j < q.k; ++j) {
+        const int v = !ok ? 1 : herrs[j] ? -1 : 0;
+        if (v == -1) report_error_bits(herrs[j]);
+        if (status) status[j] = v;
+        bad += v != 0;
+    }
+    r->waited = r->head;
+    r->head ^= 1;
+    --r->queued;
+    return bad;
+}
+}  // namespace
+
 WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsigned char *const *dst_scale,
                                   unsigned char *const *dst_weight, void *stream) {
     if (!r || k <= 0 || !index || !dst_scale || !dst_weight) return -1;
@@ -488,8 +521,9 @@ WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsi
         for (int m = 0; m < 3; ++m) if (!dst_scale[3 * j + m] || !dst_weight[3 * j + m]) return -1;
     }
     if (cudaSetDevice(r->device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
-    if (r->queued && cudaEventSynchronize(r->done) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
-    r->queued = false;
+    if (r->queued == 2) (void)resident_retire(r, nullptr);   // both slots busy: the oldest decode's statuses are dropped
+    const int si = (r->head + r->queued) & 1;
+    ResSlot &q = r->slot[si];
     cudaStream_t st = stream ? (cudaStream_t)stream : r->own;
     const int wthreads = weight_threads();
     std::vector<Nr3Task> stasks, wtasks;
@@ -500,19 +534,19 @@ WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsi
         scr_off[(size_t)j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
         plan_tasks(p, (uint32_t)j, wthreads, stasks, wtasks);
     }
-    r->L.compute((size_t)k, stasks.size(), wtasks.size(), (size_t)k, 0);
-    if (!r->dscratch.grow(scr_bytes) || !r->dmeta.grow(r->L.total) || !r->hmeta.grow(r->L.total)) return 1;
-    uint8_t *hm = r->hmeta.p, *dm = r->dmeta.p;
-    Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + r->L.recs);
-    CommitJob *hjobs = reinterpret_cast<CommitJob *>(hm + r->L.jobs);
-    uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + r->L.errs);
-    uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + r->L.errs);
-    std::memcpy(hm + r->L.stasks, stasks.data(), stasks.size() * sizeof(Nr3Task));
-    std::memcpy(hm + r->L.wtasks, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
+    q.L.compute((size_t)k, stasks.size(), wtasks.size(), (size_t)k, 0);
+    if (!q.dscratch.grow(scr_bytes) || !q.dmeta.grow(q.L.total) || !q.hmeta.grow(q.L.total)) return 1;
+    uint8_t *hm = q.hmeta.p, *dm = q.dmeta.p;
+    Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + q.L.recs);
+    CommitJob *hjobs = reinterpret_cast<CommitJob *>(hm + q.L.jobs);
+    uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + q.L.errs);
+    uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + q.L.errs);
+    std::memcpy(hm + q.L.stasks, stasks.data(), stasks.size() * sizeof(Nr3Task));
+    std::memcpy(hm + q.L.wtasks, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
     for (int j = 0; j < k; ++j) {
         const size_t x = (size_t)index[j];
         const Plan &p = r->plans[x];
-        uint8_t *scr = r->dscratch.p + scr_off[(size_t)j];
+        uint8_t *scr = q.dscratch.p + scr_off[(size_t)j];
         plan_descriptor(p, r->tabs[x], r->store.p + r->rec_off[x],
                         reinterpret_cast<const uint32_t *>(r->store.p + r->offs_at) + r->off_off[x], scr, derrs + j, &hrecs[j]);
         herrs[j] = 0;
@@ -523,56 +557,45 @@ WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsi
         }
         J.error = derrs + j;
     }
-    const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + r->L.recs);
-    auto mark = [&](int i) { return !r->profiling || cudaEventRecord(r->marks[i], st) == cudaSuccess; };
-    bool ok = cudaMemcpyAsync(dm, hm, r->L.total, cudaMemcpyHostToDevice, st) == cudaSuccess && mark(0) &&
-              launch_nr3_scales(drecs, reinterpret_cast<const Nr3Task *>(dm + r->L.stasks), (uint32_t)stasks.size(), st) == cudaSuccess &&
+    if (r->profiling && !q.marks[0])
+        for (auto &e : q.marks)
+            if (cudaEventCreate(&e) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + q.L.recs);
+    auto mark = [&](int i) { return !r->profiling || cudaEventRecord(q.marks[i], st) == cudaSuccess; };
+    bool ok = cudaMemcpyAsync(dm, hm, q.L.total, cudaMemcpyHostToDevice, st) == cudaSuccess && mark(0) &&
+              launch_nr3_scales(drecs, reinterpret_cast<const Nr3Task *>(dm + q.L.stasks), (uint32_t)stasks.size(), st) == cudaSuccess &&
               mark(1) &&
-              launch_nr3_weights(drecs, reinterpret_cast<const Nr3Task *>(dm + r->L.wtasks), (uint32_t)wtasks.size(), wthreads, st) == cudaSuccess &&
-              mark(2) && launch_commit(reinterpret_cast<const CommitJob *>(dm + r->L.jobs), (uint32_t)k, st) == cudaSuccess &&
+              launch_nr3_weights(drecs, reinterpret_cast<const Nr3Task *>(dm + q.L.wtasks), (uint32_t)wtasks.size(), wthreads, st) == cudaSuccess &&
+              mark(2) && launch_commit(reinterpret_cast<const CommitJob *>(dm + q.L.jobs), (uint32_t)k, st) == cudaSuccess &&
               mark(3) && cudaMemcpyAsync(herrs, derrs, 4 * (size_t)k, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-              cudaEventRecord(r->done, st) == cudaSuccess;
+              cudaEventRecord(q.done, st) == cudaSuccess;
     if (!ok) { (void)cudaGetLastError(); return 1; }
-    r->timed = r->profiling;
-    r->queued = true;
-    r->last_k = k;
+    q.timed = r->profiling;
+    q.k = k;
+    if (r->waited == si) r->waited = -1;   // its kernel times are being overwritten
+    ++r->queued;
     r->launches = 3;
     return 0;
 }
 
 WEXB_API int wexb_resident_wait(WexbResident *r, int *status) {
     if (!r || !r->queued) return -1;
-    const bool ok = cudaSetDevice(r->device) == cudaSuccess && cudaEventSynchronize(r->done) == cudaSuccess;
-    if (!ok) (void)cudaGetLastError();
-    r->queued = false;
-    const uint32_t *herrs = reinterpret_cast<const uint32_t *>(r->hmeta.p + r->L.errs);
-    int bad = 0;
-    for (int j = 0; j < r->last_k; ++j) {
-        const int v = !ok ? 1 : herrs[j] ? -1 : 0;
-        if (v == -1) report_error_bits(herrs[j]);
-        if (status) status[j] = v;
-        bad += v != 0;
-    }
-    return bad;
+    return resident_retire(r, status);
 }
 
 WEXB_API int wexb_resident_launches(const WexbResident *r) { return r ? r->launches : 0; }
 
 WEXB_API int wexb_resident_profile(WexbResident *r, int on) {
     if (!r) return -1;
-    if (on && !r->marks[0]) {
-        if (cudaSetDevice(r->device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
-        for (auto &e : r->marks)
-            if (cudaEventCreate(&e) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
-    }
     r->profiling = on != 0;
     return 0;
 }
 
 WEXB_API int wexb_resident_kernel_ms(const WexbResident *r, float *ms3) {
-    if (!r || !ms3 || !r->timed || r->queued) return -1;
+    if (!r || !ms3 || r->waited < 0 || !r->slot[r->waited].timed) return -1;
+    const ResSlot &q = r->slot[r->waited];
     for (int i = 0; i < 3; ++i)
-        if (cudaEventElapsedTime(&ms3[i], r->marks[i], r->marks[i + 1]) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
+        if (cudaEventElapsedTime(&ms3[i], q.marks[i], q.marks[i + 1]) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
     return 0;
 }
 
@@ -580,10 +603,13 @@ WEXB_API void wexb_resident_destroy(WexbResident *r) {
     if (!r) return;
     if (r->device >= 0 && cudaSetDevice(r->device) == cudaSuccess) {
         if (r->own) cudaStreamSynchronize(r->own);
-        if (r->done) { cudaEventSynchronize(r->done); cudaEventDestroy(r->done); }
+        for (ResSlot &q : r->slot) {
+            if (q.done) { cudaEventSynchronize(q.done); cudaEventDestroy(q.done); }
+            for (auto &e : q.marks) if (e) cudaEventDestroy(e);
+            q.dscratch.release(); q.dmeta.release(); q.hmeta.release();
+        }
         if (r->own) cudaStreamDestroy(r->own);
-        for (auto &e : r->marks) if (e) cudaEventDestroy(e);
-        r->store.release(); r->dscratch.release(); r->dmeta.release(); r->hmeta.release();
+        r->store.release();
     }
     (void)cudaGetLastError();
     delete r;
