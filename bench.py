@@ -10,7 +10,9 @@ i.e. 384 expert records and 962 MB of decoded slabs. Inputs are seeded synthetic
 involved) and larger than L2 between steps.
 
   value  records resident in HBM (wexb_resident_*), the step's 384 records decoded by one queued
-         decode (3 kernel launches), timed with CUDA events on the launching stream
+         decode (3 kernel launches; the next step's decode is planned while this one runs), timed
+         with CUDA events on the launching stream; roofline: the weight kernel against HBM and, as
+         roofline.issue, against the warp-instruction issue rate that binds it
   e2e    from pinned host memory through the C ABI: per layer one call of 8 records (H2D inside the
          timed region, statuses read back), 48 calls a step, timed by the host clock (max over
          ranks); the headline keeps --depth calls in flight (wexb_batch_submit / wexb_batch_wait),
@@ -23,6 +25,10 @@ final gather of per-rank outcome counters.
 --impl reference: the reference's own CPU decoder (wex_nr2_decode via its wex_nr3_decode tool,
 compiled from its sources into oracle/_ref) on all host cores, one record per core, on a bounded
 sample of the same records.
+
+Other workloads (--config): large and box (hidden 7168, FFN 2048, canonical zero), wnr4 (draft codec
+8 through the WNR4 ABI), tiny-file and mixed (WEX4 containers checked by wex4_check), file (expert
+misses read from a container file on disk: wexb_file_decode) and encode (the GPU record writer).
 """
 import argparse
 import hashlib
