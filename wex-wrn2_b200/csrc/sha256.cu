@@ -161,11 +161,32 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *_
     const uint32_t mine = active ? msg_blocks(m.bytes) : 0u;
     const uint32_t blocks = __reduce_max_sync(0xffffffffu, mine);
     if (warp == 1) {   // producer
+        // a whole data block's four 16-byte loads are issued one block ahead, before the schedule work of
+        // the current block, so their latency is hidden behind it
+        uint4 v[4];
+        bool ahead = false;
+        auto load = [&](uint32_t b) {
+            ahead = 64ull * b + 64 <= m.bytes;
+            if (!ahead) return;
+            const uint4 *q = reinterpret_cast<const uint4 *>(m.data + 64ull * b);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = __ldg(q + k);
+        };
+        if (mine) load(0);
         for (uint32_t b = 0; b < blocks; ++b) {
             if (b < mine) {
-                if (64ull * (b + 8) + 64 <= m.bytes) asm volatile("prefetch.global.L2 [%0];" :: "l"(m.data + 64ull * (b + 8)));
                 uint32_t w[16];
-                produce_block(m.data, m.bytes, b, w);
+                if (ahead) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        w[4 * k] = bswap(v[k].x); w[4 * k + 1] = bswap(v[k].y);
+                        w[4 * k + 2] = bswap(v[k].z); w[4 * k + 3] = bswap(v[k].w);
+                    }
+                } else {
+                    produce_block(m.data, m.bytes, b, w);
+                }
+                if (b + 1 < mine) load(b + 1);
+                if (64ull * (b + 8) + 64 <= m.bytes) asm volatile("prefetch.global.L2 [%0];" :: "l"(m.data + 64ull * (b + 8)));
                 uint32_t (*out)[kShaLanes] = sched[b & 1];
 #pragma unroll
                 for (int t = 0; t < 64; ++t) {
@@ -192,11 +213,17 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *_
         if (b >= mine) continue;
         const uint32_t (*in)[kShaLanes] = sched[b & 1];
         uint32_t a = st[0], bb = st[1], c = st[2], d = st[3], e = st[4], f = st[5], g = st[6], h = st[7];
+        // hk = h + W[t] + K[t], formed a round early (the next round's h is this round's g), so that the
+        // new e and a are one three-input add after the round's rotations and logic functions
+        uint32_t hk = h + in[0][lane];
 #pragma unroll
         for (int t = 0; t < 64; ++t) {
-            const uint32_t t1 = h + (ror(e, 6) ^ ror(e, 11) ^ ror(e, 25)) + ((e & f) ^ (~e & g)) + in[t][lane];
-            const uint32_t t2 = (ror(a, 2) ^ ror(a, 13) ^ ror(a, 22)) + ((a & bb) ^ (a & c) ^ (bb & c));
-            h = g; g = f; f = e; e = d + t1; d = c; c = bb; bb = a; a = t1 + t2;
+            const uint32_t s1 = ror(e, 6) ^ ror(e, 11) ^ ror(e, 25), ch = (e & f) ^ (~e & g);
+            const uint32_t s0 = ror(a, 2) ^ ror(a, 13) ^ ror(a, 22), mj = (a & bb) ^ (a & c) ^ (bb & c);
+            const uint32_t dhk = d + hk, t1 = hk + s1 + ch;
+            const uint32_t next_hk = t < 63 ? g + in[t + 1][lane] : 0u;
+            h = g; g = f; f = e; e = dhk + s1 + ch; d = c; c = bb; bb = a; a = t1 + (s0 + mj);
+            hk = next_hk;
         }
         st[0] += a; st[1] += bb; st[2] += c; st[3] += d; st[4] += e; st[5] += f; st[6] += g; st[7] += h;
     }
