@@ -2,8 +2,7 @@
 build_image in nr3_host.cpp makes from a WNM2 model), emulated on the CPU with numpy's 32-bit wrap-around
 arithmetic for every slot of every reachable context of a trained model: the quartile from the level-1
 row, the rank from the level-2 row, and start and end taken by the byte permute and the funnel shift,
-against a direct search of the context's CDF. Also the byte table of triangular numbers that gives the
-next context and the two-symbol payload window."""
+against a direct search of the context's CDF. Also the two-symbol payload window."""
 import numpy as np
 
 import synth
@@ -87,12 +86,6 @@ def test_lookup_matches_a_direct_search_on_every_slot():
                     assert np.array_equal(freq.astype(np.int64), cdf[want + 1] - cdf[want])
                     checked += 1
     assert checked == 3 * 7 * 37
-
-
-def test_triangular_numbers_by_byte_permute():
-    tops = np.arange(8, dtype=np.uint64)
-    got = byte_perm(np.full(8, 0x06030100, np.uint64), np.full(8, 0x1C150F0A, np.uint64), tops)
-    assert list(got) == [t * (t + 1) // 2 for t in range(8)]
 
 
 def test_two_symbol_window():
