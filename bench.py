@@ -665,7 +665,6 @@ def open_expert_file(wexcuda, path):
 
 def run_file(args, cfg):
     import torch
-    import wexcuda
     world, rank, local = dist_init()
     torch.cuda.set_device(local)
     threads = max(1, (os.cpu_count() or 8) // max(1, int(os.environ.get('LOCAL_WORLD_SIZE', world))))
@@ -673,6 +672,16 @@ def run_file(args, cfg):
     path, owners, experts, _ = write_expert_file(cfg, rank, world, threads)
     log(f'[rank {rank}] file of {len(owners)} records ({os.path.getsize(path) / 1e9:.2f} GB) written in '
         f'{time.time() - t0:.1f} s at {path}')
+    try:   # the file is removed however the run ends
+        return file_steps(args, cfg, world, rank, local, path, owners, experts)
+    finally:
+        if os.path.exists(path):
+            os.remove(path)
+
+
+def file_steps(args, cfg, world, rank, local, path, owners, experts):
+    import torch
+    import wexcuda
     by_owner = {(e.layer, e.index): e for e in experts}
     raw = len(experts[0].expected)
     N = min(cfg['misses'], len(owners))
@@ -744,7 +753,6 @@ def run_file(args, cfg):
         'gpu_launches': 3 * -(-N // 8), 'clocks': clk, 'verified_records': 2,
     }
     f.close()
-    os.remove(path)
     if rank == 0:
         if not args.no_cpu_baseline and world == 1:
             line['cpu_baseline'] = reference_file_miss_rate(args, cfg, None, seconds=args.cpu_seconds)
