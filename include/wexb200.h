@@ -75,6 +75,13 @@ void wexb_resident_destroy(WexbResident *r);
 int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned char *record, int device,
                                   unsigned char *const *dst_scale, unsigned char *const *dst_weight);
 
+/* Self-test of the bounded waits. Every kernel waits on its shared-memory mbarriers for at most a fixed
+ * number of polls, then sets error bit 16 in the record's error word and returns: it never spins
+ * forever. This runs the same wait, limited to `polls` polls, on a barrier that completes and on one
+ * that nothing arrives on; *bits receives the second one's error bits (16). Returns 0 when the first
+ * completes and the second gives up, -1 otherwise or for bad arguments, 1 when CUDA is unavailable. */
+int wexb_selftest_bounded_wait(int device, unsigned int polls, unsigned int *bits);
+
 /* Error bits of the last failed record seen by this process (1 structure, 2 stream hash, 4 ceil form
  * at scale 0, 8 canonical zero, 16 bounded wait expired); 0 if none failed. */
 unsigned int wexb_last_error_bits(void);

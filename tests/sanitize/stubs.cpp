@@ -10,6 +10,7 @@
 
 namespace wexb {
 cudaError_t launch_zero_check(const ZeroJob *, uint32_t, cudaStream_t) { return cudaErrorNotSupported; }
+cudaError_t launch_wait_probe(uint32_t, uint32_t, uint32_t *, cudaStream_t) { return cudaErrorNotSupported; }
 cudaError_t launch_encode(const uint8_t *, EncRecord *, uint32_t, uint32_t, const EncTask *, uint32_t, const uint32_t *,
                           uint32_t, cudaStream_t) { return cudaErrorNotSupported; }
 cudaError_t launch_count(EncRecord *, uint32_t, const CountTask *, uint32_t, unsigned long long *, unsigned long long *,

@@ -45,3 +45,4 @@ def test_argument_errors_need_no_gpu():
     assert L.wex_cuda_decode_batch_to_host(3, None, None, 0, None, None) == 3
     assert L.wex_cuda_host_register(None, 0) == -1
     assert L.wex_cuda_register_model(b'\0' * 16, 16) == -1
+    assert wexcuda.selftest_bounded_wait(0, 0)[0] == -1 and wexcuda.selftest_bounded_wait(-1, 10)[0] == -1

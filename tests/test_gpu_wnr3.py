@@ -318,6 +318,16 @@ def test_resident_two_decodes_queued(torch_cuda, tiny):
     res.close()
 
 
+def test_bounded_wait_gives_up_and_the_context_stays_usable(torch_cuda, tiny):
+    """The mbarrier wait every kernel uses, on a barrier nothing arrives on, gives up after its polls
+    with error bit 16 (no spin without end, no fault); a decode right after it is bit-exact."""
+    st, bits = wexcuda.selftest_bounded_wait(0, 2000)
+    assert st == 0 and bits == 16
+    blob, ex = tiny
+    bad, st2, ts = _decode_device(torch_cuda, [e.entry for e in ex], [e.record for e in ex])
+    assert bad == 0 and all(_slab(ts, j) == e.expected for j, e in enumerate(ex))
+
+
 def test_queued_batches(torch_cuda, tiny):
     """wexb_batch_submit / wexb_batch_wait: several batches in flight, one with a damaged and an
     unavailable record; each wait gives the statuses of the synchronous call; tickets are single-use."""

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "bufs.h"
+#include "container.cuh"
 #include "nr3_host.h"
 #include "wex_cuda_helper.h"
 #include "wexb200.h"
@@ -358,6 +359,20 @@ WEXB_API int wex_cuda_host_unregister(void *pointer) {
     if (!pointer) return -1;
     if (cudaHostUnregister(pointer) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
     return 0;
+}
+
+WEXB_API int wexb_selftest_bounded_wait(int device, unsigned int polls, unsigned int *bits) {
+    if (!bits || !polls || device < 0 || device >= kMaxDevices) return -1;
+    if (cudaSetDevice(device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+    uint32_t *d = nullptr, h[2] = {~0u, ~0u};
+    bool ok = cudaMalloc(&d, sizeof h) == cudaSuccess &&
+              launch_wait_probe(1, polls, d, nullptr) == cudaSuccess &&       // a barrier that completes
+              launch_wait_probe(0, polls, d + 1, nullptr) == cudaSuccess &&   // one that nothing arrives on
+              cudaMemcpy(h, d, sizeof h, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (d) cudaFree(d);
+    if (!ok) { (void)cudaGetLastError(); return 1; }
+    *bits = h[1];
+    return h[0] == 0 && h[1] == kErrTimeout ? 0 : -1;
 }
 
 WEXB_API int wexb_batch_submit(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,

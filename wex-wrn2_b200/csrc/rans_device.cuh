@@ -54,10 +54,10 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  :: "r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src), "r"(bytes),
                     "r"((unsigned)__cvta_generic_to_shared(bar)) : "memory");
 }
-// Waits for phase `parity` of the mbarrier, at most kSpinLimit polls; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Waits for phase `parity` of the mbarrier, at most `limit` polls; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = kSpinLimit) {
     const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    for (uint32_t i = 0; i < limit; ++i) {
         uint32_t done;
         asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
                      : "=r"(done) : "r"(a), "r"(parity) : "memory");

@@ -60,6 +60,7 @@ def lib():
         L.wexb_file_close.argtypes = [P]; L.wexb_file_close.restype = None
         L.wexb_encode_batch.argtypes = [I, P, P, P, P, I, ctypes.c_uint, ctypes.c_uint, P, SZ, I, P, P, P, P, P]
         L.wexb_count_batch.argtypes = [I, P, P, I, I, P, P, P]
+        L.wexb_selftest_bounded_wait.argtypes = [I, ctypes.c_uint, P]
         _lib = L
     return _lib
 
@@ -303,3 +304,10 @@ def count_batch(entries, coded, nr3=True, device=0):
     lib().wexb_count_batch(n, ep, _ptrs([x[0] for x in srcs]), 1 if nr3 else 0, device, wc.ctypes.data, sc.ctypes.data,
                            status)
     return list(status)[:n], wc, sc
+
+
+def selftest_bounded_wait(device=0, polls=1000):
+    """(status, error bits of the wait that nothing completes): wexb_selftest_bounded_wait."""
+    bits = ctypes.c_uint()
+    st = lib().wexb_selftest_bounded_wait(device, polls, ctypes.byref(bits))
+    return st, bits.value
