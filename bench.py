@@ -49,8 +49,10 @@ sys.path.insert(0, os.path.join(ROOT, 'wex-wrn2_b200'))
 CONFIGS = {
     'tiny': dict(hidden=1024, ffn=512, layers=1, experts=8, batch=8, cz=False, sigma=(0.02, 0.02), neg_zero=0.0),
     'mid': dict(hidden=2048, ffn=768, layers=48, experts=128, batch=8, cz=False, sigma=(0.01, 0.04), neg_zero=0.0),
+    # the largest single-GPU workload (the default): a token step routes 464 experts of 23.4 MB; the routing
+    # trace has `trace_steps` distinct token steps, cycled, so that the distinct records fit in host memory
     'large': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
-                  lean=True),
+                  lean=True, trace_steps=2),
     # whole-box streaming: 1536 large experts, each rank decodes all of its shard every step
     'box': dict(hidden=7168, ffn=2048, layers=8, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
                 lean=True, all_experts=True),
@@ -89,10 +91,15 @@ def layer_sigmas(cfg):
 
 def routing_trace(cfg, steps, rank, world, layers):
     """[step][layer] -> 8 distinct expert ids of this rank's shard (id % world == rank), Zipf(1.1); for a
-    streaming config (all_experts) every expert of the shard, every step."""
+    streaming config (all_experts) every expert of the shard, every step. A config with `trace_steps`
+    draws that many token steps and cycles them."""
     shard = np.arange(rank, cfg['experts'], world)
     if cfg.get('all_experts'):
         return [[[int(e) for e in shard] for _ in range(layers)] for _ in range(steps)]
+    period = cfg.get('trace_steps')
+    if period and steps > period:
+        base = routing_trace(cfg, period, rank, world, layers)
+        return [base[s % period] for s in range(steps)]
     trace = []
     for layer in range(layers):
         rng = np.random.default_rng([SEED, layer, rank])
@@ -424,6 +431,86 @@ def run_reference_wnr4(args, cfg):
     return 0
 
 
+def numpy_expert_slab(hidden, ffn, seed, sigma, neg_zero):
+    """A seeded synthetic MXFP4 expert slab made with numpy alone, for the reference arm (whose process maps
+    none of this repository's libraries): per matrix N(0, sigma) elements in blocks of 32, an E8M0 scale of
+    floor(log2 amax) - 2, E2M1 codes {0, .5, 1, 1.5, 2, 3, 4, 6} by nearest with ties to the even code, the
+    sign only on non-zero codes, and a fraction neg_zero of the zero codes written as -0. Layout: the
+    scales of w1, w2, w3, then their packed nibbles (even element in the low nibble)."""
+    rng = np.random.default_rng(seed)
+    scales, packed = [], []
+    for r, c in ((ffn, hidden), (hidden, ffn), (ffn, hidden)):
+        g = rng.standard_normal((r * c // 32, 32), dtype=np.float32) * np.float32(sigma)
+        amax = np.abs(g).max(axis=1)
+        _, ex = np.frexp(amax)                      # amax = m 2^ex, m in [0.5, 1): floor(log2 amax) = ex - 1
+        e = np.where(amax > 0, ex - 3, -127).clip(-127, 127).astype(np.int32)
+        x = np.ldexp(g, -e[:, None])                # a power-of-two scaling: exact
+        mag = np.minimum(np.abs(x), np.float32(6.0))
+        code = ((mag > 0.25).astype(np.uint8) + (mag >= 0.75) + (mag > 1.25) + (mag >= 1.75) + (mag > 2.5) +
+                (mag >= 3.5) + (mag > 5.0)).astype(np.uint8)
+        nib = code | np.where((x < 0) & (code > 0), 8, 0).astype(np.uint8)
+        if neg_zero:
+            nib[(nib == 0) & (rng.random(nib.shape, dtype=np.float32) < neg_zero)] = 8
+        scales.append((e + 127).astype(np.uint8).tobytes())
+        packed.append((nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8).tobytes())
+    return b''.join(scales) + b''.join(packed)
+
+
+class RefExpert:
+    """One record of the reference arm's pool."""
+    def __init__(self, layer, index, entry, record, raw):
+        self.layer, self.index, self.entry, self.record, self.raw = layer, index, entry, record, raw
+
+
+def reference_pool(cfg, owners, cores):
+    """The reference arm's inputs, made entirely by the reference's own tools (oracle/_ref/wex_nr3_tools.so,
+    c/tools/wex_nr3_tools.c:37-120): numpy MXFP4 slabs, the coded domain (wex_nr3_prepare: canonical zero and
+    ceil form), a WNM2 model trained on them (wex_nr3_count_expert, wex_nr3_build_model) and their WNR3
+    records (wex_nr3_encode_record, chunks 2048:512). Returns (blob, experts) or None when the tools are
+    not built."""
+    import ctypes
+    import synth   # pure Python here: expert_entry / entry_with load no library
+    sys.path.insert(0, os.path.join(ROOT, 'oracle'))
+    import oracle
+    L = oracle.ref_lib('wex_nr3_tools')
+    if L is None:
+        return None
+    sig = layer_sigmas(cfg)
+    entry = synth.expert_entry(cfg['hidden'], cfg['ffn'])
+    raw = synth.raw_bytes(cfg['hidden'], cfg['ffn'])
+
+    def coded_of(o):
+        layer, idx = o
+        slab = numpy_expert_slab(cfg['hidden'], cfg['ffn'], [SEED, 7, layer, idx], sig[layer], cfg['neg_zero'])
+        coded = ctypes.create_string_buffer(raw)
+        flags = L.wex_nr3_prepare(entry, slab, 1 if cfg['cz'] else 0, coded, None)
+        if flags < 0:
+            raise RuntimeError('reference prepare refused an expert')
+        return flags, coded
+    with ThreadPoolExecutor(cores) as pool:
+        coded = list(pool.map(coded_of, owners))
+    wc, sc = np.zeros(3 * 567 * 16, np.uint64), np.zeros(3 * 256, np.uint64)
+    for _, c in coded:
+        if L.wex_nr3_count_expert(entry, c, wc.ctypes.data, sc.ctypes.data) != 0:
+            raise RuntimeError('reference counts refused an expert')
+    blob = ctypes.create_string_buffer(59408)
+    if L.wex_nr3_build_model(wc.ctypes.data, sc.ctypes.data, blob, None) != 0:
+        raise RuntimeError('reference model build failed')
+    blob = blob.raw
+
+    def encode(i):
+        (layer, idx), (flags, c) = owners[i], coded[i]
+        cap = 2 * raw + 65536
+        out, used, total = ctypes.create_string_buffer(cap), ctypes.c_size_t(), ctypes.c_size_t()
+        if L.wex_nr3_encode_record(blob, entry, c, flags, layer << 16 | idx, 2048, 512, out, cap, ctypes.byref(used),
+                                   ctypes.byref(total)) != 0:
+            raise RuntimeError('reference encoder did not compress an expert')
+        rec = out.raw[:total.value]
+        return RefExpert(layer, idx, synth.entry_with(entry, total=len(rec), codec=5), rec, raw)
+    with ThreadPoolExecutor(cores) as pool:
+        return blob, list(pool.map(encode, range(len(owners))))
+
+
 def run_reference(args, cfg):
     world, rank, local = int(os.environ.get('WORLD_SIZE', '1')), int(os.environ.get('RANK', '0')), 0
     if rank != 0:
@@ -438,41 +525,38 @@ def run_reference(args, cfg):
         return run_reference_encode(args, cfg)
     cores = os.cpu_count() or 1
     layers = args.layers or cfg['layers']
-    trace = routing_trace(cfg, args.warmup + args.steps, 0, 1, layers)
+    trace = routing_trace(cfg, 1, 0, 1, layers)
     k = sum(len(trace[0][l]) for l in range(layers))   # records per step of the GPU arm's workload
-    # one step of the reference arm: ceil(cores / 8) layer batches of the trace (bounded sample)
+    # the bounded sample decoded every step: the first ceil(cores / batch) layer batches of the first token
+    # step, one record per host thread
     per_step = max(1, min(layers, -(-cores // cfg['batch'])))
-    owners = []
-    for s in range(args.warmup + args.steps):
-        for l in range(per_step):
-            for e in trace[s][(s * per_step + l) % layers][:cfg['batch']]:
-                if ((s * per_step + l) % layers, int(e)) not in owners:
-                    owners.append(((s * per_step + l) % layers, int(e)))
-    blob, experts = build_pool(cfg, owners, threads=cores)
-    by_owner = {(e.layer, e.index): e for e in experts}
+    owners = [(l, int(e)) for l in range(per_step) for e in trace[0][l][:cfg['batch']]]
+    t0 = time.time()
+    made = reference_pool(cfg, owners, cores)
+    if made is None:
+        print(json.dumps({'impl': 'reference', 'unavailable': 'oracle/_ref/wex_nr3_tools.so was not built'}))
+        return 0
+    blob, experts = made
+    log(f'[reference] {len(experts)} records made by the reference tools in {time.time() - t0:.1f} s')
     sys.path.insert(0, os.path.join(ROOT, 'oracle'))
     import ctypes
     import oracle
     L = oracle.ref_lib('wex_nr3_tools')
-    if L is None:
-        print(json.dumps({'impl': 'reference', 'unavailable': 'oracle/_ref/wex_nr3_tools.so was not built'}))
-        return 0
+    outs = [ctypes.create_string_buffer(experts[0].raw) for _ in experts]
 
-    def one(e):
-        out = ctypes.create_string_buffer(e.raw)
-        if L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, out) != 0:
+    def one(i):
+        e = experts[i]
+        if L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, outs[i]) != 0:
             raise RuntimeError('reference decoder refused a record')
         return e.raw
     times, nbytes, nrec = [], 0, 0
     with ThreadPoolExecutor(cores) as pool:
         for s in range(args.warmup + args.steps):
-            recs = [by_owner[((s * per_step + l) % layers, int(e))] for l in range(per_step)
-                    for e in trace[s][(s * per_step + l) % layers][:cfg['batch']]]
             t0 = time.perf_counter()
-            b = sum(pool.map(one, recs))
+            b = sum(pool.map(one, range(len(experts))))
             dt = time.perf_counter() - t0
             if s >= args.warmup:
-                times.append(dt); nbytes += b; nrec += len(recs)
+                times.append(dt); nbytes += b; nrec += len(experts)
     total = sum(times)
     value = nbytes / total / 1e9
     line = {
@@ -482,8 +566,9 @@ def run_reference(args, cfg):
         'experts_per_s': round(nrec / total, 2),
         'config': config_desc(args, cfg, k),
         'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': cores, 'kind': 'reference',
-                         'sample': f'{per_step} layer batch(es) of {cfg["batch"]} records per step, one record per '
-                                   f'host thread, reference wex_nr2_decode'},
+                         'sample': f'{len(experts)} records ({per_step} layer batch(es) of {cfg["batch"]} of the first '
+                                   f'token step) decoded every step, one record per host thread, by the reference '
+                                   f'wex_nr3_decode -> wex_nr2_decode; records made by the reference encoder'},
         'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line))
@@ -1149,6 +1234,31 @@ def measure_h2d(torch, mib=256, reps=5):
     return best
 
 
+def measure_h2d_calls(torch, views, calls, reps=3):
+    """Pinned host-to-device bandwidth (GB/s) of the copies the end-to-end calls issue: each call's records
+    copied one cudaMemcpyAsync each, in call order, into a device buffer of one call's records, on one
+    stream; best of reps over all calls of a step (CUDA events)."""
+    cap = max(sum(len(views[i]) for i in c) for c in calls)
+    dst = torch.empty(cap, dtype=torch.uint8, device='cuda')
+    srcs = [[torch.from_numpy(views[i]) for i in c] for c in calls]
+    total = sum(int(t.numel()) for c in srcs for t in c)
+    best = 0.0
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for c in srcs:
+            at = 0
+            for t in c:
+                n = int(t.numel())
+                dst[at:at + n].copy_(t, non_blocking=True)
+                at += n
+        b.record()
+        torch.cuda.synchronize()
+        best = max(best, total / (a.elapsed_time(b) / 1e3) / 1e9)
+    del dst
+    return best
+
+
 def profile_value(config, key):
     """A figure of the weight kernel's committed ncu summary (a `key: value` line), if there is one."""
     path = os.path.join(ROOT, 'profiles', f'nr3_weights_{config}.md')
@@ -1179,6 +1289,49 @@ def config_desc(args, cfg, records):
             'records_per_step_per_gpu': records,
             'chunks': '2048:512', 'placement': 'expert id mod world size',
             'l2': 'inputs larger than L2 (126 MB) between steps'}
+
+
+def gpu_reference_rate(args, blob, call_args, steps_total, check):
+    """The reference's own CUDA helper (c/tools/wex_cuda_bridge.cu compiled unchanged for sm_100a into
+    oracle/_ref/libwex_cuda_ref.so) on the same pinned records, destinations and calls as the
+    synchronous drop-in form of e2e: per layer one wex_cuda_decode_batch_to_device of `batch` records.
+    A yardstick beside this library on the same GPU, never part of it. Times as many of the timed
+    steps as fit about 20 s (host clock, device synchronised), then checks the sampled slabs with
+    check(). Returns a dict, or one saying why it did not run."""
+    import ctypes
+    import torch
+    path = os.path.join(ROOT, 'oracle', '_ref', 'libwex_cuda_ref.so')
+    if not os.path.exists(path):
+        return {'unavailable': 'oracle/_ref/libwex_cuda_ref.so was not built (make -C oracle gpuref)'}
+    R = ctypes.CDLL(path)
+    P, I = ctypes.c_void_p, ctypes.c_int
+    R.wex_cuda_helper_abi.restype = ctypes.c_uint
+    R.wex_cuda_register_model.argtypes = [P, ctypes.c_size_t]
+    R.wex_cuda_decode_batch_to_device.argtypes = [I, P, P, I, P, P, P]
+    if R.wex_cuda_helper_abi() != 1 or R.wex_cuda_register_model(blob, len(blob)) != 0:
+        return {'unavailable': 'the reference helper refused its ABI check or the model'}
+    dev = torch.cuda.current_device()
+
+    def step(s):
+        bad = 0
+        for ep, rp, sp, wp, st in call_args[s]:
+            bad += R.wex_cuda_decode_batch_to_device(len(st), ep, rp, dev, sp, wp, st)
+        return bad
+    for s in range(args.warmup):
+        assert step(s) == 0, 'the reference helper refused a record'
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert step(args.warmup) == 0
+    torch.cuda.synchronize()
+    first = time.perf_counter() - t0
+    n = max(1, min(args.steps, int(20.0 / max(first, 1e-6))))
+    t0 = time.perf_counter()
+    for s in range(args.warmup, args.warmup + n):
+        assert step(s) == 0
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    ok = check(args.warmup + n - 1)
+    return {'steps': n, 'seconds': dt, 'verified': ok}
 
 
 def run_gpu(args, cfg):
@@ -1224,6 +1377,10 @@ def run_gpu(args, cfg):
     h2d_gbs = measure_h2d(torch)
     barrier(world)
     h2d_together = min_over_ranks(measure_h2d(torch), world) if world > 1 else h2d_gbs   # every rank copying at once
+    # the same link with the copies the end-to-end calls make (a call's records, one copy each), every rank at once
+    step_calls = [step_idx[0][c:c + cfg['batch']] for c in range(0, k, cfg['batch'])]
+    barrier(world)
+    h2d_calls = min_over_ranks(measure_h2d_calls(torch, views, step_calls), world)
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     kernel_ms, launches = [], 0
@@ -1401,10 +1558,13 @@ def run_gpu(args, cfg):
                          'ms_per_step': round(1e3 * sync_s / args.steps, 3),
                          'samples_ms_per_step': [round(1e3 * t / args.steps, 3) for t in sync_runs]},
                 'roofline': {'bound': 'h2d', 'achieved': round(h2d_per_step / e2e_step_s / 1e9, 2),
-                             'peak': round(h2d_together, 2), 'unit': 'GB/s (stored bytes per GPU)',
-                             'frac': round(h2d_per_step / e2e_step_s / 1e9 / h2d_together, 4),
-                             'peak_source': 'measured here: one pinned 256 MiB host-to-device copy, best of 5, '
-                                            'every rank copying at once (the slowest rank)',
+                             'peak': round(h2d_calls, 2), 'unit': 'GB/s (stored bytes per GPU)',
+                             'frac': round(h2d_per_step / e2e_step_s / 1e9 / h2d_calls, 4),
+                             'peak_source': 'measured here: the copies of one step\'s calls (each record one '
+                                            'pinned cudaMemcpyAsync, in call order), best of 3, every rank copying '
+                                            'at once (the slowest rank)',
+                             'peak_one_copy': round(h2d_together, 2),
+                             'frac_of_one_copy': round(h2d_per_step / e2e_step_s / 1e9 / h2d_together, 4),
                              'peak_one_gpu': round(h2d_gbs, 2),
                              'hbm_frac': round(hbm_bytes / e2e_step_s / 1e9 / hbm_peak, 4)}},
         'value_roofline': {'bound': 'hbm', 'achieved': round(hbm_bytes / step_s / 1e9, 2), 'peak': hbm_peak, 'unit': 'GB/s',
@@ -1445,6 +1605,29 @@ def run_gpu(args, cfg):
                                         'experts_per_s': round(fn / fdt, 2),
                                         'sample': f'{fn} records, one per host thread: the reference fast decoder '
                                                   f'(wex4_tools built with WEX4_FAST_NR3, SHA-256 checked), {fdt:.1f} s'}
+    if rank == 0 and world == 1 and not args.no_gpu_reference:
+        def check_step(s):   # the sampled slabs of step s against the source digests
+            got_ = dst[check].cpu().numpy()
+            ids = step_idx[s]
+            return all(hashlib.sha256(got_[n].tobytes()).digest() == experts[ids[j]].expected_sha
+                       for n, j in enumerate(check))
+        dst.fill_(0xA5)
+        g = gpu_reference_rate(args, blob, call_args, steps_total, check_step)
+        if 'steps' in g:
+            gb = sum(experts[i].raw for s in range(args.warmup, args.warmup + g['steps']) for i in step_idx[s])
+            line['gpu_reference'] = {
+                'value': round(gb / g['seconds'] / 1e9, 3), 'unit': 'GB/s',
+                'experts_per_s': round(k * g['steps'] / g['seconds'], 1),
+                'ms_per_step': round(1e3 * g['seconds'] / g['steps'], 3), 'steps': g['steps'],
+                'verified_slabs': g['verified'],
+                'api': f'the reference CUDA helper (c/tools/wex_cuda_bridge.cu, compiled unchanged for sm_100a): '
+                       f'wex_cuda_decode_batch_to_device, {B} records per call, {ncalls} calls per step, from the '
+                       f'same pinned records into the same destinations',
+                'vs': {'e2e_sync': round(e2e_sync / (gb / g['seconds'] / 1e9), 3),
+                       'e2e': round(e2e / (gb / g['seconds'] / 1e9), 3)}}
+            assert g['verified'], 'the reference helper decoded different bytes'
+        else:
+            line['gpu_reference'] = g
     res.close()
     if rank == 0:
         print(json.dumps(line))
@@ -1460,10 +1643,12 @@ def main():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', choices=['wexb', 'reference'], default='wexb')
-    ap.add_argument('--config', choices=sorted(CONFIGS), default='mid')
+    ap.add_argument('--config', choices=sorted(CONFIGS), default='large')
     ap.add_argument('--layers', type=int, default=0, help='layers per step (default: all of the config)')
     ap.add_argument('--cpu-seconds', type=float, default=12.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-gpu-reference', action='store_true',
+                    help='skip the reference CUDA helper timed beside this library (1 GPU)')
     ap.add_argument('--depth', type=int, default=3, help='e2e: batch calls kept in flight')
     args = ap.parse_args()
     assert args.warmup >= 1

@@ -46,9 +46,12 @@ int wex4_bp_encode_record(const unsigned char *data, uint32_t decoded, uint32_t 
                           uint32_t transform, uint32_t owner, unsigned char *out, size_t capacity, size_t *written);
 int wex4_bp_decode_record(const unsigned char *record, size_t total, uint32_t decoded, uint32_t owner,
                           unsigned char *out);
-/* Test tooling of the reference (guard pages, mutation fuzzing, an engine store on disk), not part of
- * the decode path: they return WEX4_E_UNSUPPORTED (-15) (wex4/wex4_tools.c:170-178, :250-312, :317-348). */
+/* wex4_check on a copy of the file that ends right before an inaccessible page, so that a host read past
+ * the end faults instead of passing silently (wex4/wex4_tools.c:170-178; the reference also guard-pages
+ * its host decode buffer: here the decoded bytes are in device memory). Same return values. */
 int wex4_fuzz_check(const unsigned char *file, uint64_t len, int flags, unsigned char *digest);
+/* Test tooling of the reference (mutation fuzzing, an engine store on disk), not part of the decode
+ * path: they return WEX4_E_UNSUPPORTED (-15) (wex4/wex4_tools.c:250-312, :317-348). */
 int wex4_fuzz_run(const unsigned char *file, uint64_t len, uint64_t seed, uint32_t iterations, int mode,
                   uint64_t *counts);
 int wex4_store_probe(const char *path, const unsigned char *root, unsigned char *out, uint64_t capacity,

@@ -69,18 +69,34 @@ void wexb_resident_destroy(WexbResident *r);
  * in the library, held by every device that loads the library until the process exits. Limits:
  * records of at most 24 MiB stored and 24 MiB decoded and 32,768 streams (larger ones return -2 with
  * a message on stderr), at most 4 models per device (a fifth returns 1). The first call on a device
- * sets that device up (looks up the array's address) and should come before any stream capture there.
- * Calls are synchronous and serialised by a process-wide lock; calls that overlapped on the GPU would
- * race on the shared array. Returns 0, -1 invalid (destination untouched), 1 unavailable, -2 too large. */
+ * sets that device up (looks up the array's address, creates the stream its calls run on) and the first
+ * call with a model on a device copies that model's tables into the array; both synchronise with the
+ * device and should come before any stream capture there. Calls are synchronous and serialised by a
+ * process-wide lock; calls that overlapped on the GPU would race on the shared array. The wait for the
+ * decode is bounded (wexb_set_wait_limit): after a wait that gave up, calls on that device return 1
+ * until the decode still using the array has ended. The caller's current device is restored. Returns
+ * 0, -1 invalid (destination untouched), 1 unavailable, -2 too large. */
 int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned char *record, int device,
                                   unsigned char *const *dst_scale, unsigned char *const *dst_weight);
 
 /* Self-test of the bounded waits. Every kernel waits on its shared-memory mbarriers for at most a fixed
- * number of polls, then sets error bit 16 in the record's error word and returns: it never spins
- * forever. This runs the same wait, limited to `polls` polls, on a barrier that completes and on one
- * that nothing arrives on; *bits receives the second one's error bits (16). Returns 0 when the first
- * completes and the second gives up, -1 otherwise or for bad arguments, 1 when CUDA is unavailable. */
+ * number of polls (2^24), then sets error bit 16 in the record's error word and returns: it never spins
+ * forever. This runs the same wait, limited to `polls` polls (1 .. 2^24; more is refused with -1), on a
+ * barrier that completes and on one that nothing arrives on; *bits receives the second one's error bits
+ * (16). The host waits for the probe under the library's wait limit (wexb_set_wait_limit). Returns 0
+ * when the first completes and the second gives up, -1 otherwise or for bad arguments, 1 when CUDA is
+ * unavailable, when the host's wait gave up before the probe ended (the probe then ends on its own),
+ * or while the previous probe on that device is still running. */
 int wexb_selftest_bounded_wait(int device, unsigned int polls, unsigned int *bits);
+
+/* Host waits. No entry point of this library blocks on the GPU without a limit: each polls its CUDA
+ * event or stream until the work ends or `seconds` pass (default 60, or WEXB_WAIT_SECONDS at load),
+ * and a call whose wait gave up returns status 1 ("unavailable, decode again") for the records it had
+ * queued. Their GPU work may still be running: the buffers it uses are not handed to another call
+ * until it ends, and a device destination may still be written afterwards by that work's error-gated
+ * commit (with correct bytes only). Returns 0, or -1 for a limit outside (0, 86400]. */
+int wexb_set_wait_limit(double seconds);
+double wexb_wait_limit(void);
 
 /* Error bits of the last failed record seen by this process (1 structure, 2 stream hash, 4 ceil form
  * at scale 0, 8 canonical zero, 16 bounded wait expired); 0 if none failed. */

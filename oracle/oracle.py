@@ -11,6 +11,10 @@ import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_DIR = os.path.join(HERE, '_ref')
+# Where the reference tree is read from when it is present (this recipe's build of oracle/_ref and the
+# tests that read its vectors); WEXB_REFERENCE overrides it. Absent on hosts that only run the prebuilt
+# checkers.
+REFERENCE = os.environ.get('WEXB_REFERENCE', '/root/reference')
 P, U32, U64, SZ, I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_int
 
 _lib = None
@@ -19,9 +23,10 @@ _lib = None
 def build():
     """Compile liboracle.so (and the reference tools when the reference sources are present)."""
     subprocess.run(['make', '-s', '-C', HERE], check=True)
-    ref = os.environ.get('WEXB_REFERENCE', '/root/reference')
-    if os.path.isdir(ref):
-        subprocess.run(['make', '-s', '-C', HERE, 'ref', f'REF={ref}'], check=True)
+    if os.path.isdir(REFERENCE):
+        subprocess.run(['make', '-s', '-C', HERE, 'ref', f'REF={REFERENCE}'], check=True)
+        if os.path.exists(os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')):
+            subprocess.run(['make', '-s', '-C', HERE, 'gpuref', f'REF={REFERENCE}'], check=True)
 
 
 def lib():
@@ -101,6 +106,7 @@ def ref_lib(name):
     if L is not None and name.startswith('wex4_tools'):
         L.wex4_tools_abi.restype = U32
         L.wex4_check.argtypes = [P, U64, I, P]
+        L.wex4_fuzz_check.argtypes = [P, U64, I, P]
         L.wex4_validate.argtypes = [P, U64, P, SZ]
         L.wex4_decode_record_buf.argtypes = [P, U64, P, SZ, U32, P, P, I, P]
         L.wex4_expert_table.argtypes = [P, U64, P, SZ, P]

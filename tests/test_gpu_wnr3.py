@@ -328,6 +328,40 @@ def test_bounded_wait_gives_up_and_the_context_stays_usable(torch_cuda, tiny):
     assert bad == 0 and all(_slab(ts, j) == e.expected for j, e in enumerate(ex))
 
 
+def test_host_wait_gives_up_before_a_long_device_wait(torch_cuda, tiny):
+    """Every host wait of the library is bounded (wexb_set_wait_limit). With a host limit shorter than a
+    device-side bounded wait, the self-test call returns 1 (host gave up) while its probe still polls; the
+    probe then gives up on its own, the device stays usable, and a decode afterwards is bit-exact."""
+    import time
+    default = wexcuda.wait_limit()
+    assert wexcuda.set_wait_limit(0) == -1 and wexcuda.set_wait_limit(-1) == -1
+    assert wexcuda.selftest_bounded_wait(0, (1 << 24) + 1)[0] == -1   # above the kernels' own limit
+    t = time.perf_counter()
+    assert wexcuda.selftest_bounded_wait(0, 1 << 16) == (0, 16)
+    per_poll = (time.perf_counter() - t) / (1 << 16)
+    polls = min(1 << 24, max(1 << 16, int(0.5 / max(per_poll, 1e-9))))   # about half a second of polling
+    if polls * per_poll < 0.1:
+        pytest.skip(f'2^24 polls take only {polls * per_poll:.3f} s here')
+    try:
+        assert wexcuda.set_wait_limit(0.02) == 0
+        t = time.perf_counter()
+        st, _ = wexcuda.selftest_bounded_wait(0, polls)
+        gave_up = time.perf_counter() - t
+        assert st == 1 and gave_up < 0.5 * polls * per_poll, (st, gave_up)
+    finally:
+        assert wexcuda.set_wait_limit(default) == 0
+    deadline = time.perf_counter() + 60
+    while True:   # 1 while the previous probe still runs, then a clean self-test
+        st, bits = wexcuda.selftest_bounded_wait(0, 2000)
+        if st != 1 or time.perf_counter() > deadline:
+            break
+        time.sleep(0.01)
+    assert (st, bits) == (0, 16)
+    blob, ex = tiny
+    bad, st2, ts = _decode_device(torch_cuda, [e.entry for e in ex], [e.record for e in ex])
+    assert bad == 0 and all(_slab(ts, j) == e.expected for j, e in enumerate(ex))
+
+
 def test_queued_batches(torch_cuda, tiny):
     """wexb_batch_submit / wexb_batch_wait: several batches in flight, one with a damaged and an
     unavailable record; each wait gives the statuses of the synchronous call; tickets are single-use."""

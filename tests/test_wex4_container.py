@@ -14,12 +14,13 @@ import pytest
 import oracle
 import wexcuda
 
-REF_VECTORS = '/root/reference/wex4/vectors'
+REF_VECTORS = os.path.join(oracle.REFERENCE, 'wex4', 'vectors')
 P, U32, U64, SZ, I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_int
 def lib():
     L = wexcuda.lib()
     L.wex4_tools_abi.restype = U32
     L.wex4_check.argtypes = [P, U64, I, P]
+    L.wex4_fuzz_check.argtypes = [P, U64, I, P]
     L.wex4_validate.argtypes = [P, U64, P, SZ]
     L.wex4_decode_record_buf.argtypes = [P, U64, P, SZ, U32, P, P, I, P]
     L.wex4_expert_table.argtypes = [P, U64, P, SZ, P]
@@ -90,6 +91,25 @@ def test_check_without_hashes_matches_reference(golden_dir):
         assert L.wex4_check(data, len(data), 0, None) == ref.wex4_check(data, len(data), 0, None), path
 
 
+def test_guarded_check_without_hashes_matches_reference(golden_dir):
+    """wex4_fuzz_check (the same check on a copy that ends at an inaccessible page) with flags 0, on every
+    vector: the reference's guard-paged verdict, and never a fault from a read past the file's end."""
+    ref = oracle.ref_lib('wex4_tools_ref')
+    L = lib()
+    n = 0
+    for path, data, row in all_vectors(golden_dir):
+        got = L.wex4_fuzz_check(data, len(data), 0, None)
+        assert got == L.wex4_check(data, len(data), 0, None), path
+        if ref is not None:
+            assert got == ref.wex4_fuzz_check(data, len(data), 0, None), path
+        n += 1
+        for cut in (1, 4096):   # truncated copies end at the guard page too
+            if len(data) > cut:
+                assert L.wex4_fuzz_check(data[:-cut], len(data) - cut, 0, None) == \
+                    L.wex4_check(data[:-cut], len(data) - cut, 0, None), (path, cut)
+    assert n >= 25
+
+
 def test_expert_table_matches_reference(golden_dir):
     ref = oracle.ref_lib('wex4_tools_ref')
     if ref is None:
@@ -121,6 +141,9 @@ def test_check_with_hashes_and_decode(golden_dir, flags):
         data = open(os.path.join(golden_dir, 'vectors', name), 'rb').read()
         digest = ctypes.create_string_buffer(32)
         st = L.wex4_check(data, len(data), flags, digest)
+        guarded = ctypes.create_string_buffer(32)
+        assert L.wex4_fuzz_check(data, len(data), flags, guarded) == st, (name, flags)
+        assert guarded.raw == digest.raw, name
         ref = oracle.ref_lib('wex4_tools_ref')
         want = ref.wex4_check(data, len(data), flags, None) if ref is not None else (item['ref_check'] if flags == 3 else None)
         if want is not None:

@@ -71,6 +71,16 @@ def test_noalloc_matches_the_allocating_entry_point():
     # and a clean call right after the refused one
     assert noalloc(ex[0].entry, ex[0].record, 0, [t.data_ptr() for t in got_s], [t.data_ptr() for t in got_w]) == 0
     assert _bytes(got_s) + _bytes(got_w) == ex[0].expected
+    # what the entry point exists for: after the set-up call above, further calls leave the device's
+    # free memory exactly as it was (no allocation of any size, by the library or the runtime)
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info(0)[0]
+    for e in ex * 2:
+        assert noalloc(e.entry, e.record, 0, [t.data_ptr() for t in got_s], [t.data_ptr() for t in got_w]) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(0)[0] == free_before
+    # and the caller's current device is the one it had before the call
+    assert torch.cuda.current_device() == 0
 
 
 def test_noalloc_rejects_records_beyond_its_fixed_size():
@@ -84,3 +94,34 @@ def test_noalloc_rejects_records_beyond_its_fixed_size():
     s, w = _buffers(torch, e.entry)
     assert noalloc(e.entry, e.record, 0, [t.data_ptr() for t in s], [t.data_ptr() for t in w]) == -2
     assert all(bool((t == POISON).all()) for t in s + w)
+
+
+def test_noalloc_holds_at_most_four_models_per_device():
+    """The array has table room for 4 models per device: a model that finds every slot taken is
+    refused with 1 (unavailable) and its destination is left untouched; models already held still decode.
+    Runs last in this file, since it fills the slots; earlier tests (here or in other files) may have
+    taken some, so at most 4 of 5 new models fit and the fifth is refused."""
+    import torch
+    noalloc = _noalloc()
+    got = []
+    experts = []
+    for k in range(5):   # five different models, one small expert each
+        blob, ex = synth.make_experts(1024, 512, [(k, 1)], seed=700 + k, sigma=0.02 + 0.002 * k, train_every=1)
+        assert wexcuda.register_model(blob) == 0
+        e = ex[0]
+        s, w = _buffers(torch, e.entry)
+        st = noalloc(e.entry, e.record, 0, [t.data_ptr() for t in s], [t.data_ptr() for t in w])
+        torch.cuda.synchronize()
+        got.append(st)
+        experts.append((e, st))
+        if st == 0:
+            assert _bytes(s) + _bytes(w) == e.expected
+        else:
+            assert all(bool((t == POISON).all()) for t in s + w)
+    fit = got.count(0)
+    assert got == [0] * fit + [1] * (5 - fit) and 1 <= fit <= 4, got
+    e, _ = experts[0]   # a model that got a slot keeps decoding
+    s, w = _buffers(torch, e.entry)
+    assert noalloc(e.entry, e.record, 0, [t.data_ptr() for t in s], [t.data_ptr() for t in w]) == 0
+    torch.cuda.synchronize()
+    assert _bytes(s) + _bytes(w) == e.expected

@@ -54,7 +54,7 @@ def build_cuda(verbose=False, extra=()):
         return None
     if _stale(CUDA_LIB, deps) or extra:
         os.makedirs(LIB, exist_ok=True)
-        objs = []
+        objs, cmds = [], []
         for src in cuda_sources():
             obj = os.path.join(LIB, os.path.basename(src) + '.o')
             cmd = [NVCC, '-O3', '-std=c++17', '-lineinfo', '-Xcompiler', '-fPIC,-fvisibility=hidden', '-I',
@@ -63,8 +63,16 @@ def build_cuda(verbose=False, extra=()):
                 cmd.insert(1, '-x'); cmd.insert(2, 'cu')
             if verbose:
                 print(' '.join(cmd))
-            subprocess.run(cmd, check=True)
+            cmds.append(cmd)
             objs.append(obj)
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(max(1, min(len(cmds), os.cpu_count() or 4))) as pool:
+            for r in list(pool.map(lambda c: subprocess.run(c, capture_output=True, text=True), cmds)):
+                if r.returncode:
+                    sys.stderr.write(r.stdout + r.stderr)
+                    raise subprocess.CalledProcessError(r.returncode, r.args)
+                if verbose and (r.stdout or r.stderr):
+                    sys.stderr.write(r.stdout + r.stderr)
         cmd = [NVCC, '-shared', *ARCH, '-o', CUDA_LIB, *objs, '-lcudart_static', '-lpthread', '-ldl', '-lrt']
         if verbose:
             print(' '.join(cmd))

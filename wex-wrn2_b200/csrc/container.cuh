@@ -19,5 +19,7 @@ cudaError_t launch_zero_check(const ZeroJob *jobs, uint32_t n, cudaStream_t st);
 // arrival: after `arrivals` arrivals (0 or 1), a wait of at most `polls` polls. bits[0] receives the
 // timeout bit (16) when the wait gave up, else 0.
 cudaError_t launch_wait_probe(uint32_t arrivals, uint32_t polls, uint32_t *bits, cudaStream_t st);
+// The self-test's largest poll count: the kernels' own limit (kWaitPolls, wnr3.cuh).
+constexpr uint32_t kSelftestMaxPolls = 1u << 24;
 
 }  // namespace wexb

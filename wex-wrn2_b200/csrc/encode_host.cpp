@@ -12,6 +12,7 @@
 
 #include "bufs.h"
 #include "encode.cuh"
+#include "host_wait.h"
 #include "nr3_host.h"
 #include "wexb200.h"
 
@@ -63,12 +64,28 @@ struct EncSpace {
     PinBuf hmeta;
     cudaStream_t st[2] = {}, down = nullptr;   // uploads and kernels of groups in turn; downloads
     cudaEvent_t meta_done = nullptr, verdicts[2] = {};
+    bool unsettled = false;   // a bounded wait gave up: the buffers may still be in use on the GPU
     bool ready() {
         for (cudaStream_t *s : {&st[0], &st[1], &down})
             if (!*s && cudaStreamCreateWithFlags(s, cudaStreamNonBlocking) != cudaSuccess) return false;
         for (cudaEvent_t *e : {&meta_done, &verdicts[0], &verdicts[1]})
             if (!*e && cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return false;
+        if (unsettled) {   // reuse the buffers only once the work of the call that gave up has ended
+            for (cudaStream_t s : {st[0], st[1], down})
+                if (cudaStreamQuery(s) != cudaSuccess) { (void)cudaGetLastError(); return false; }
+            unsettled = false;
+        }
         return true;
+    }
+    // Bounded waits for every stream of the space; false (and unsettled on a timeout) unless all ended.
+    bool settle() {
+        bool ok = true;
+        for (cudaStream_t s : {st[0], st[1], down}) {
+            const Waited w = wait_stream(s);
+            if (w == Waited::TimedOut) unsettled = true;
+            ok = ok && w == Waited::Done;
+        }
+        return ok;
     }
 };
 constexpr size_t kGroup = 16;   // records per pipelined group of an encode launch
@@ -199,7 +216,9 @@ WEXB_API int wexb_encode_batch(int n, const WexEntry *const *entries, const unsi
                   cudaStreamWaitEvent(S.st[1], S.meta_done, 0) == cudaSuccess;
         const size_t groups = (k + kGroup - 1) / kGroup;
         auto fetch = [&](size_t gi) {   // group gi's verdicts, then its records' copies back
-            if (cudaEventSynchronize(S.verdicts[gi & 1]) != cudaSuccess) return false;
+            const Waited w = wait_event(S.verdicts[gi & 1]);
+            if (w == Waited::TimedOut) S.unsettled = true;
+            if (w != Waited::Done) return false;
             for (size_t q = gi * kGroup; q < std::min(k, (gi + 1) * kGroup); ++q) {
                 const Job &j = jobs[at + q];
                 const int64_t st = (int64_t)hres[3 * q];
@@ -227,8 +246,7 @@ WEXB_API int wexb_encode_batch(int n, const WexEntry *const *entries, const unsi
             if (cuda_ok && gi) cuda_ok = fetch(gi - 1);
         }
         if (cuda_ok && groups) cuda_ok = fetch(groups - 1);
-        cuda_ok = cuda_ok && cudaStreamSynchronize(S.st[0]) == cudaSuccess && cudaStreamSynchronize(S.st[1]) == cudaSuccess &&
-                  cudaStreamSynchronize(S.down) == cudaSuccess;
+        cuda_ok = S.settle() && cuda_ok;   // also after a failed step: what was queued must end first
         if (!cuda_ok)
             for (size_t q = 0; q < k; ++q) status[jobs[at + q].i] = -2;
         at = end;
@@ -307,8 +325,8 @@ WEXB_API int wexb_count_batch(int n, const WexEntry *const *entries, const unsig
         for (size_t q = 0; ok && q < k; ++q)
             ok = cudaMemcpyAsync(S.slabs.p + slab_at[q], coded[jobs[at + q].i], jobs[at + q].L.raw, cudaMemcpyHostToDevice,
                                  S.st[0]) == cudaSuccess;
-        ok = ok && launch_count(drec, (uint32_t)k, dtask, (uint32_t)tasks.size(), dwc, dsc, S.st[0]) == cudaSuccess &&
-             cudaStreamSynchronize(S.st[0]) == cudaSuccess;   // the slabs and metadata are reused by the next launch
+        ok = ok && launch_count(drec, (uint32_t)k, dtask, (uint32_t)tasks.size(), dwc, dsc, S.st[0]) == cudaSuccess;
+        ok = S.settle() && ok;   // the slabs and metadata are reused by the next launch
         at = end;
     }
     std::vector<unsigned long long> hwc(3 * kEncContexts * 16), hsc(3 * 256);

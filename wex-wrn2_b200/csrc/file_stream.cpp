@@ -28,6 +28,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "host_wait.h"
 #include "nr3_host.h"
 #include "wex4_index.h"
 #include "wexb200.h"
@@ -97,6 +98,9 @@ struct WexbFile {
     int device = -1;
     cudaStream_t raw_st = nullptr;
     cudaEvent_t raw_done[kSlots] = {};
+    // A bounded wait for a slot's uploads gave up: the GPU may still read the ring, so no later call
+    // reuses it (every record then reports 1).
+    bool stuck = false;
 
     void reader_loop() {
         for (;;) {
@@ -333,7 +337,7 @@ WEXB_API int wexb_file_decode(WexbFile *f, int device, int n, const unsigned int
     if (!n) return 0;
     std::lock_guard<std::mutex> lock(f->call_mu);
     Work w = resolve(*f, n, layer, expert, status);
-    if (!w.rec.empty() && (!f->alloc_ring() || !f->bind(device))) {
+    if (!w.rec.empty() && (f->stuck || !f->alloc_ring() || !f->bind(device))) {
         for (int i : w.who) status[i] = 1;
         w.rec.clear();
     }
@@ -350,6 +354,7 @@ WEXB_API int wexb_file_decode(WexbFile *f, int device, int n, const unsigned int
         ticket[b] = -1;
     };
     for (size_t b = 0; b < nb && b < (size_t)kSlots; ++b) f->issue((int)(b % kSlots), &w.rec[b * kBatch], w.size(b));
+    size_t issued = std::min(nb, (size_t)kSlots), done_at = nb;
     for (size_t b = 0; b < nb; ++b) {
         const int s = (int)(b % kSlots), k = w.size(b);
         f->wait_reads(s);
@@ -386,15 +391,29 @@ WEXB_API int wexb_file_decode(WexbFile *f, int device, int n, const unsigned int
             if (ticket[b] < 0) { for (int i : queued[b]) status[i] = 1; queued[b].clear(); }
         }
         if (cudaEventRecord(f->raw_done[s], f->raw_st) != cudaSuccess) { (void)cudaGetLastError(); raw_ok = false; }
-        if (b + kSlots < nb) {   // the slot is read again once its uploads have landed
-            if (ticket[b] >= 0 && !batch_uploads_wait(ticket[b])) retire(b);
-            if (cudaEventSynchronize(f->raw_done[s]) != cudaSuccess) { (void)cudaGetLastError(); raw_ok = false; }
+        if (b + kSlots < nb) {   // the slot is read again once its uploads have landed (bounded waits)
+            const bool uploaded = ticket[b] < 0 || batch_uploads_wait(ticket[b]);
+            const Waited copied = wait_event(f->raw_done[s]);
+            if (copied != Waited::Done) raw_ok = false;
+            if (!uploaded || copied != Waited::Done) {   // the slot may still be read: stop here
+                f->stuck = true;
+                done_at = b + 1;
+                break;
+            }
             f->issue(s, &w.rec[(b + kSlots) * kBatch], w.size(b + kSlots));
+            ++issued;
         }
         if (b >= (size_t)kInflight) retire(b - kInflight);
     }
+    for (size_t b = done_at; b < issued; ++b) f->wait_reads((int)(b % kSlots));   // reads already handed out
+    for (size_t b = done_at; b < nb; ++b)
+        for (int j = 0; j < w.size(b); ++j) status[w.who[b * kBatch + (size_t)j]] = 1;
     for (size_t b = 0; b < nb; ++b) retire(b);
-    if (!raw.empty() && cudaStreamSynchronize(f->raw_st) != cudaSuccess) { (void)cudaGetLastError(); raw_ok = false; }
+    if (!raw.empty()) {
+        const Waited copied = wait_stream(f->raw_st);
+        if (copied == Waited::TimedOut) f->stuck = true;
+        if (copied != Waited::Done) raw_ok = false;
+    }
     for (int i : raw) status[i] = raw_ok ? 0 : 1;
     int bad = 0;
     for (int i = 0; i < n; ++i) bad += status[i] != 0;

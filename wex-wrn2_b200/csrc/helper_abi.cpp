@@ -20,79 +20,16 @@
 
 #include "bufs.h"
 #include "container.cuh"
+#include "host_wait.h"
 #include "nr3_host.h"
 #include "wex_cuda_helper.h"
+#include "workspace.h"
 #include "wexb200.h"
 
 #define WEXB_API extern "C" __attribute__((visibility("default")))
 
 namespace wexb {
 namespace {
-
-// Kernel streams per device, handed to calls in turn, so that the kernels of consecutive queued
-// calls may overlap.
-constexpr int kLanes = 4;
-
-// The streams of a device, shared by every call on it: uploads in call order on `upload`, each
-// call's kernels and read-back on the next kernel stream. Created once, never destroyed (CUDA
-// cannot be called while the process unloads).
-struct Queues {
-    cudaStream_t upload = nullptr, lane[kLanes] = {};
-    unsigned next = 0;
-    bool ok = false;
-};
-std::mutex g_queues_mu;
-Queues g_queues[kMaxDevices];
-
-// The device's upload stream and the kernel stream of a new call (device current).
-bool device_streams(int device, cudaStream_t *up, cudaStream_t *st) {
-    std::lock_guard<std::mutex> lock(g_queues_mu);
-    Queues &q = g_queues[device];
-    if (!q.ok) {
-        bool ok = cudaStreamCreateWithFlags(&q.upload, cudaStreamNonBlocking) == cudaSuccess;
-        for (int l = 0; ok && l < kLanes; ++l) ok = cudaStreamCreateWithFlags(&q.lane[l], cudaStreamNonBlocking) == cudaSuccess;
-        if (!ok) { (void)cudaGetLastError(); return false; }   // streams made so far leak, on CUDA failure only
-        q.ok = true;
-    }
-    *up = q.upload;
-    *st = q.lane[q.next];
-    q.next = (q.next + 1u) % kLanes;
-    return true;
-}
-
-// A call's workspace: events and grown buffers. Pooled per device and never freed (the reference's
-// pools, c/tools/wex_cuda_bridge.cu:111-153, for the same reason). A queued call holds its
-// workspace until it is waited for.
-struct Workspace {
-    int device = -1;
-    cudaEvent_t uploads_done = nullptr, done = nullptr;
-    DevBuf drec, dscratch, dmeta;
-    PinBuf hmeta;
-    bool init(int dev) {
-        if (cudaEventCreateWithFlags(&uploads_done, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&done, cudaEventDisableTiming) != cudaSuccess) return false;
-        device = dev;
-        return true;
-    }
-};
-
-std::mutex g_pool_mu;
-std::vector<Workspace *> g_idle[kMaxDevices];
-
-Workspace *take(int device) {
-    {
-        std::lock_guard<std::mutex> lock(g_pool_mu);
-        if (!g_idle[device].empty()) { Workspace *w = g_idle[device].back(); g_idle[device].pop_back(); return w; }
-    }
-    Workspace *w = new (std::nothrow) Workspace();
-    if (w && !w->init(device)) { (void)cudaGetLastError(); delete w; w = nullptr; }   // streams leak only on CUDA failure
-    return w;
-}
-void give(Workspace *w) {
-    if (!w) return;
-    std::lock_guard<std::mutex> lock(g_pool_mu);
-    g_idle[w->device].push_back(w);
-}
 
 // Byte layout of a call's metadata block (host pinned, copied to the device in one piece).
 struct MetaLayout {
@@ -122,6 +59,7 @@ struct Call {
     std::vector<size_t> scr_off;
     Workspace *w = nullptr;
     size_t k = 0, broken_at = 0;
+    bool unsettled = false;   // a bounded wait during submit gave up: the workspace may still be in use
     MetaLayout L;
     int failures() const { int bad = 0; for (int v : status) bad += v != 0; return bad; }
     void settle(int v) { for (int &s : status) if (s == kPending) s = v; }
@@ -163,7 +101,7 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     }
     const size_t k = c.k = c.pend.size();
     if (!k) return false;
-    Workspace *w = c.w = take(device);
+    Workspace *w = c.w = workspace_take(device);
     if (!w) { c.settle(1); return false; }
     // layout
     const int wthreads = weight_threads();
@@ -181,7 +119,7 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     MetaLayout &L = c.L;
     L.compute(k, stasks.size(), wtasks.size(), host_dst ? 0 : k, noffs);
     if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total)) {
-        c.settle(1); give(w); c.w = nullptr; return false;
+        c.settle(1); workspace_give(w, true); c.w = nullptr; return false;
     }
     uint8_t *hm = w->hmeta.p, *dm = w->dmeta.p;
     Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + L.recs);
@@ -215,7 +153,7 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     // enqueue: metadata and records on the upload stream; then, on the call's kernel stream, the
     // three kernels (every record of the call in one grid each) and the read-back of the error words
     cudaStream_t up = nullptr, st = nullptr;
-    if (!device_streams(device, &up, &st)) { c.settle(1); give(w); c.w = nullptr; return false; }
+    if (!device_streams(device, &up, &st)) { c.settle(1); workspace_give(w, true); c.w = nullptr; return false; }
     bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, up) == cudaSuccess;
     for (size_t j = 0; ok && j < k; ++j)
         ok = cudaMemcpyAsync(w->drec.p + rec_off[j], records[c.pend[j]], c.plans[(size_t)c.pend[j]].total,
@@ -223,7 +161,7 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     // the kernel stream waits for every upload, so `done`, recorded on it last, covers the whole call
     if (cudaEventRecord(w->uploads_done, up) != cudaSuccess || cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess) {
         (void)cudaGetLastError();
-        (void)cudaStreamSynchronize(up);
+        if (wait_stream(up) == Waited::TimedOut) c.unsettled = true;
         ok = false;
     }
     if (ok)
@@ -243,23 +181,24 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     if (cudaMemcpyAsync(herrs, derrs, k * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
         cudaEventRecord(w->done, st) != cudaSuccess) {
         (void)cudaGetLastError();
-        (void)cudaStreamSynchronize(st);
+        if (wait_stream(st) == Waited::TimedOut) c.unsettled = true;
         c.broken_at = 0;
     }
     return true;
 }
 
-// Waits for a submitted call, writes its statuses, releases its workspace.
+// Waits (bounded) for a submitted call, writes its statuses, releases its workspace. A call whose wait
+// gives up reports status 1 for its records and parks its workspace.
 void finish(Call &c) {
     Workspace *w = c.w;
     if (!w) { c.settle(1); return; }
     (void)cudaSetDevice(c.device);
-    const bool synced = cudaEventSynchronize(w->done) == cudaSuccess;
-    if (!synced) (void)cudaGetLastError();
+    const Waited waited = c.unsettled ? Waited::TimedOut : wait_event(w->done);
+    const bool synced = waited == Waited::Done;
     const uint32_t *herrs = reinterpret_cast<const uint32_t *>(w->hmeta.p + c.L.errs);
     for (size_t j = 0; j < c.k; ++j) {
         const int i = c.pend[j];
-        c.status[(size_t)i] = (j >= c.broken_at || !synced) ? 1 : herrs[j] ? -1 : 0;
+        c.status[(size_t)i] = (j >= c.broken_at || !synced) ? 1 : status_of_bits(herrs[j]);
         if (c.status[(size_t)i] == -1) report_error_bits(herrs[j]);
     }
     if (c.mode == Dest::HostChecked && synced) {   // the single to-host call: copy back only a clean decode
@@ -275,7 +214,7 @@ void finish(Call &c) {
             }
         }
     }
-    give(w);
+    workspace_give(w, synced);
     c.w = nullptr;
 }
 
@@ -361,19 +300,58 @@ WEXB_API int wex_cuda_host_unregister(void *pointer) {
     return 0;
 }
 
+namespace wexb {
+namespace {
+// Per device, for the self-test: two result words (device), their page-locked copy, a stream and an
+// event. Made once and kept, so a call whose host wait gave up never frees memory its probe may still
+// write; the next call refuses (1) until that probe has ended.
+struct ProbeSpace {
+    uint32_t *dev = nullptr, *host = nullptr;
+    cudaStream_t st = nullptr;
+    cudaEvent_t done = nullptr;
+    bool ok = false;
+};
+std::mutex g_probe_mu;
+ProbeSpace g_probe[kMaxDevices];
+}  // namespace
+}  // namespace wexb
+
 WEXB_API int wexb_selftest_bounded_wait(int device, unsigned int polls, unsigned int *bits) {
-    if (!bits || !polls || device < 0 || device >= kMaxDevices) return -1;
+    if (!bits || !polls || polls > kSelftestMaxPolls || device < 0 || device >= kMaxDevices) return -1;
+    KeepDevice keep;
     if (cudaSetDevice(device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
-    uint32_t *d = nullptr, h[2] = {~0u, ~0u};
-    bool ok = cudaMalloc(&d, sizeof h) == cudaSuccess &&
-              launch_wait_probe(1, polls, d, nullptr) == cudaSuccess &&       // a barrier that completes
-              launch_wait_probe(0, polls, d + 1, nullptr) == cudaSuccess &&   // one that nothing arrives on
-              cudaMemcpy(h, d, sizeof h, cudaMemcpyDeviceToHost) == cudaSuccess;
-    if (d) cudaFree(d);
-    if (!ok) { (void)cudaGetLastError(); return 1; }
-    *bits = h[1];
-    return h[0] == 0 && h[1] == kErrTimeout ? 0 : -1;
+    std::lock_guard<std::mutex> lock(g_probe_mu);
+    ProbeSpace &P = g_probe[device];
+    if (!P.ok) {
+        if (cudaMalloc(&P.dev, 8) != cudaSuccess || cudaMallocHost(&P.host, 8) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&P.st, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&P.done, cudaEventDisableTiming) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return 1;   // whatever was made stays allocated; nothing is retried on a failing device
+        }
+        P.ok = true;
+    } else if (cudaEventQuery(P.done) != cudaSuccess) {   // the previous probe has not ended yet
+        (void)cudaGetLastError();
+        return 1;
+    }
+    P.host[0] = P.host[1] = ~0u;
+    const bool queued = launch_wait_probe(1, polls, P.dev, P.st) == cudaSuccess &&       // a barrier that completes
+                        launch_wait_probe(0, polls, P.dev + 1, P.st) == cudaSuccess &&   // one that nothing arrives on
+                        cudaMemcpyAsync(P.host, P.dev, 8, cudaMemcpyDeviceToHost, P.st) == cudaSuccess &&
+                        cudaEventRecord(P.done, P.st) == cudaSuccess;
+    if (!queued) { (void)cudaGetLastError(); return 1; }
+    if (wait_event(P.done) != Waited::Done) return 1;   // the host gave up first: the probe ends on its own
+    *bits = P.host[1];
+    return P.host[0] == 0 && P.host[1] == kErrTimeout ? 0 : -1;
 }
+
+WEXB_API int wexb_set_wait_limit(double seconds) {
+    if (!(seconds > 0) || seconds > 86400.0) return -1;
+    set_wait_limit(seconds);
+    return 0;
+}
+
+WEXB_API double wexb_wait_limit(void) { return wait_limit(); }
 
 WEXB_API int wexb_batch_submit(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
                                unsigned char *const *dst_scale, unsigned char *const *dst_weight) {
@@ -415,8 +393,8 @@ bool batch_uploads_wait(int t) {
         if (!c->w) return true;   // nothing was queued
         e = c->w->uploads_done; device = c->device;
     }
-    if (cudaSetDevice(device) != cudaSuccess || cudaEventSynchronize(e) != cudaSuccess) { (void)cudaGetLastError(); return false; }
-    return true;
+    if (cudaSetDevice(device) != cudaSuccess) { (void)cudaGetLastError(); return false; }
+    return wait_event(e) == Waited::Done;
 }
 }  // namespace wexb
 
@@ -429,6 +407,7 @@ struct ResSlot {
     cudaEvent_t done = nullptr;
     cudaEvent_t marks[4] = {};
     bool timed = false;
+    bool stale = false;   // its wait gave up: the GPU may still be using it until `done` completes
     int k = 0;
 };
 // Two decodes may be queued at once: the host plans the next one while the GPU runs the previous one.
@@ -511,12 +490,15 @@ namespace {
 // nullptr-safe counts. Returns the number of non-zero statuses.
 int resident_retire(WexbResident *r, int *status) {
     ResSlot &q = r->slot[r->head];
-    const bool ok = cudaSetDevice(r->device) == cudaSuccess && cudaEventSynchronize(q.done) == cudaSuccess;
-    if (!ok) (void)cudaGetLastError();
+    Waited waited = Waited::Failed;
+    if (cudaSetDevice(r->device) == cudaSuccess) waited = wait_event(q.done);
+    else (void)cudaGetLastError();
+    const bool ok = waited == Waited::Done;
+    q.stale = waited == Waited::TimedOut;
     const uint32_t *herrs = reinterpret_cast<const uint32_t *>(q.hmeta.p + q.L.errs);
     int bad = 0;
     for (int j = 0; j < q.k; ++j) {
-        const int v = !ok ? 1 : herrs[j] ? -1 : 0;
+        const int v = !ok ? 1 : status_of_bits(herrs[j]);
         if (v == -1) report_error_bits(herrs[j]);
         if (status) status[j] = v;
         bad += v != 0;
@@ -539,6 +521,10 @@ WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsi
     if (r->queued == 2) (void)resident_retire(r, nullptr);   // both slots busy: the oldest decode's statuses are dropped
     const int si = (r->head + r->queued) & 1;
     ResSlot &q = r->slot[si];
+    if (q.stale) {   // an earlier wait on this slot gave up: reuse it only once its work has ended
+        if (cudaEventQuery(q.done) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+        q.stale = false;
+    }
     cudaStream_t st = stream ? (cudaStream_t)stream : r->own;
     const int wthreads = weight_threads();
     std::vector<Nr3Task> stasks, wtasks;
@@ -616,16 +602,23 @@ WEXB_API int wexb_resident_kernel_ms(const WexbResident *r, float *ms3) {
 
 WEXB_API void wexb_resident_destroy(WexbResident *r) {
     if (!r) return;
-    if (r->device >= 0 && cudaSetDevice(r->device) == cudaSuccess) {
-        if (r->own) cudaStreamSynchronize(r->own);
-        for (ResSlot &q : r->slot) {
-            if (q.done) { cudaEventSynchronize(q.done); cudaEventDestroy(q.done); }
-            for (auto &e : q.marks) if (e) cudaEventDestroy(e);
-            q.dscratch.release(); q.dmeta.release(); q.hmeta.release();
+    if (r->device >= 0) {
+        KeepDevice keep;
+        if (cudaSetDevice(r->device) == cudaSuccess) {
+            // bounded: if queued work does not end, the device memory it may use is left allocated
+            bool ended = !r->own || wait_stream(r->own) == Waited::Done;
+            for (ResSlot &q : r->slot) if (q.done) ended = wait_event(q.done) == Waited::Done && ended;
+            for (ResSlot &q : r->slot) {
+                if (q.done) cudaEventDestroy(q.done);
+                for (auto &e : q.marks) if (e) cudaEventDestroy(e);
+                if (ended) { q.dscratch.release(); q.dmeta.release(); q.hmeta.release(); }
+            }
+            if (ended) {
+                if (r->own) cudaStreamDestroy(r->own);
+                r->store.release();
+            }
         }
-        if (r->own) cudaStreamDestroy(r->own);
-        r->store.release();
+        (void)cudaGetLastError();
     }
-    (void)cudaGetLastError();
     delete r;
 }

@@ -17,14 +17,20 @@
 //
 // In host code `g_na_scratch` is only a host-side stand-in for the device array, never a device
 // address: the first call on each device, with that device current, asks the runtime for the real
-// address (cudaGetSymbolAddress) and every pointer given to a kernel is derived from it. That set-up
-// call should therefore come before any stream capture on that device.
+// address (cudaGetSymbolAddress), creates the non-blocking stream its calls run on, and every pointer
+// given to a kernel is derived from that address. That set-up call, and the first call that uses a
+// model on a device (it copies the model's tables into the array with a synchronous cudaMemcpy),
+// synchronise with the device; they should therefore come before any stream capture on that device.
+// The call waits for its decode under the library's host wait limit; if that wait gives up it returns 1,
+// and later calls on the device return 1 until the decode still using the array has ended. The caller's
+// current device is restored on return.
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstdio>
 #include <mutex>
 
+#include "host_wait.h"
 #include "nr3_host.h"
 #include "wex_cuda_helper.h"
 #include "wexb200.h"
@@ -57,9 +63,14 @@ static __device__ __align__(256) uint8_t g_na_scratch[kNaBytes];
 
 std::mutex g_na_mu;
 uint8_t *g_na_base[kMaxDevices];                 // device address of g_na_scratch, per device
+cudaStream_t g_na_stream[kMaxDevices];           // the stream the calls on each device run on
 uint32_t g_na_slot[kMaxDevices][kNaModels];      // model id held by each table slot (0 = free)
 alignas(256) uint8_t g_na_host[kNaMeta];         // host image of the per-call metadata
-uint32_t g_na_error;
+// The record's error word is read back into this page, page-locked once per process at the first set-up
+// (cudaHostRegister of static memory, no allocation): a read-back into pageable memory would block the
+// host until the decode ends, outside the bounded wait.
+alignas(4096) uint32_t g_na_word[1024];
+bool g_na_word_locked = false;
 
 }  // namespace
 }  // namespace wexb
@@ -82,13 +93,28 @@ WEXB_API int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned
     const uint8_t *image = model_image(p.model_id);
     if (!image || device < 0 || device >= kMaxDevices) return 1;
     std::lock_guard<std::mutex> lock(g_na_mu);
+    KeepDevice keep;
     if (cudaSetDevice(device) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
     if (!g_na_base[device]) {   // set-up, once per device, with that device current
         void *ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_na_scratch) != cudaSuccess || !ptr) { (void)cudaGetLastError(); return 1; }
         if (prepare_nr3_kernels() != cudaSuccess) { (void)cudaGetLastError(); return 1; }
+        if (!g_na_stream[device] && cudaStreamCreateWithFlags(&g_na_stream[device], cudaStreamNonBlocking) != cudaSuccess) {
+            (void)cudaGetLastError();
+            g_na_stream[device] = nullptr;
+            return 1;
+        }
+        if (!g_na_word_locked) {
+            if (cudaHostRegister(g_na_word, sizeof g_na_word, cudaHostRegisterPortable) != cudaSuccess) {
+                (void)cudaGetLastError();
+                return 1;
+            }
+            g_na_word_locked = true;
+        }
         g_na_base[device] = static_cast<uint8_t *>(ptr);
     }
+    cudaStream_t st = g_na_stream[device];
+    if (cudaStreamQuery(st) != cudaSuccess) { (void)cudaGetLastError(); return 1; }   // an earlier decode still runs
     uint8_t *const base = g_na_base[device];
     int slot = -1;
     for (int s = 0; s < kNaModels && slot < 0; ++s) if (g_na_slot[device][s] == p.model_id) slot = s;
@@ -130,23 +156,18 @@ WEXB_API int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned
     job->error = derr;
     *reinterpret_cast<uint32_t *>(g_na_host + kNaErr) = 0;   // the error word starts at zero every call
     const size_t meta_bytes = kNaOffs + 4ull * (p.streams() + 1);
-    cudaStream_t st = cudaStreamPerThread;
     const Nr3Record *drec = reinterpret_cast<const Nr3Record *>(base + kNaRec);
     const Nr3Task *dtasks = reinterpret_cast<const Nr3Task *>(base + kNaTasks);
-    g_na_error = ~0u;
+    uint32_t &error = g_na_word[0];
+    error = ~0u;
     const bool ok = cudaMemcpyAsync(base + kNaRecord, record, p.total, cudaMemcpyHostToDevice, st) == cudaSuccess &&
                     cudaMemcpyAsync(base, g_na_host, meta_bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
                     launch_nr3_scales(drec, dtasks, ns, st) == cudaSuccess &&
                     launch_nr3_weights(drec, dtasks + ns, nw, (int)wthreads, st) == cudaSuccess &&
                     launch_commit(reinterpret_cast<const CommitJob *>(base + kNaJob), 1, st) == cudaSuccess &&
-                    cudaMemcpyAsync(&g_na_error, derr, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-                    cudaStreamSynchronize(st) == cudaSuccess;
-    if (!ok) {   // let whatever was queued finish before the array can be reused
-        (void)cudaGetLastError();
-        (void)cudaStreamSynchronize(st);
-        (void)cudaGetLastError();
-        return 1;
-    }
-    if (g_na_error) { report_error_bits(g_na_error); return -1; }
-    return 0;
+                    cudaMemcpyAsync(&error, derr, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    const Waited waited = wait_stream(st);   // also after a failed step: whatever was queued must end
+    if (!ok || waited != Waited::Done) { (void)cudaGetLastError(); return 1; }
+    if (error) report_error_bits(error);
+    return status_of_bits(error);
 }

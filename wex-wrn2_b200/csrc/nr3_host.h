@@ -64,6 +64,11 @@ void plan_tasks(const Plan &p, uint32_t rec, int wthreads, std::vector<Nr3Task> 
 int weight_threads();
 // Reports an integrity failure once per process (c/tools/wex_cuda_bridge.cu:117-122).
 void report_error_bits(uint32_t bits);
+// The status of a record from its error word: 0 clean, -1 the record failed a check, 1 a bounded
+// device wait gave up (kErrTimeout). A TMA copy may still have been in flight when that CTA returned,
+// so the device is suspect and the record must be decoded again (status 1, "unavailable"), never
+// reported as invalid data.
+inline int status_of_bits(uint32_t bits) { return !bits ? 0 : (bits & kErrTimeout) ? 1 : -1; }
 uint32_t last_error_bits();
 
 // Queued batches (helper_abi.cpp): waits until the host records of ticket `t` (wexb_batch_submit) have

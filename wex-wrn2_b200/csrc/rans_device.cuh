@@ -12,7 +12,7 @@ namespace rans {
 
 constexpr uint32_t kRingWords = 32;
 constexpr uint32_t kAhead = 24;
-constexpr uint32_t kSpinLimit = 1u << 24;   // bounded waits: never spin forever on a barrier
+constexpr uint32_t kSpinLimit = kWaitPolls;   // bounded waits: never spin forever on a barrier
 
 __device__ __forceinline__ uint32_t rotl32(uint32_t x, int r) { return __funnelshift_l(x, x, r); }
 __device__ __forceinline__ uint32_t mm3_mix(uint32_t k) { return rotl32(k * 0xcc9e2d51u, 15) * 0x1b873593u; }

@@ -5,6 +5,8 @@
 // its rule). GPU: every record's stored bytes go up once; record SHA-256 checks, RAW padding checks,
 // WNR3 decodes (the kernels of wnr3_kernels.cu) and the content digest run there.
 #include <cuda_runtime.h>
+#include <sys/mman.h>
+#include <unistd.h>
 
 #include <cstdio>
 #include <cstring>
@@ -13,6 +15,7 @@
 
 #include "bufs.h"
 #include "container.cuh"
+#include "host_wait.h"
 #include "nr3_host.h"
 #include "sha256.cuh"
 #include "wex4_index.h"
@@ -369,6 +372,7 @@ struct Space {   // the container layer's device workspace: one call at a time
     std::vector<cudaEvent_t> landed;           // one per group of uploaded records, then one per hash stream
     DevBuf stage, out, scratch, meta;
     PinBuf hmeta;
+    bool unsettled = false;   // a bounded wait gave up: its work may still use the buffers and streams
     bool events(size_t n) {
         while (landed.size() < n) {
             cudaEvent_t e;
@@ -443,6 +447,13 @@ int prepare_wbp1(Job &j, int device) {
 bool run_jobs(std::vector<Job> &jobs, int device) {
     Space &S = g_space;
     if (cudaSetDevice(device) != cudaSuccess) { (void)cudaGetLastError(); return false; }
+    if (S.unsettled) {   // reuse the workspace only once the work of the call that gave up has ended
+        bool ended = cudaStreamQuery(S.st) == cudaSuccess;
+        for (cudaStream_t h : S.sh) ended = ended && cudaStreamQuery(h) == cudaSuccess;
+        (void)cudaGetLastError();
+        if (!ended) return false;
+        S.unsettled = false;
+    }
     if (S.device != device) {
         if (S.st) {
             S.stage.release(); S.out.release(); S.scratch.release(); S.meta.release();
@@ -621,9 +632,14 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     ok = ok &&
          cudaMemcpyAsync(hm + o_err, dm + o_err, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
          cudaMemcpyAsync(hm + o_ver, dm + o_ver, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess;
-    if (cudaStreamSynchronize(st) != cudaSuccess) ok = false;
-    for (cudaStream_t h : S.sh) if (cudaStreamSynchronize(h) != cudaSuccess) ok = false;
-    if (!ok) { (void)cudaGetLastError(); return false; }
+    // bounded waits, also after a failed step: whatever was queued must end before the space is reused
+    Waited waited = wait_stream(st);
+    for (cudaStream_t h : S.sh) {
+        const Waited w = wait_stream(h);
+        if (w != Waited::Done && waited == Waited::Done) waited = w;
+    }
+    if (waited == Waited::TimedOut) S.unsettled = true;
+    if (!ok || waited != Waited::Done) { (void)cudaGetLastError(); return false; }
     const uint32_t *herr = reinterpret_cast<const uint32_t *>(hm + o_err), *hver = reinterpret_cast<const uint32_t *>(hm + o_ver);
     for (size_t i = 0; i < n; ++i) {
         Job &j = jobs[i];
@@ -842,8 +858,10 @@ WEXB_API int wex4_check(const unsigned char *file, uint64_t len, int flags, unsi
         msgs[i] = {segs[i].host ? dmeta.p + 32 + segs[i].at : segs[i].dev, segs[i].bytes, nullptr, nullptr, nullptr, 0};
     ok = ok && cudaMemcpy(dmeta.p + 32, metas.data(), metas.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
          cudaMemcpy(dsegs.p, msgs.data(), msgs.size() * sizeof(ShaMsg), cudaMemcpyHostToDevice) == cudaSuccess &&
-         launch_sha256_segments(reinterpret_cast<const ShaMsg *>(dsegs.p), (uint32_t)msgs.size(), dmeta.p, g_space.st) == cudaSuccess &&
-         cudaStreamSynchronize(g_space.st) == cudaSuccess;
+         launch_sha256_segments(reinterpret_cast<const ShaMsg *>(dsegs.p), (uint32_t)msgs.size(), dmeta.p, g_space.st) == cudaSuccess;
+    const Waited waited = wait_stream(g_space.st);
+    if (waited == Waited::TimedOut) { g_space.unsettled = true; return E_ARG; }   // dmeta / dsegs stay allocated
+    ok = ok && waited == Waited::Done;
     uint8_t dg[32];
     ok = ok && cudaMemcpy(dg, dmeta.p, 32, cudaMemcpyDeviceToHost) == cudaSuccess;
     dmeta.release(); dsegs.release();
@@ -872,6 +890,26 @@ WEXB_API int wex4_bp_decode_record(const unsigned char *record, size_t total, ui
     if (cudaMemcpy(out, j.out_dev, decoded, cudaMemcpyDeviceToHost) != cudaSuccess) { (void)cudaGetLastError(); return -1; }
     return 0;
 }
-WEXB_API int wex4_fuzz_check(const unsigned char *, uint64_t, int, unsigned char *) { return E_UNSUPPORTED; }
+// The same check as wex4_check on a copy of the file that ends right before an inaccessible page, so
+// that any host read past the end of the file faults instead of passing silently (the reference's
+// guard-paged check, wex4/wex4_tools.c:36-59, :170-178). The decoded bytes live in device memory here,
+// where host guard pages do not apply: a kernel never reads past a record's stored bytes by design
+// (every stream read is bounded by its offsets, the record lengths checked on the host first).
+WEXB_API int wex4_fuzz_check(const unsigned char *file, uint64_t len, int flags, unsigned char *digest) {
+    if (!file && len) return E_ARG;
+    const long ps = sysconf(_SC_PAGESIZE);
+    const size_t page = ps > 0 ? (size_t)ps : 4096;
+    if (len > (uint64_t)SIZE_MAX - 2 * page) return E_ARG;
+    const size_t body = ((size_t)len + page - 1) / page * page;
+    void *base = mmap(nullptr, body + page, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+    if (base == MAP_FAILED) return E_ARG;
+    uint8_t *const guard = static_cast<uint8_t *>(base) + body;
+    if (mprotect(guard, page, PROT_NONE) != 0) { munmap(base, body + page); return E_ARG; }
+    uint8_t *copy = guard - len;
+    if (len) std::memcpy(copy, file, (size_t)len);
+    const int st = wex4_check(copy, len, flags, digest);
+    munmap(base, body + page);
+    return st;
+}
 WEXB_API int wex4_fuzz_run(const unsigned char *, uint64_t, uint64_t, uint32_t, int, uint64_t *) { return E_UNSUPPORTED; }
 WEXB_API int wex4_store_probe(const char *, const unsigned char *, unsigned char *, uint64_t, uint32_t *) { return E_UNSUPPORTED; }

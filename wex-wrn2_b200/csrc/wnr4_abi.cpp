@@ -1,6 +1,12 @@
 // The WNR4 ABI 5 of include/wnr4_cuda.h (kind MX) over wnr4_kernel.cu: WNM4 model registry with
 // per-device tables, host validation of records and geometry (wnr4/wnr4.h:108-140, :170-190,
-// :317-346), batches queued on tickets, up to WNR4_CUDA_SLOTS in flight per thread and device.
+// :317-346), and batches queued on tickets. A ticket is served by the same pooled workspaces and
+// per-device streams as the WNR3 helper's queued batches (workspace.h): the records and one metadata
+// block (record descriptors, tile jobs, zeroed error words) go up on the device's upload stream (or the
+// caller's stream), the tile kernel and the read-back of the error words run on a kernel stream, and
+// the wait is bounded (host_wait.h). The ABI's in-flight rule is kept: a thread's n-th ticket takes
+// lane n mod WNR4_CUDA_SLOTS on its device, and a submit whose lane still holds a ticket that was not
+// waited for is refused with WNR4_E_BUSY.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -9,10 +15,12 @@
 #include <vector>
 
 #include "bufs.h"
+#include "host_wait.h"
 #include "nr3_host.h"
 #include "wnr4.cuh"
 #include "wnr4_cuda.h"
 #include "wnr4_host.h"
+#include "workspace.h"
 
 #define WEXB_API extern "C" __attribute__((visibility("default")))
 
@@ -93,15 +101,9 @@ Model4 *find4(uint32_t id, int device) {
     return nullptr;
 }
 
-struct DeviceGuard {
-    int saved = -1;
-    DeviceGuard() { if (cudaGetDevice(&saved) != cudaSuccess) { (void)cudaGetLastError(); saved = -1; } }
-    ~DeviceGuard() { if (saved >= 0) (void)cudaSetDevice(saved); }
-};
-
 // Device tables of a validated blob on `device` (once per model and device): 0, or 1 on a CUDA failure.
 int register4(const uint8_t *blob, size_t, uint32_t pb, uint32_t id, int device) {
-    DeviceGuard guard;
+    KeepDevice keep;
     std::lock_guard<std::mutex> lock(g_m4_mu);
     for (Model4 *m : g_m4) if (m->id == id && m->device == device) return 0;
     const std::vector<uint8_t> img = model4_image(blob, pb);
@@ -195,67 +197,53 @@ int wnr4_tables(const uint8_t *blob, size_t bytes, int device, W4Tables *tab, ui
 }
 
 namespace {
-// ---- tickets ------------------------------------------------------------------------------------
-struct Slot {
-    DevBuf drec, djob, dinfo, derr;
-    PinBuf hjob, hinfo, herr;
-    cudaEvent_t done = nullptr;
-    cudaStream_t own = nullptr;
-    std::vector<int> status;
-    bool busy = false, broken = false;
-    int ticket = -1;
-    void release() {
-        if (busy && done) (void)cudaEventSynchronize(done);
-        drec.release(); djob.release(); dinfo.release(); derr.release();
-        hjob.release(); hinfo.release(); herr.release();
-        if (done) cudaEventDestroy(done);
-        if (own) cudaStreamDestroy(own);
-        (void)cudaGetLastError();
-        done = nullptr; own = nullptr; busy = false; ticket = -1; status.clear();
-    }
-};
-struct Ring { int device = -1; Slot slot[WNR4_CUDA_SLOTS]; };
-struct Rings {
-    std::vector<Ring *> rings;
-    unsigned next = 0;
-    Ring *get(int device) {
-        for (Ring *r : rings) if (r->device == device) return r;
-        Ring *r = new Ring();
-        r->device = device;
-        rings.push_back(r);
-        return r;
-    }
-    void release() {
-        int cur = -1;
-        if (cudaGetDevice(&cur) != cudaSuccess) { (void)cudaGetLastError(); cur = -1; }
-        for (Ring *r : rings) {
-            if (cudaSetDevice(r->device) == cudaSuccess) for (Slot &s : r->slot) s.release();
-            (void)cudaGetLastError();
-            delete r;
-        }
-        rings.clear();
-        if (cur >= 0) (void)cudaSetDevice(cur);
-    }
-    ~Rings() { release(); }
-};
-thread_local Rings t_rings;
 
-int finish(Slot &s, int *status) {
-    const int n = (int)s.status.size();
-    const bool ok = !s.broken && cudaEventSynchronize(s.done) == cudaSuccess;
-    if (!ok) (void)cudaGetLastError();
-    const uint32_t *herr = reinterpret_cast<const uint32_t *>(s.herr.p);
-    int bad = 0;
-    for (int i = 0; i < n; ++i) {
-        int v = s.status[(size_t)i];
-        if (!v) v = !ok ? 1 : herr[i] ? -1 : 0;
-        if (status) status[i] = v;
-        bad += v != 0;
+// ---- tickets ------------------------------------------------------------------------------------
+// One submitted batch of the calling thread: its workspace and the host verdict of each record
+// (-1 refused before queueing, 0 queued).
+struct Batch4 {
+    int ticket = -1, device = -1;
+    Workspace *w = nullptr;
+    size_t err_at = 0;          // byte offset of the error words in the metadata block
+    bool queued = false;        // every queueing step succeeded
+    std::vector<int> pre;
+};
+
+// The calling thread's tickets: those it submitted and has not waited for yet.
+struct TicketBook {
+    uint32_t issued = 0;
+    std::vector<Batch4> open;
+
+    bool lane_taken(int device, int lane) const {
+        for (const Batch4 &b : open)
+            if (b.device == device && (b.ticket % WNR4_CUDA_SLOTS) == lane) return true;
+        return false;
     }
-    s.busy = false;
-    s.ticket = -1;
-    return bad;
-}
+    // Waits (bounded) for open[i], writes its statuses, gives its workspace back and removes it.
+    int close(size_t i, int *status) {
+        Batch4 b = std::move(open[i]);
+        open.erase(open.begin() + (std::ptrdiff_t)i);
+        Waited waited = Waited::Failed;
+        if (b.w) {
+            KeepDevice keep;
+            if (cudaSetDevice(b.device) == cudaSuccess) waited = wait_event(b.w->done);
+            else (void)cudaGetLastError();
+        }
+        const bool ok = b.queued && waited == Waited::Done;
+        const uint32_t *err = b.w ? reinterpret_cast<const uint32_t *>(b.w->hmeta.p + b.err_at) : nullptr;
+        int bad = 0;
+        for (size_t r = 0; r < b.pre.size(); ++r) {
+            const int v = b.pre[r] ? b.pre[r] : !ok ? 1 : status_of_bits(err[r]);
+            if (status) status[r] = v;
+            bad += v != 0;
+        }
+        workspace_give(b.w, waited != Waited::TimedOut);
+        return bad;
+    }
+    void close_all() { while (!open.empty()) close(open.size() - 1, nullptr); }
+    ~TicketBook() { close_all(); }
+};
+thread_local TicketBook t_book;
 
 }  // namespace
 }  // namespace wexb
@@ -277,77 +265,88 @@ WEXB_API int wnr4_cuda_batch_submit(int n, const uint32_t *geo, const unsigned c
     if (n <= 0 || !geo || !records || !totals || !owners || !dst_scale || !dst_weight || !wnr4_geo(geo, &g)) return WNR4_E_ARGS;
     Model4 *md = find4(model_id, device);
     if (!md) return WNR4_E_MODEL;
-    DeviceGuard guard;
+    const int ticket = (int)(t_book.issued & 0x7fffffffu);
+    if (t_book.lane_taken(device, ticket % WNR4_CUDA_SLOTS)) return WNR4_E_BUSY;   // unread verdicts are never dropped
+    KeepDevice keep;
     if (cudaSetDevice(device) != cudaSuccess) { (void)cudaGetLastError(); return WNR4_E_CUDA; }
-    Ring *R = t_rings.get(device);
-    const int ticket = (int)(t_rings.next & 0x7fffffffu);
-    Slot &s = R->slot[(unsigned)ticket % WNR4_CUDA_SLOTS];
-    if (s.busy) return WNR4_E_BUSY;   // never drop verdicts the caller has not read
-    if ((!s.done && cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming) != cudaSuccess) ||
-        (!s.own && cudaStreamCreateWithFlags(&s.own, cudaStreamNonBlocking) != cudaSuccess)) {
-        (void)cudaGetLastError();
-        return WNR4_E_CUDA;
-    }
-    cudaStream_t st = stream ? (cudaStream_t)stream : s.own;
-    std::vector<size_t> at((size_t)n);
-    size_t bytes = 0;
-    for (int i = 0; i < n; ++i) { at[(size_t)i] = bytes; bytes += align_up(totals[i], 256); }
-    if (!s.drec.grow(bytes) || !s.dinfo.grow(sizeof(W4Rec) * (size_t)n) || !s.hinfo.grow(sizeof(W4Rec) * (size_t)n) ||
-        !s.derr.grow(4ull * n) || !s.herr.grow(4ull * n)) return WNR4_E_CUDA;
-    s.status.assign((size_t)n, -1);
+    Batch4 b;
+    b.ticket = ticket; b.device = device;
+    b.pre.assign((size_t)n, -1);
+    // records, 256-byte aligned, in the workspace's record buffer
+    std::vector<size_t> rec_at((size_t)n);
+    size_t rec_bytes = 0;
+    for (int i = 0; i < n; ++i) { rec_at[(size_t)i] = rec_bytes; rec_bytes += align_up(totals[i], 256); }
+    Workspace *w = workspace_take(device);
+    if (!w) return WNR4_E_CUDA;
+    if (!w->drec.grow(rec_bytes + 256)) { workspace_give(w, true); return WNR4_E_CUDA; }
+    std::vector<W4Rec> info((size_t)n);
     std::vector<W4Job> by_m[3];
-    W4Rec *info = reinterpret_cast<W4Rec *>(s.hinfo.p);
     for (int i = 0; i < n; ++i) {
-        uint8_t *ds[3] = {dst_scale[3 * i], dst_scale[3 * i + 1], dst_scale[3 * i + 2]};
-        uint8_t *dw[3] = {dst_weight[3 * i], dst_weight[3 * i + 1], dst_weight[3 * i + 2]};
-        std::memset(&info[i], 0, sizeof(W4Rec));
-        const bool targets = records[i] && ds[0] && ds[1] && ds[2] && dw[0] && dw[1] && dw[2] &&
-                             !((reinterpret_cast<uintptr_t>(dw[0]) | reinterpret_cast<uintptr_t>(dw[1]) |
-                                reinterpret_cast<uintptr_t>(dw[2])) & 15u);
-        std::vector<W4Job> mine[3];
-        if (targets && wnr4_plan(records[i], totals[i], g, owners[i], model_id, s.drec.p + at[(size_t)i], (uint32_t)i,
-                                 &info[i], mine)) {
-            for (int m = 0; m < 3; ++m) {
-                info[i].dst_s[m] = ds[m]; info[i].dst_w[m] = dw[m];
-                by_m[m].insert(by_m[m].end(), mine[m].begin(), mine[m].end());
-            }
-            info[i].error = reinterpret_cast<uint32_t *>(s.derr.p) + i;
-            s.status[(size_t)i] = 0;
+        W4Rec &R = info[(size_t)i];
+        std::memset(&R, 0, sizeof R);
+        bool targets = records[i] != nullptr;
+        uintptr_t wbits = 0;
+        for (int m = 0; m < 3; ++m) {
+            targets = targets && dst_scale[3 * i + m] && dst_weight[3 * i + m];
+            wbits |= reinterpret_cast<uintptr_t>(dst_weight[3 * i + m]);
         }
+        if (!targets || (wbits & 15u)) continue;   // packed weights take 16-byte stores
+        std::vector<W4Job> tiles[3];
+        if (!wnr4_plan(records[i], totals[i], g, owners[i], model_id, w->drec.p + rec_at[(size_t)i], (uint32_t)i, &R, tiles))
+            continue;
+        for (int m = 0; m < 3; ++m) {
+            R.dst_s[m] = dst_scale[3 * i + m];
+            R.dst_w[m] = dst_weight[3 * i + m];
+            by_m[m].insert(by_m[m].end(), tiles[m].begin(), tiles[m].end());
+        }
+        b.pre[(size_t)i] = 0;
     }
     const std::vector<W4Job> jobs = wnr4_launch_order(by_m);
-    if (!s.djob.grow(sizeof(W4Job) * (jobs.size() + 1)) || !s.hjob.grow(sizeof(W4Job) * (jobs.size() + 1))) return WNR4_E_CUDA;
-    if (!jobs.empty()) std::memcpy(s.hjob.p, jobs.data(), sizeof(W4Job) * jobs.size());
-    cudaError_t e = cudaSuccess;
-    for (int i = 0; i < n && e == cudaSuccess; ++i)
-        if (!s.status[(size_t)i]) e = cudaMemcpyAsync(s.drec.p + at[(size_t)i], records[i], totals[i], cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(s.dinfo.p, s.hinfo.p, sizeof(W4Rec) * (size_t)n, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess && !jobs.empty())
-        e = cudaMemcpyAsync(s.djob.p, s.hjob.p, sizeof(W4Job) * jobs.size(), cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(s.derr.p, 0, 4ull * n, st);
-    if (e == cudaSuccess)
-        e = launch_wnr4(md->tab, reinterpret_cast<const W4Job *>(s.djob.p), (uint32_t)jobs.size(),
-                        reinterpret_cast<const W4Rec *>(s.dinfo.p), st);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(s.herr.p, s.derr.p, 4ull * n, cudaMemcpyDeviceToHost, st);
-    const cudaError_t ev = cudaEventRecord(s.done, st);   // recorded even after a failed step: wait waits for what was queued
-    s.broken = e != cudaSuccess || ev != cudaSuccess;
-    if (s.broken) (void)cudaGetLastError();
-    s.busy = true;
-    s.ticket = ticket;
-    t_rings.next++;
+    // one metadata block: record descriptors, tile jobs, zeroed error words
+    const size_t info_at = 0, job_at = align_up(sizeof(W4Rec) * (size_t)n, 256);
+    b.err_at = align_up(job_at + sizeof(W4Job) * (jobs.size() + 1), 256);
+    const size_t meta_bytes = b.err_at + 4ull * (size_t)n;
+    if (!w->dmeta.grow(meta_bytes) || !w->hmeta.grow(meta_bytes)) { workspace_give(w, true); return WNR4_E_CUDA; }
+    uint8_t *hm = w->hmeta.p, *dm = w->dmeta.p;
+    uint32_t *derr = reinterpret_cast<uint32_t *>(dm + b.err_at);
+    for (int i = 0; i < n; ++i) if (!b.pre[(size_t)i]) info[(size_t)i].error = derr + i;
+    std::memcpy(hm + info_at, info.data(), sizeof(W4Rec) * (size_t)n);
+    if (!jobs.empty()) std::memcpy(hm + job_at, jobs.data(), sizeof(W4Job) * jobs.size());
+    std::memset(hm + b.err_at, 0, 4ull * (size_t)n);
+    // uploads, then the kernel and the read-back of the error words
+    cudaStream_t up = (cudaStream_t)stream, st = (cudaStream_t)stream;
+    if (!stream && !device_streams(device, &up, &st)) { workspace_give(w, true); return WNR4_E_CUDA; }
+    bool ok = cudaMemcpyAsync(dm, hm, meta_bytes, cudaMemcpyHostToDevice, up) == cudaSuccess;
+    for (int i = 0; ok && i < n; ++i)
+        if (!b.pre[(size_t)i])
+            ok = cudaMemcpyAsync(w->drec.p + rec_at[(size_t)i], records[i], totals[i], cudaMemcpyHostToDevice, up) == cudaSuccess;
+    if (ok && up != st)
+        ok = cudaEventRecord(w->uploads_done, up) == cudaSuccess && cudaStreamWaitEvent(st, w->uploads_done, 0) == cudaSuccess;
+    ok = ok &&
+         launch_wnr4(md->tab, reinterpret_cast<const W4Job *>(dm + job_at), (uint32_t)jobs.size(),
+                     reinterpret_cast<const W4Rec *>(dm + info_at), st) == cudaSuccess &&
+         cudaMemcpyAsync(hm + b.err_at, derr, 4ull * (size_t)n, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    // `done` is recorded even after a failed step, so the wait covers whatever was queued
+    if (cudaEventRecord(w->done, st) != cudaSuccess) {
+        (void)cudaGetLastError();
+        ok = false;
+        if (wait_stream(st) == Waited::TimedOut || (up != st && wait_stream(up) == Waited::TimedOut)) {
+            workspace_give(w, false);   // its work may still be running; nothing else will wait for it
+            return WNR4_E_CUDA;
+        }
+    }
+    if (!ok) (void)cudaGetLastError();
+    b.w = w;
+    b.queued = ok;
+    t_book.open.push_back(std::move(b));
+    t_book.issued++;
     return ticket;
 }
 
 WEXB_API int wnr4_cuda_batch_wait(int ticket, int *status) {
     if (ticket < 0) return -1;
-    for (Ring *R : t_rings.rings) {
-        Slot &s = R->slot[(unsigned)ticket % WNR4_CUDA_SLOTS];
-        if (s.busy && s.ticket == ticket) {
-            DeviceGuard guard;
-            (void)cudaSetDevice(R->device);
-            return finish(s, status);
-        }
-    }
+    for (size_t i = 0; i < t_book.open.size(); ++i)
+        if (t_book.open[i].ticket == ticket) return t_book.close(i, status);
     return -1;
 }
 
@@ -357,15 +356,13 @@ WEXB_API int wnr4_cuda_decode_batch(int n, const uint32_t *geo, const unsigned c
     if (n <= 0) return 0;
     if (!status) return n;
     const int t = wnr4_cuda_batch_submit(n, geo, records, totals, owners, model_id, device, dst_scale, dst_weight, nullptr);
-    if (t < 0) {
-        const int v = t == WNR4_E_ARGS ? -1 : 1;
-        for (int i = 0; i < n; ++i) status[i] = v;
-        return n;
-    }
-    return wnr4_cuda_batch_wait(t, status);
+    if (t >= 0) return wnr4_cuda_batch_wait(t, status);
+    const int v = t == WNR4_E_ARGS ? -1 : 1;
+    for (int i = 0; i < n; ++i) status[i] = v;
+    return n;
 }
 
-WEXB_API void wnr4_cuda_release_thread(void) { t_rings.release(); }
+WEXB_API void wnr4_cuda_release_thread(void) { t_book.close_all(); }
 
 WEXB_API int wnr4_cuda_gg_register_model(const unsigned char *, size_t, int, uint32_t *id) {
     if (id) *id = 0;

@@ -1,0 +1,88 @@
+// Per-device streams and the pool of call workspaces (workspace.h).
+#include "workspace.h"
+
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "nr3_host.h"
+
+namespace wexb {
+namespace {
+
+constexpr int kLanes = 4;   // kernel streams per device
+
+struct Queues {
+    cudaStream_t upload = nullptr, lane[kLanes] = {};
+    unsigned next = 0;
+    bool ok = false;
+};
+std::mutex g_queues_mu;
+Queues g_queues[kMaxDevices];
+
+std::mutex g_pool_mu;
+std::vector<Workspace *> g_idle[kMaxDevices];
+std::vector<Workspace *> g_parked[kMaxDevices];   // gave up waiting: back to g_idle once `done` completes
+
+Workspace *fresh(int device) {
+    auto *w = new (std::nothrow) Workspace();
+    if (!w) return nullptr;
+    if (cudaEventCreateWithFlags(&w->uploads_done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&w->done, cudaEventDisableTiming) != cudaSuccess) {
+        (void)cudaGetLastError();   // an event made before the failure leaks, on CUDA failure only
+        delete w;
+        return nullptr;
+    }
+    w->device = device;
+    return w;
+}
+
+}  // namespace
+
+bool device_streams(int device, cudaStream_t *up, cudaStream_t *st) {
+    if (device < 0 || device >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lock(g_queues_mu);
+    Queues &q = g_queues[device];
+    if (!q.ok) {
+        bool ok = cudaStreamCreateWithFlags(&q.upload, cudaStreamNonBlocking) == cudaSuccess;
+        for (int l = 0; ok && l < kLanes; ++l) ok = cudaStreamCreateWithFlags(&q.lane[l], cudaStreamNonBlocking) == cudaSuccess;
+        if (!ok) { (void)cudaGetLastError(); return false; }   // streams made so far leak, on CUDA failure only
+        q.ok = true;
+    }
+    *up = q.upload;
+    *st = q.lane[q.next];
+    q.next = (q.next + 1u) % kLanes;
+    return true;
+}
+
+Workspace *workspace_take(int device) {
+    if (device < 0 || device >= kMaxDevices) return nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_pool_mu);
+        std::vector<Workspace *> &parked = g_parked[device];
+        for (size_t i = 0; i < parked.size();) {
+            if (cudaEventQuery(parked[i]->done) == cudaSuccess) {
+                g_idle[device].push_back(parked[i]);
+                parked[i] = parked.back();
+                parked.pop_back();
+            } else {
+                ++i;
+            }
+        }
+        (void)cudaGetLastError();
+        if (!g_idle[device].empty()) {
+            Workspace *w = g_idle[device].back();
+            g_idle[device].pop_back();
+            return w;
+        }
+    }
+    return fresh(device);
+}
+
+void workspace_give(Workspace *w, bool settled) {
+    if (!w) return;
+    std::lock_guard<std::mutex> lock(g_pool_mu);
+    (settled ? g_idle : g_parked)[w->device].push_back(w);
+}
+
+}  // namespace wexb

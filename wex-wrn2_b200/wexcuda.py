@@ -61,6 +61,8 @@ def lib():
         L.wexb_encode_batch.argtypes = [I, P, P, P, P, I, ctypes.c_uint, ctypes.c_uint, P, SZ, I, P, P, P, P, P]
         L.wexb_count_batch.argtypes = [I, P, P, I, I, P, P, P]
         L.wexb_selftest_bounded_wait.argtypes = [I, ctypes.c_uint, P]
+        L.wexb_set_wait_limit.argtypes = [ctypes.c_double]
+        L.wexb_wait_limit.restype = ctypes.c_double
         _lib = L
     return _lib
 
@@ -304,6 +306,15 @@ def count_batch(entries, coded, nr3=True, device=0):
     lib().wexb_count_batch(n, ep, _ptrs([x[0] for x in srcs]), 1 if nr3 else 0, device, wc.ctypes.data, sc.ctypes.data,
                            status)
     return list(status)[:n], wc, sc
+
+
+def set_wait_limit(seconds):
+    """Host wait limit of every entry point (wexb_set_wait_limit): 0, or -1 for a value out of range."""
+    return lib().wexb_set_wait_limit(float(seconds))
+
+
+def wait_limit():
+    return lib().wexb_wait_limit()
 
 
 def selftest_bounded_wait(device=0, polls=1000):
