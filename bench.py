@@ -1598,7 +1598,7 @@ def run_gpu(args, cfg):
         # 32 records of the pool
         import wex4file
         sample = sorted({(e.layer, e.index): e for e in experts if e.codec == 5}.values(), key=lambda e: (e.layer, e.index))[:32]
-        fdata = wex4file.write([wex4file.expert_record(e) for e in sample], [(wex4file.BLOB_WNM2, fnv1a(blob), blob)],
+        fdata = wex4file.write([wex4file.expert_record(e, 0, value_exact=cfg["cz"]) for e in sample], [(wex4file.BLOB_WNM2, fnv1a(blob), blob)],
                                grid=(cfg['layers'], cfg['experts']), value_exact=cfg['cz'])
         fdt, fn, fnb = reference_file_rate(fdata, cores, min_seconds=args.cpu_seconds / 2, lib='wex4_tools_fast')
         line['cpu_baseline']['fast'] = {'value': round(fnb / fdt / 1e9, 4), 'unit': 'GB/s', 'cores': cores,

@@ -20,9 +20,7 @@ cudaError_t launch_sha256_segments(const ShaMsg *, uint32_t, uint8_t *, cudaStre
 cudaError_t launch_wbp1_streams(const Wbp1Record *, const Wbp1Task *, uint32_t, cudaStream_t) { return cudaErrorNotSupported; }
 cudaError_t launch_wbp1_join(const Wbp1Record *, uint32_t, cudaStream_t) { return cudaErrorNotSupported; }
 cudaError_t prepare_wbp1_kernels() { return cudaErrorNotSupported; }
-cudaError_t launch_nr3_scales(const Nr3Record *, const Nr3Task *, uint32_t, cudaStream_t) { return cudaErrorNotSupported; }
-cudaError_t launch_nr3_weights(const Nr3Record *, const Nr3Task *, uint32_t, int, cudaStream_t) { return cudaErrorNotSupported; }
-cudaError_t launch_commit(const CommitJob *, uint32_t, cudaStream_t) { return cudaErrorNotSupported; }
+cudaError_t launch_nr3(const Nr3Launch &, int, cudaStream_t) { return cudaErrorNotSupported; }
 cudaError_t prepare_nr3_kernels() { return cudaErrorNotSupported; }
 cudaError_t launch_wnr4(const W4Tables &, const W4Job *, uint32_t, const W4Rec *, cudaStream_t) { return cudaErrorNotSupported; }
 }  // namespace wexb

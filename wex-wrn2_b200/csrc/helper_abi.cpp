@@ -31,14 +31,15 @@
 namespace wexb {
 namespace {
 
-// Byte layout of a call's metadata block (host pinned, copied to the device in one piece).
+// Byte layout of a call's metadata block (host pinned, copied to the device in one piece): record
+// descriptors, the work queue, its counters, commit jobs, error words, stream offsets.
 struct MetaLayout {
-    size_t recs = 0, stasks = 0, wtasks = 0, jobs = 0, errs = 0, offs = 0, total = 0;
-    void compute(size_t k, size_t ns, size_t nw, size_t njobs, size_t noffs) {
+    size_t recs = 0, items = 0, counters = 0, jobs = 0, errs = 0, offs = 0, total = 0;
+    void compute(size_t k, size_t nitems, size_t ncounters, size_t njobs, size_t noffs) {
         size_t at = 0;
         recs = at; at = align_up(at + k * sizeof(Nr3Record), 256);
-        stasks = at; at = align_up(at + ns * sizeof(Nr3Task), 256);
-        wtasks = at; at = align_up(at + nw * sizeof(Nr3Task), 256);
+        items = at; at = align_up(at + nitems * sizeof(Nr3Item), 256);
+        counters = at; at = align_up(at + ncounters * 4, 256);
         jobs = at; at = align_up(at + njobs * sizeof(CommitJob), 256);
         errs = at; at = align_up(at + k * 4, 256);
         offs = at; at = align_up(at + noffs * 4, 256);
@@ -89,35 +90,41 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     if (device < 0 || device >= kMaxDevices || cudaSetDevice(device) != cudaSuccess) {
         (void)cudaGetLastError(); c.settle(1); return false;
     }
-    std::vector<Nr3Tables> tabs;   // device tables of every record's model
+    std::vector<const uint8_t *> tabs;   // device tables of every record's model
     {
-        std::vector<int> keep;
+        std::vector<std::pair<int, const uint8_t *>> keep;
         for (int i : c.pend) {
-            Nr3Tables t;
+            const uint8_t *t = nullptr;
             if (model_tables(c.plans[(size_t)i].model_id, device, &t)) { c.status[(size_t)i] = 1; continue; }
-            keep.push_back(i); tabs.push_back(t);
+            keep.emplace_back(i, t);
         }
-        c.pend.swap(keep);
+        // one launch per model: the records of a model contiguous (call order otherwise)
+        std::stable_sort(keep.begin(), keep.end(), [](const auto &a, const auto &b) { return a.second < b.second; });
+        c.pend.clear();
+        for (const auto &e : keep) { c.pend.push_back(e.first); tabs.push_back(e.second); }
     }
     const size_t k = c.k = c.pend.size();
     if (!k) return false;
+    const int sms = device_sms(device);
     Workspace *w = c.w = workspace_take(device);
-    if (!w) { c.settle(1); return false; }
+    if (!w || !sms) { c.settle(1); workspace_give(w, true); c.w = nullptr; return false; }
     // layout
-    const int wthreads = weight_threads();
+    const bool commit = mode == Dest::Device;
     std::vector<size_t> rec_off(k), off_off(k);
+    std::vector<const Plan *> plans(k);
     c.scr_off.assign(k, 0);
-    std::vector<Nr3Task> stasks, wtasks;
     size_t rec_bytes = 0, scr_bytes = 0, noffs = 0;
     for (size_t j = 0; j < k; ++j) {
         const Plan &p = c.plans[(size_t)c.pend[j]];
-        rec_off[j] = rec_bytes; rec_bytes += align_up(p.total, 256);
+        plans[j] = &p;
+        rec_off[j] = rec_bytes; rec_bytes += align_up(p.total + kRecordSlack, 256);
         c.scr_off[j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
         off_off[j] = noffs; noffs += p.streams() + 1;
-        plan_tasks(p, (uint32_t)j, wthreads, stasks, wtasks);
     }
+    LaunchSet launches;
+    launches.plan(plans.data(), tabs.data(), (uint32_t)k, commit);
     MetaLayout &L = c.L;
-    L.compute(k, stasks.size(), wtasks.size(), host_dst ? 0 : k, noffs);
+    L.compute(k, launches.items, launches.counter_words(), commit ? k : 0, noffs);
     if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total)) {
         c.settle(1); workspace_give(w, true); c.w = nullptr; return false;
     }
@@ -127,31 +134,27 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + L.errs);
     uint32_t *hoffs = reinterpret_cast<uint32_t *>(hm + L.offs);
     const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + L.recs);
-    const Nr3Task *dst_tasks = reinterpret_cast<const Nr3Task *>(dm + L.stasks);
-    const Nr3Task *dwt_tasks = reinterpret_cast<const Nr3Task *>(dm + L.wtasks);
     const CommitJob *djobs = reinterpret_cast<const CommitJob *>(dm + L.jobs);
     uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + L.errs);
-    std::memcpy(hm + L.stasks, stasks.data(), stasks.size() * sizeof(Nr3Task));
-    std::memcpy(hm + L.wtasks, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
+    launches.fill(plans.data(), commit, sms, reinterpret_cast<Nr3Item *>(hm + L.items), reinterpret_cast<uint32_t *>(hm + L.counters));
     for (size_t j = 0; j < k; ++j) {
         const int i = c.pend[j];
         const Plan &p = c.plans[(size_t)i];
         uint8_t *scr = w->dscratch.p + c.scr_off[j];
         plan_offsets(p, hoffs + off_off[j]);
-        plan_descriptor(p, tabs[j], w->drec.p + rec_off[j], reinterpret_cast<const uint32_t *>(dm + L.offs) + off_off[j],
-                        scr, derrs + j, &hrecs[j]);
+        plan_descriptor(p, w->drec.p + rec_off[j], reinterpret_cast<const uint32_t *>(dm + L.offs) + off_off[j], scr,
+                        derrs + j, commit ? djobs + j : nullptr, &hrecs[j]);
         herrs[j] = 0;
-        if (!host_dst) {
+        if (commit) {
             CommitJob &J = hjobs[j];
             for (int m = 0; m < 3; ++m) {
                 J.src[m] = scr + p.soff[m]; J.dst[m] = dst_scale[3 * i + m]; J.bytes[m] = p.dst_bytes[m];
                 J.src[3 + m] = scr + p.wout[m]; J.dst[3 + m] = dst_weight[3 * i + m]; J.bytes[3 + m] = p.dst_bytes[3 + m];
             }
-            J.error = derrs + j;
         }
     }
-    // enqueue: metadata and records on the upload stream; then, on the call's kernel stream, the
-    // three kernels (every record of the call in one grid each) and the read-back of the error words
+    // enqueue: metadata and records on the upload stream; then, on the call's kernel stream, one
+    // persistent launch per model over every record of the call, and the read-back of the error words
     cudaStream_t up = nullptr, st = nullptr;
     if (!device_streams(device, &up, &st)) { c.settle(1); workspace_give(w, true); c.w = nullptr; return false; }
     bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, up) == cudaSuccess;
@@ -165,9 +168,8 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
         ok = false;
     }
     if (ok)
-        ok = launch_nr3_scales(drecs, dst_tasks, (uint32_t)stasks.size(), st) == cudaSuccess &&
-             launch_nr3_weights(drecs, dwt_tasks, (uint32_t)wtasks.size(), wthreads, st) == cudaSuccess &&
-             (mode != Dest::Device || launch_commit(djobs, (uint32_t)k, st) == cudaSuccess);
+        ok = launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + L.items), reinterpret_cast<uint32_t *>(dm + L.counters),
+                             sms, st);
     for (size_t j = 0; ok && mode == Dest::Host && j < k; ++j) {
         const int i = c.pend[j];
         const Plan &p = c.plans[(size_t)i];
@@ -409,13 +411,14 @@ struct ResSlot {
     bool timed = false;
     bool stale = false;   // its wait gave up: the GPU may still be using it until `done` completes
     int k = 0;
+    std::vector<int> order;   // launch position -> the caller's index j (records grouped by model)
 };
 // Two decodes may be queued at once: the host plans the next one while the GPU runs the previous one.
 struct WexbResident {
     int device = -1;
     cudaStream_t own = nullptr;
     std::vector<Plan> plans;          // lengths pointers cleared: the records live on the device
-    std::vector<Nr3Tables> tabs;
+    std::vector<const uint8_t *> tabs;
     std::vector<size_t> rec_off, off_off;
     DevBuf store;                     // records, then offset tables
     size_t offs_at = 0, bytes = 0;
@@ -444,7 +447,7 @@ WEXB_API int wexb_resident_create(int n, const WexEntry *const *entries, const u
     std::vector<std::vector<uint32_t>> offs;
     for (int i = 0; i < n; ++i) {
         Plan p{};
-        Nr3Tables t{};
+        const uint8_t *t = nullptr;
         status[i] = -1;
         if (!entries[i] || !records[i] || plan_record(entries[i], records[i], &p)) { ++bad; continue; }
         if (!dev_ok || !model_registered(p.model_id) || model_tables(p.model_id, device, &t)) { status[i] = 1; ++bad; continue; }
@@ -452,7 +455,7 @@ WEXB_API int wexb_resident_create(int n, const WexEntry *const *entries, const u
         std::vector<uint32_t> o(p.streams() + 1);
         plan_offsets(p, o.data());
         offs.push_back(std::move(o));
-        r->rec_off.push_back(rec_bytes); rec_bytes += align_up(p.total, 256);
+        r->rec_off.push_back(rec_bytes); rec_bytes += align_up(p.total + kRecordSlack, 256);
         r->off_off.push_back(noffs); noffs += p.streams() + 1;
         p.lengths = nullptr;
         r->plans.push_back(p);
@@ -497,10 +500,10 @@ int resident_retire(WexbResident *r, int *status) {
     q.stale = waited == Waited::TimedOut;
     const uint32_t *herrs = reinterpret_cast<const uint32_t *>(q.hmeta.p + q.L.errs);
     int bad = 0;
-    for (int j = 0; j < q.k; ++j) {
+    for (int j = 0; j < q.k; ++j) {   // launch position j holds the caller's record order[j]
         const int v = !ok ? 1 : status_of_bits(herrs[j]);
         if (v == -1) report_error_bits(herrs[j]);
-        if (status) status[j] = v;
+        if (status) status[q.order[(size_t)j]] = v;
         bad += v != 0;
     }
     r->waited = r->head;
@@ -526,56 +529,67 @@ WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsi
         q.stale = false;
     }
     cudaStream_t st = stream ? (cudaStream_t)stream : r->own;
-    const int wthreads = weight_threads();
-    std::vector<Nr3Task> stasks, wtasks;
+    const int sms = device_sms(r->device);
+    if (!sms) return 1;
+    // launch order: the records of a model contiguous, the caller's order otherwise
+    std::vector<int> &order = q.order;
+    order.resize((size_t)k);
+    for (int j = 0; j < k; ++j) order[(size_t)j] = j;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int a, int b) { return r->tabs[(size_t)index[a]] < r->tabs[(size_t)index[b]]; });
+    std::vector<const Plan *> plans((size_t)k);
+    std::vector<const uint8_t *> tabs((size_t)k);
     size_t scr_bytes = 0;
     std::vector<size_t> scr_off((size_t)k);
     for (int j = 0; j < k; ++j) {
-        const Plan &p = r->plans[(size_t)index[j]];
-        scr_off[(size_t)j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
-        plan_tasks(p, (uint32_t)j, wthreads, stasks, wtasks);
+        const size_t x = (size_t)index[order[(size_t)j]];
+        plans[(size_t)j] = &r->plans[x];
+        tabs[(size_t)j] = r->tabs[x];
+        scr_off[(size_t)j] = scr_bytes; scr_bytes += align_up(r->plans[x].scratch, 256);
     }
-    q.L.compute((size_t)k, stasks.size(), wtasks.size(), (size_t)k, 0);
+    LaunchSet launches;
+    launches.plan(plans.data(), tabs.data(), (uint32_t)k, true);
+    q.L.compute((size_t)k, launches.items, launches.counter_words(), (size_t)k, 0);
     if (!q.dscratch.grow(scr_bytes) || !q.dmeta.grow(q.L.total) || !q.hmeta.grow(q.L.total)) return 1;
     uint8_t *hm = q.hmeta.p, *dm = q.dmeta.p;
     Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + q.L.recs);
     CommitJob *hjobs = reinterpret_cast<CommitJob *>(hm + q.L.jobs);
     uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + q.L.errs);
     uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + q.L.errs);
-    std::memcpy(hm + q.L.stasks, stasks.data(), stasks.size() * sizeof(Nr3Task));
-    std::memcpy(hm + q.L.wtasks, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
+    const CommitJob *djobs = reinterpret_cast<const CommitJob *>(dm + q.L.jobs);
+    launches.fill(plans.data(), true, sms, reinterpret_cast<Nr3Item *>(hm + q.L.items),
+                  reinterpret_cast<uint32_t *>(hm + q.L.counters));
     for (int j = 0; j < k; ++j) {
-        const size_t x = (size_t)index[j];
+        const int cj = order[(size_t)j];   // the caller's index of the record at launch position j
+        const size_t x = (size_t)index[cj];
         const Plan &p = r->plans[x];
         uint8_t *scr = q.dscratch.p + scr_off[(size_t)j];
-        plan_descriptor(p, r->tabs[x], r->store.p + r->rec_off[x],
-                        reinterpret_cast<const uint32_t *>(r->store.p + r->offs_at) + r->off_off[x], scr, derrs + j, &hrecs[j]);
+        plan_descriptor(p, r->store.p + r->rec_off[x], reinterpret_cast<const uint32_t *>(r->store.p + r->offs_at) + r->off_off[x],
+                        scr, derrs + j, djobs + j, &hrecs[j]);
         herrs[j] = 0;
         CommitJob &J = hjobs[j];
         for (int m = 0; m < 3; ++m) {
-            J.src[m] = scr + p.soff[m]; J.dst[m] = dst_scale[3 * j + m]; J.bytes[m] = p.dst_bytes[m];
-            J.src[3 + m] = scr + p.wout[m]; J.dst[3 + m] = dst_weight[3 * j + m]; J.bytes[3 + m] = p.dst_bytes[3 + m];
+            J.src[m] = scr + p.soff[m]; J.dst[m] = dst_scale[3 * cj + m]; J.bytes[m] = p.dst_bytes[m];
+            J.src[3 + m] = scr + p.wout[m]; J.dst[3 + m] = dst_weight[3 * cj + m]; J.bytes[3 + m] = p.dst_bytes[3 + m];
         }
-        J.error = derrs + j;
     }
     if (r->profiling && !q.marks[0])
         for (auto &e : q.marks)
             if (cudaEventCreate(&e) != cudaSuccess) { (void)cudaGetLastError(); return 1; }
     const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + q.L.recs);
     auto mark = [&](int i) { return !r->profiling || cudaEventRecord(q.marks[i], st) == cudaSuccess; };
-    bool ok = cudaMemcpyAsync(dm, hm, q.L.total, cudaMemcpyHostToDevice, st) == cudaSuccess && mark(0) &&
-              launch_nr3_scales(drecs, reinterpret_cast<const Nr3Task *>(dm + q.L.stasks), (uint32_t)stasks.size(), st) == cudaSuccess &&
-              mark(1) &&
-              launch_nr3_weights(drecs, reinterpret_cast<const Nr3Task *>(dm + q.L.wtasks), (uint32_t)wtasks.size(), wthreads, st) == cudaSuccess &&
-              mark(2) && launch_commit(reinterpret_cast<const CommitJob *>(dm + q.L.jobs), (uint32_t)k, st) == cudaSuccess &&
-              mark(3) && cudaMemcpyAsync(herrs, derrs, 4 * (size_t)k, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-              cudaEventRecord(q.done, st) == cudaSuccess;
+    // events around: the metadata upload, the decode launch(es), the read-back of the error words
+    bool ok = mark(0) && cudaMemcpyAsync(dm, hm, q.L.total, cudaMemcpyHostToDevice, st) == cudaSuccess && mark(1) &&
+              launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + q.L.items),
+                              reinterpret_cast<uint32_t *>(dm + q.L.counters), sms, st) &&
+              mark(2) && cudaMemcpyAsync(herrs, derrs, 4 * (size_t)k, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+              mark(3) && cudaEventRecord(q.done, st) == cudaSuccess;
     if (!ok) { (void)cudaGetLastError(); return 1; }
+    r->launches = (int)launches.groups.size();
     q.timed = r->profiling;
     q.k = k;
     if (r->waited == si) r->waited = -1;   // its kernel times are being overwritten
     ++r->queued;
-    r->launches = 3;
     return 0;
 }
 

@@ -6,9 +6,9 @@
 // cudaMalloc and cudaFree can cause. Every other entry point of this library grows pooled device
 // buffers on demand; this one works entirely inside a fixed array defined in this file.
 //
-// The scratch (record staging, the decoded slab before its gated commit, launch metadata, model
-// tables) is the file-scope device array below, of a fixed size: records of at most 24 MiB stored and
-// 24 MiB decoded, at most 32,768 streams, at most 4 models per device. Every device on which this
+// The scratch (record staging, the decoded slab before its gated commit, launch metadata with the work
+// queue and its counters, model tables) is the file-scope device array below, of a fixed size: records
+// of at most 24 MiB stored and 24 MiB decoded, at most 32,768 streams, at most 4 models per device. Every device on which this
 // library's module is loaded holds the array (about 50 MiB) until the process exits; with CUDA's
 // default lazy module loading that starts at the first call on the device. Every call shares the
 // array and it keeps the last call's contents, so each call rewrites all the metadata it reads and
@@ -46,17 +46,19 @@ constexpr size_t kNaMaxRecord = 24ull << 20;    // stored record bytes
 constexpr size_t kNaMaxSlab = 24ull << 20;      // decoded bytes (decode layout)
 constexpr uint32_t kNaMaxStreams = 32768;
 constexpr int kNaModels = 4;
+constexpr uint32_t kNaMaxItems = kNaMaxStreams / 32u + 64u + (uint32_t)(kNaMaxSlab / kCommitChunk) + 8u;
 // byte layout of the array
 constexpr size_t kNaRec = 0;                                          // one Nr3Record
 constexpr size_t kNaJob = al256(sizeof(Nr3Record));                   // one CommitJob
 constexpr size_t kNaErr = kNaJob + al256(sizeof(CommitJob));          // the error word
-constexpr size_t kNaTasks = kNaErr + 256;                             // CTA tasks (at most one per stream)
-constexpr size_t kNaOffs = kNaTasks + al256((size_t)kNaMaxStreams * sizeof(Nr3Task));
+constexpr size_t kNaCounters = kNaErr + 256;                          // the queue head, then 4 counters
+constexpr size_t kNaItems = kNaCounters + 256;                        // the work queue
+constexpr size_t kNaOffs = kNaItems + al256((size_t)kNaMaxItems * sizeof(Nr3Item));
 constexpr size_t kNaMeta = kNaOffs + al256(((size_t)kNaMaxStreams + 1) * 4);   // per-call metadata ends here
 constexpr size_t kNaTableStride = al256(kTableBytes);
 constexpr size_t kNaTables = al256(kNaMeta);
 constexpr size_t kNaRecord = kNaTables + kNaModels * kNaTableStride;
-constexpr size_t kNaSlab = kNaRecord + kNaMaxRecord;
+constexpr size_t kNaSlab = kNaRecord + al256(kNaMaxRecord + kRecordSlack);
 constexpr size_t kNaBytes = kNaSlab + kNaMaxSlab;
 
 static __device__ __align__(256) uint8_t g_na_scratch[kNaBytes];
@@ -130,41 +132,34 @@ WEXB_API int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned
         }
         g_na_slot[device][slot] = p.model_id;
     }
-    uint8_t *const tab = base + kNaTables + slot * kNaTableStride;
-    const Nr3Tables t{tab, tab + kWTableBytes, reinterpret_cast<const uint16_t *>(tab + kWTableBytes + kSsymBytes)};
+    const uint8_t *const tab = base + kNaTables + slot * kNaTableStride;
+    const int sms = device_sms(device);
+    if (!sms) return 1;
     // this call's metadata, written in full (the array keeps the previous call's bytes)
     plan_offsets(p, reinterpret_cast<uint32_t *>(g_na_host + kNaOffs));
-    Nr3Task *tasks = reinterpret_cast<Nr3Task *>(g_na_host + kNaTasks);
-    uint32_t ns = 0, nw = 0;
-    const uint32_t wthreads = (uint32_t)weight_threads();
-    for (uint32_t m = 0; m < 3; ++m) {
-        const uint32_t n = (p.scount[m] + p.schunk - 1) / p.schunk;
-        for (uint32_t f = 0; f < n; f += kScaleThreads) tasks[ns++] = {0, m, f, std::min<uint32_t>(kScaleThreads, n - f)};
-    }
-    for (uint32_t m = 0; m < 3; ++m) {
-        const uint32_t n = (p.wcount[m] + p.wchunk - 1) / p.wchunk;
-        for (uint32_t f = 0; f < n; f += wthreads) tasks[ns + nw++] = {0, m, f, std::min<uint32_t>(wthreads, n - f)};
-    }
+    const Plan *plans[1] = {&p};
+    LaunchSet launch;
+    launch.plan(plans, &tab, 1, true);
+    if (launch.items > kNaMaxItems) return -2;   // not reached within the stream and slab limits above
+    launch.fill(plans, true, sms, reinterpret_cast<Nr3Item *>(g_na_host + kNaItems),
+                reinterpret_cast<uint32_t *>(g_na_host + kNaCounters));
     uint32_t *derr = reinterpret_cast<uint32_t *>(base + kNaErr);
-    plan_descriptor(p, t, base + kNaRecord, reinterpret_cast<const uint32_t *>(base + kNaOffs), base + kNaSlab, derr,
+    const CommitJob *djob = reinterpret_cast<const CommitJob *>(base + kNaJob);
+    plan_descriptor(p, base + kNaRecord, reinterpret_cast<const uint32_t *>(base + kNaOffs), base + kNaSlab, derr, djob,
                     reinterpret_cast<Nr3Record *>(g_na_host + kNaRec));
     CommitJob *job = reinterpret_cast<CommitJob *>(g_na_host + kNaJob);
     for (int m = 0; m < 3; ++m) {
         job->src[m] = base + kNaSlab + p.soff[m]; job->dst[m] = dst_scale[m]; job->bytes[m] = p.dst_bytes[m];
         job->src[3 + m] = base + kNaSlab + p.wout[m]; job->dst[3 + m] = dst_weight[m]; job->bytes[3 + m] = p.dst_bytes[3 + m];
     }
-    job->error = derr;
     *reinterpret_cast<uint32_t *>(g_na_host + kNaErr) = 0;   // the error word starts at zero every call
     const size_t meta_bytes = kNaOffs + 4ull * (p.streams() + 1);
-    const Nr3Record *drec = reinterpret_cast<const Nr3Record *>(base + kNaRec);
-    const Nr3Task *dtasks = reinterpret_cast<const Nr3Task *>(base + kNaTasks);
     uint32_t &error = g_na_word[0];
     error = ~0u;
     const bool ok = cudaMemcpyAsync(base + kNaRecord, record, p.total, cudaMemcpyHostToDevice, st) == cudaSuccess &&
                     cudaMemcpyAsync(base, g_na_host, meta_bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
-                    launch_nr3_scales(drec, dtasks, ns, st) == cudaSuccess &&
-                    launch_nr3_weights(drec, dtasks + ns, nw, (int)wthreads, st) == cudaSuccess &&
-                    launch_commit(reinterpret_cast<const CommitJob *>(base + kNaJob), 1, st) == cudaSuccess &&
+                    launch.launch(reinterpret_cast<const Nr3Record *>(base + kNaRec), reinterpret_cast<const Nr3Item *>(base + kNaItems),
+                                  reinterpret_cast<uint32_t *>(base + kNaCounters), sms, st) &&
                     cudaMemcpyAsync(&error, derr, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     const Waited waited = wait_stream(st);   // also after a failed step: whatever was queued must end
     if (!ok || waited != Waited::Done) { (void)cudaGetLastError(); return 1; }

@@ -3,6 +3,7 @@
 
 #include <cstring>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -34,11 +35,11 @@ uint32_t fnv1a(const uint8_t *p, size_t n) {
     return h ? h : 1u;
 }
 
-// Table image: per matrix the two-level weight block (wnr3.cuh), then ssym [3][16384 u8], scdf [3][528 B].
+// Table image (wnr3.cuh): per matrix the two-level weight block, then ssym [3][16384 u8], then sf [3][256 u32].
 void build_image(const uint8_t *blob, std::vector<uint8_t> &img) {
     img.assign(kTableBytes, 0);
     uint8_t *ssym = img.data() + kWTableBytes;
-    uint8_t *scdf = img.data() + kWTableBytes + kSsymBytes;
+    uint32_t *sf = reinterpret_cast<uint32_t *>(img.data() + kWTableBytes + kSsymBytes);
     for (uint32_t m = 0; m < 3; ++m) {
         uint32_t *l1 = reinterpret_cast<uint32_t *>(img.data() + (size_t)m * kWBlockBytes);
         uint32_t *l2 = reinterpret_cast<uint32_t *>(img.data() + (size_t)m * kWBlockBytes + kWL1Bytes);
@@ -67,8 +68,8 @@ void build_image(const uint8_t *blob, std::vector<uint8_t> &img) {
         for (uint32_t s = 0; s < 256; ++s) {
             const uint32_t lo = rd16(c + 2 * s), hi = rd16(c + 2 * s + 2);
             for (uint32_t slot = lo; slot < hi; ++slot) ssym[m * kTotal + slot] = (uint8_t)s;
+            sf[m * 256u + s] = lo | (hi - lo) << 16;
         }
-        std::memcpy(scdf + (size_t)m * kScdfBytes, c, 514);
     }
 }
 Model *find_locked(uint32_t id) {
@@ -108,7 +109,7 @@ bool model_registered(uint32_t id) {
     return find_locked(id) != nullptr;
 }
 
-int model_tables(uint32_t id, int device, Nr3Tables *out) {
+int model_tables(uint32_t id, int device, const uint8_t **out) {
     std::lock_guard<std::mutex> lock(g_models_mu);
     Model *m = find_locked(id);
     if (!m || device < 0 || device >= kMaxDevices) return 1;
@@ -124,10 +125,7 @@ int model_tables(uint32_t id, int device, Nr3Tables *out) {
         }
         m->dev[device] = p;
     }
-    uint8_t *p = m->dev[device];
-    out->wblk = p;
-    out->ssym = p + kWTableBytes;
-    out->scdf = reinterpret_cast<const uint16_t *>(p + kWTableBytes + kSsymBytes);
+    *out = m->dev[device];
     return 0;
 }
 
@@ -218,33 +216,108 @@ void plan_offsets(const Plan &p, uint32_t *off) {
     off[p.streams()] = at;
 }
 
-void plan_descriptor(const Plan &p, const Nr3Tables &t, const uint8_t *drec, const uint32_t *doff, uint8_t *dout,
-                     uint32_t *derr, Nr3Record *r) {
+void plan_descriptor(const Plan &p, const uint8_t *drec, const uint32_t *doff, uint8_t *dout, uint32_t *derr,
+                     const CommitJob *djob, Nr3Record *r) {
     std::memset(r, 0, sizeof *r);
-    r->rec = drec; r->offsets = doff; r->out = dout; r->error = derr; r->t = t;
+    r->rec = drec; r->offsets = doff; r->out = dout; r->error = derr; r->job = djob;
+    r->witems = 0;
     for (int m = 0; m < 3; ++m) {
         r->scount[m] = p.scount[m]; r->wcount[m] = p.wcount[m];
         r->soff[m] = p.soff[m]; r->wout[m] = p.wout[m];
         r->sbase[m] = p.sbase[m]; r->wbase[m] = p.wbase[m];
+        r->sitems[m] = ((p.scount[m] + p.schunk - 1) / p.schunk + 31) / 32;
+        r->witems += ((p.wcount[m] + p.wchunk - 1) / p.wchunk + 31) / 32;
     }
     r->schunk = p.schunk; r->wchunk = p.wchunk;
     r->model_id = p.model_id; r->owner = p.owner; r->word24 = p.word24; r->flags = p.flags;
 }
 
-void plan_tasks(const Plan &p, uint32_t rec, int wthreads, std::vector<Nr3Task> &stasks, std::vector<Nr3Task> &wtasks) {
-    for (uint32_t m = 0; m < 3; ++m) {
-        const uint32_t ns = (p.scount[m] + p.schunk - 1) / p.schunk, nw = (p.wcount[m] + p.wchunk - 1) / p.wchunk;
-        for (uint32_t f = 0; f < ns; f += kScaleThreads) stasks.push_back({rec, m, f, std::min<uint32_t>(kScaleThreads, ns - f)});
-        for (uint32_t f = 0; f < nw; f += (uint32_t)wthreads) wtasks.push_back({rec, m, f, std::min<uint32_t>(wthreads, nw - f)});
+namespace {
+uint32_t warp_items(uint32_t symbols, uint32_t chunk) { return ((symbols + chunk - 1) / chunk + 31) / 32; }
+uint32_t commit_items(const Plan &p) {
+    uint32_t n = 0;
+    for (int r = 0; r < 6; ++r) n += (p.dst_bytes[r] + kCommitChunk - 1) / kCommitChunk;
+    return n;
+}
+uint32_t weight_items(const Plan &p) {
+    uint32_t n = 0;
+    for (int m = 0; m < 3; ++m) n += warp_items(p.wcount[m], p.wchunk);
+    return n;
+}
+}  // namespace
+
+uint32_t queue_items(const Plan &p, bool commit) {
+    uint32_t n = weight_items(p) + (commit ? commit_items(p) : 0u);
+    for (int m = 0; m < 3; ++m) n += warp_items(p.scount[m], p.schunk);
+    return n;
+}
+
+uint32_t queue_fill(const Plan *const *plans, uint32_t n, bool commit, int sms, Nr3Item *items) {
+    uint32_t at = 0;
+    for (uint32_t r = 0; r < n; ++r)
+        for (uint32_t m = 0; m < 3; ++m)
+            for (uint32_t i = 0, k = warp_items(plans[r]->scount[m], plans[r]->schunk); i < k; ++i)
+                items[at++] = {r, item_what(kItemScale, m, 32u * i)};
+    // commits trail the decode by about one wave of warps (every warp of the device busy with weight items)
+    const uint32_t per_record = n ? std::max(1u, weight_items(*plans[0])) : 1u;
+    const uint32_t delay = (uint32_t)std::max(1, sms) * (kDecodeThreads / 32u) / per_record + 1u;
+    auto commits = [&](uint32_t r) {
+        for (uint32_t region = 0; region < 6; ++region)
+            for (uint32_t c = 0, k = (plans[r]->dst_bytes[region] + kCommitChunk - 1) / kCommitChunk; c < k; ++c)
+                items[at++] = {r, item_what(kItemCommit, region, c)};
+    };
+    for (uint32_t r = 0; r < n; ++r) {
+        for (uint32_t m = 0; m < 3; ++m)
+            for (uint32_t i = 0, k = warp_items(plans[r]->wcount[m], plans[r]->wchunk); i < k; ++i)
+                items[at++] = {r, item_what(kItemWeight, m, 32u * i)};
+        if (commit && r >= delay) commits(r - delay);
+    }
+    if (commit)
+        for (uint32_t r = n > delay ? n - delay : 0; r < n; ++r) commits(r);
+    return at;
+}
+
+void LaunchSet::plan(const Plan *const *plans, const uint8_t *const *tables, uint32_t k, bool commit) {
+    groups.clear();
+    items = 0;
+    records = k;
+    for (uint32_t j = 0; j < k; ++j) {
+        if (groups.empty() || groups.back().tables != tables[j]) groups.push_back({j, 0, items, 0, tables[j]});
+        Group &g = groups.back();
+        const uint32_t n = queue_items(*plans[j], commit);
+        ++g.nrecs;
+        g.nitems += n;
+        items += n;
     }
 }
 
-int weight_threads() {
-    static int v = [] {
-        const char *s = std::getenv("WEXB_WEIGHT_THREADS");
-        const int t = s ? std::atoi(s) : 256;
-        return t == 128 ? 128 : 256;
-    }();
+void LaunchSet::fill(const Plan *const *plans, bool commit, int sms, Nr3Item *items_out, uint32_t *counters) const {
+    for (const Group &g : groups) queue_fill(plans + g.first_rec, g.nrecs, commit, sms, items_out + g.first_item);
+    std::memset(counters, 0, 4 * counter_words());
+}
+
+bool LaunchSet::launch(const Nr3Record *drecs, const Nr3Item *ditems, uint32_t *dcounters, int sms, cudaStream_t st) const {
+    const size_t heads = groups.size();
+    for (size_t i = 0; i < heads; ++i) {
+        const Group &g = groups[i];
+        const Nr3Launch L{drecs + g.first_rec, ditems + g.first_item, dcounters + i, dcounters + heads + 4ull * g.first_rec,
+                          g.tables, g.nitems, g.nrecs};
+        if (launch_nr3(L, sms, st) != cudaSuccess) return false;
+    }
+    return true;
+}
+
+int device_sms(int device) {
+    static std::atomic<int> cache[kMaxDevices];
+    if (device < 0 || device >= kMaxDevices) return 0;
+    int v = cache[device].load();
+    if (!v) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return 0;
+        }
+        cache[device].store(v);
+    }
     return v;
 }
 

@@ -26,9 +26,9 @@ int model_validate(const uint8_t *blob, size_t bytes, uint32_t *id);
 // 0 registered (or already, same bytes), -1 invalid or id collision, 1 registry full.
 int model_register(const uint8_t *blob, size_t bytes);
 bool model_registered(uint32_t id);
-// Device tables of model `id` on `device` (the current device), built on first use: 0, or 1 when the
-// model is not registered or CUDA failed.
-int model_tables(uint32_t id, int device, Nr3Tables *out);
+// Device tables of model `id` on `device` (the current device; kTableBytes, wnr3.cuh), built on first
+// use: 0, or 1 when the model is not registered or CUDA failed.
+int model_tables(uint32_t id, int device, const uint8_t **out);
 // Host image (kTableBytes, the device table layout) of registered model `id`, or nullptr. Registered
 // models are never freed, so the pointer stays valid.
 const uint8_t *model_image(uint32_t id);
@@ -53,15 +53,40 @@ int entry_raw_sizes(const WexEntry *e, uint64_t *raw, uint64_t *aligned);
 int plan_record(const WexEntry *e, const uint8_t *rec, Plan *p);
 // Absolute record offsets of every stream, then the end: streams() + 1 words.
 void plan_offsets(const Plan &p, uint32_t *off);
-// Fills the device descriptor of a planned record.
-void plan_descriptor(const Plan &p, const Nr3Tables &t, const uint8_t *drec, const uint32_t *doff, uint8_t *dout,
-                     uint32_t *derr, Nr3Record *out);
-// Appends the CTA tasks of record `rec`: scale tasks of kScaleThreads streams, weight tasks of
-// `wthreads` streams.
-void plan_tasks(const Plan &p, uint32_t rec, int wthreads, std::vector<Nr3Task> &stasks, std::vector<Nr3Task> &wtasks);
+// Fills the device descriptor of a planned record: its record copy, stream offsets, decode layout,
+// error word and commit job (null: the decode layout is the output) on the device.
+void plan_descriptor(const Plan &p, const uint8_t *drec, const uint32_t *doff, uint8_t *dout, uint32_t *derr,
+                     const CommitJob *djob, Nr3Record *out);
 
-// Weight CTA size: WEXB_WEIGHT_THREADS (128 or 256), default 256.
-int weight_threads();
+// ---- the work queue of a launch (wnr3.cuh) ------------------------------------------------------
+// Items a record adds to a queue: its scale and weight items, and its commit items when `commit`.
+uint32_t queue_items(const Plan &p, bool commit);
+// Writes the queue of one launch over records 0 .. n-1 (their plans, all of one model) into items and
+// returns how many: every scale item first, record by record; then each record's weight items, with
+// the commit items of an earlier record after them (`delay` records back, about one wave of the
+// device's warps), and the commits still missing at the end.
+uint32_t queue_fill(const Plan *const *plans, uint32_t n, bool commit, int sms, Nr3Item *items);
+// SMs of a device (cached), or 0 when CUDA fails.
+int device_sms(int device);
+
+// The launches of one call: its records grouped by model (equal tables contiguous in call order), one
+// persistent launch per group. Counters: one head per group, then 4 words per record.
+struct LaunchSet {
+    struct Group { uint32_t first_rec, nrecs, first_item, nitems; const uint8_t *tables; };
+    std::vector<Group> groups;
+    uint32_t items = 0, records = 0;
+    // Groups records [0, k) by their tables (already ordered so that equal tables are contiguous).
+    void plan(const Plan *const *plans, const uint8_t *const *tables, uint32_t k, bool commit);
+    size_t counter_words() const { return groups.size() + 4ull * records; }
+    // Writes every group's queue (`items` entries) and zeroes the counters (counter_words()).
+    void fill(const Plan *const *plans, bool commit, int sms, Nr3Item *items_out, uint32_t *counters) const;
+    // Launches every group on st over the device copies of the records, items and counters.
+    bool launch(const Nr3Record *drecs, const Nr3Item *ditems, uint32_t *dcounters, int sms, cudaStream_t st) const;
+};
+// Slack a record buffer keeps after each record: a stream's payload window may read up to 12 bytes
+// past the stream's end (rans_device.cuh).
+constexpr size_t kRecordSlack = 64;
+
 // Reports an integrity failure once per process (c/tools/wex_cuda_bridge.cu:117-122).
 void report_error_bits(uint32_t bits);
 // The status of a record from its error word: 0 clean, -1 the record failed a check, 1 a bounded

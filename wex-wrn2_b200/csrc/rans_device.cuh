@@ -1,6 +1,6 @@
-// Device helpers shared by the rANS stream kernels (WNR3/WNR2 in wnr3_kernels.cu, WBP1 in
-// wbp1_kernels.cu): MurmurHash3 words, bounded mbarrier waits around TMA bulk copies, cp.async, and the
-// per-lane payload ring that one stream's decoder reads its bytes from.
+// Device helpers shared by the rANS stream kernels (WNR2/WNR3 in nr3_decode.cu, WBP1 in
+// wbp1_kernels.cu): MurmurHash3 words, bounded mbarrier waits around TMA bulk copies, and the payload
+// window through which one lane reads its stream's bytes.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -10,10 +10,7 @@
 namespace wexb {
 namespace rans {
 
-constexpr uint32_t kRingWords = 32;
-constexpr uint32_t kAhead = 24;
-constexpr uint32_t kSpinLimit = kWaitPolls;   // bounded waits: never spin forever on a barrier
-
+// ---- MurmurHash3_x86_32 (Austin Appleby's published algorithm), one 32-bit block at a time ---------
 __device__ __forceinline__ uint32_t rotl32(uint32_t x, int r) { return __funnelshift_l(x, x, r); }
 __device__ __forceinline__ uint32_t mm3_mix(uint32_t k) { return rotl32(k * 0xcc9e2d51u, 15) * 0x1b873593u; }
 __device__ __forceinline__ uint32_t mm3_block(uint32_t h, uint32_t k) { return rotl32(h ^ mm3_mix(k), 13) * 5u + 0xe6546b64u; }
@@ -22,7 +19,7 @@ __device__ __forceinline__ uint32_t mm3_final(uint32_t h, uint32_t len) {
     h ^= h >> 16; h *= 0x85ebca6bu; h ^= h >> 13; h *= 0xc2b2ae35u; h ^= h >> 16;
     return h;
 }
-// MurmurHash3 state after the stream's ident words {model, owner, g, word24}, seed "WNR3"
+// MurmurHash3 state after a WNR3 stream's ident words {model, owner, g, word24}, seed "WNR3"
 // (c/wex_neural_rans.h:225-233).
 __device__ __forceinline__ uint32_t ident_hash(uint32_t model, uint32_t owner, uint32_t g, uint32_t word24) {
     uint32_t h = 0x33524e57u;
@@ -30,33 +27,23 @@ __device__ __forceinline__ uint32_t ident_hash(uint32_t model, uint32_t owner, u
     return mm3_block(h, word24);
 }
 
-// ---- async copies ----------------------------------------------------------------------------
-__device__ __forceinline__ void cp4(uint32_t *dst, const uint32_t *src, bool pred) {
-    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %2, 0;\n @p cp.async.ca.shared.global [%0], [%1], 4;\n}\n"
-                 :: "r"(d), "l"(src), "r"((int)pred) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
-
+// ---- TMA bulk copies into shared memory, completed on an mbarrier, waited for with a limit --------
+__device__ __forceinline__ unsigned smem_addr(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" :: "r"((unsigned)__cvta_generic_to_shared(bar)), "r"(count) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" :: "r"(smem_addr(bar)), "r"(count) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
 }
 __device__ __forceinline__ void mbar_expect(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n"
-                 :: "r"((unsigned)__cvta_generic_to_shared(bar)), "r"(bytes) : "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
 }
-// TMA bulk copy global -> this CTA's shared memory, completing `bytes` on the mbarrier. Both
-// addresses 16-byte aligned, bytes a multiple of 16 (every table block here is).
+// Global -> this CTA's shared memory; both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
-                 :: "r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src), "r"(bytes),
-                    "r"((unsigned)__cvta_generic_to_shared(bar)) : "memory");
+                 :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
 }
-// Waits for phase `parity` of the mbarrier, at most `limit` polls; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = kSpinLimit) {
-    const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+// Waits for phase `parity` of the mbarrier, at most `limit` polls; false when it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = kWaitPolls) {
+    const unsigned a = smem_addr(bar);
     for (uint32_t i = 0; i < limit; ++i) {
         uint32_t done;
         asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -66,8 +53,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     return false;
 }
 
-// Stages `n` blocks of table bytes into shared memory with TMA; every thread returns once they
-// landed (or, after a bounded wait, with false).
+// Stages `n` blocks of table bytes into shared memory with TMA; every thread of the CTA returns once
+// they landed, or false after a bounded wait (the copies may then still be in flight: the caller
+// reports kErrTimeout, which the host turns into status 1, and never reads the tables).
 __device__ __forceinline__ bool stage_tables(uint64_t *bar, void *const *dst, const void *const *src,
                                              const uint32_t *bytes, int n) {
     if (threadIdx.x == 0) mbar_init(bar, 1);
@@ -81,59 +69,153 @@ __device__ __forceinline__ bool stage_tables(uint64_t *bar, void *const *dst, co
     return mbar_wait(bar, 0);
 }
 
-// ---- one stream's payload: a per-lane ring in shared memory ------------------------------------
-struct Reader {
-    uint32_t *lane;          // this lane's ring base; word w lives at lane[(w % kRingWords) * stride]
-    uint32_t stride;
-    const uint32_t *src;     // the record as 32-bit words (4-byte aligned)
-    uint32_t pos;            // record offset of the next payload byte
-    uint32_t req;            // next word to request
-    uint32_t last;           // the stream's last word
+// ---- one stream's payload, as its lane sees it -----------------------------------------------------
+// The stream's bytes go through a window of kWinWords words in shared memory, laid out across the
+// CTA's lanes: word w of the stream (counted from its first 4-byte aligned word) sits in slot
+// w % kWinWords of the lane, slot s of lane l at ring[s * lanes + l], so every shared access of a warp
+// is conflict-free whatever position each lane has reached. Slot kWinWords repeats slot 0, so the two
+// words under any position are adjacent slots with no wrap.
+//
+// Words arrive in groups of 4 by 4-byte cp.async copies (the stream's bytes are not 16-byte aligned,
+// and the transposed layout needs word-sized pieces). Each top_up() keeps at least 12 words requested
+// ahead of the read position and waits for all but the newest group; it is called before every 8
+// symbols, which read at most 16 bytes. A group is requested whole even when it ends past the stream's
+// last word, so a stream's reads run at most 12 bytes past its end (record buffers carry that slack);
+// bytes past the end are never valid data: a decoder that reaches them fails its final position check.
+constexpr uint32_t kWinWords = 16;
 
-    __device__ __forceinline__ uint32_t *slot(uint32_t w) const { return lane + (w & (kRingWords - 1)) * stride; }
+// Shared-memory accesses by 32-bit shared-window address. Table loads may be reordered freely (the
+// tables do not change once staged); payload loads are volatile asm, which the compiler keeps in order
+// with the (volatile) cp.async waits.
+__device__ __forceinline__ uint32_t lds_u8(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u8 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+    uint2 v;
+    asm("ld.shared.v2.u32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_payload(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(a));
+    return v;
+}
 
-    // Opens [begin, end) (length >= 4, checked on the host) and returns its initial state.
-    __device__ __forceinline__ uint32_t open(uint32_t begin, uint32_t end) {
-        const uint32_t first = begin >> 2;
-        last = (end - 1) >> 2;
-        const uint32_t target = min(first + kAhead, last + 1);
-        for (uint32_t w = first; w < target; ++w) cp4(slot(w), src + w, true);
-        req = target;
-        cp_commit();
-        cp_wait<0>();
-        const uint32_t v = __funnelshift_r(*slot(first), *slot(first + 1), (begin & 3u) * 8u);
-        pos = begin + 4;
-        return __byte_perm(v, 0, 0x0123);   // big-endian bytes begin .. begin + 3
-    }
-    // Every 16 symbols (at most 32 bytes): keep kAhead words requested, then wait for the words of
-    // the previous request, which cover every byte the next 16 symbols can read.
-    __device__ __forceinline__ void refill() {
-        const uint32_t target = min((pos >> 2) + kAhead, last + 1);
+__device__ __forceinline__ void cp_async4(uint32_t dst, const uint32_t *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" :: "r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
+
+template <int kLanes>
+struct PayloadWindow {
+    static constexpr uint32_t kStride = 4u * kLanes;   // bytes from one slot of a lane to its next
+    uint32_t slots;           // shared address of this lane's slot 0
+    const uint32_t *words;    // the stream's first aligned word
+    uint32_t bit;             // bit position of the next unread byte, from `words`
+    uint32_t ask;             // next word to request (a multiple of 4)
+    uint32_t stop;            // words at or past this are never requested (one past the stream's last word)
+
+    __device__ __forceinline__ void request_group() {
+        const uint32_t s = ask % kWinWords;
+        const uint32_t d = slots + s * kStride;
+        const uint32_t *g = words + ask;
 #pragma unroll
-        for (uint32_t k = 0; k < 8; ++k) {
-            const uint32_t w = req + k;
-            cp4(slot(w), src + w, w < target);
-        }
-        req = max(req, min(req + 8, target));
-        cp_commit();
-        cp_wait<1>();
+        for (int k = 0; k < 4; ++k) cp_async4(d + k * kStride, g + k);
+        if (s == 0) cp_async4(slots + kWinWords * kStride, g);   // the mirror of slot 0
+        ask += 4;
     }
-    // The next two payload bytes as a big-endian pair in bits 16..31 (read before the lookup, so
-    // the shared loads overlap it). Past the stream's end the ring holds stale words: consuming
-    // them is caught by the final pos == end check.
-    __device__ __forceinline__ uint32_t peek() const {
-        const uint32_t w = pos >> 2;
-        return __byte_perm(__funnelshift_r(*slot(w), *slot(w + 1), (pos & 3u) * 8u), 0, 0x0144);
+    // Opens the stream of record bytes [begin, end) (length >= 4, checked on the host) and returns its
+    // initial state, the big-endian word at begin. lane_slots: shared address of the lane's slot 0.
+    __device__ __forceinline__ uint32_t open(const uint8_t *rec, uint32_t begin, uint32_t end, uint32_t lane_slots) {
+        slots = lane_slots;
+        words = reinterpret_cast<const uint32_t *>(rec) + (begin >> 2);
+        stop = ((end + 3u) >> 2) - (begin >> 2);
+        ask = 0;
+        for (int k = 0; k < 3; ++k)
+            if (ask < stop) request_group();
+        cp_async_commit();
+        cp_async_wait<0>();
+        bit = (begin & 3u) * 8u;
+        const uint32_t v = take32();
+        bit += 32;
+        return v;
     }
-    // Waits for every copy this lane still has in flight (before the lane returns).
-    __device__ __forceinline__ void drain() const { cp_wait<0>(); }
-    // while (x < L) x = x << 8 | next byte, as one funnel shift of 0, 8 or 16 bits.
-    __device__ __forceinline__ uint32_t renorm(uint32_t x, uint32_t two) {
-        const uint32_t bits = x < (1u << 15) ? 16u : (x < kRansL ? 8u : 0u);
-        pos += bits >> 3;
-        return __funnelshift_l(two, x, bits);
+    // Before each 8 symbols: a new group when fewer than 12 words are requested ahead.
+    __device__ __forceinline__ void top_up() {
+        if (ask < stop && ask - (bit >> 5) < 12u) request_group();
+        cp_async_commit();
+        cp_async_wait<1>();
     }
+    // The 4 bytes at the read position, big-endian (the first byte in bits 24..31).
+    __device__ __forceinline__ uint32_t take32() const {
+        const uint32_t a = slots + ((bit >> 5) % kWinWords) * kStride;
+        return __byte_perm(__funnelshift_r(lds_payload(a), lds_payload(a + kStride), bit), 0, 0x0123);
+    }
+    // Byte offset of the read position from the stream's first aligned word.
+    __device__ __forceinline__ uint32_t byte_pos() const { return bit >> 3; }
+    // Waits for every copy this lane still has in flight (before the lane leaves the stream).
+    __device__ __forceinline__ void close() const { cp_async_wait<0>(); }
 };
+
+// Bits (0, 8 or 16) a state in [2^9, 2^31) shifts in until it is at least 2^23.
+__device__ __forceinline__ uint32_t renorm_bits(uint32_t x) { return ((uint32_t)__clz(x) - 1u) & 24u; }
+
+// Decodes `count` order-0 byte symbols of one stream (the WNR3 scale coder, also WBP1's coded planes):
+// slot -> symbol from the shared table at `ssym` (16,384 bytes), the symbol's start | freq << 16 from
+// the shared table at `sf` (256 words). The bytes go to out (4-byte stores when out is 4-byte aligned)
+// and through the MurmurHash3 state h, the last partial word as a hash tail. Returns the final state.
+template <int kLanes>
+__device__ __forceinline__ uint32_t order0_stream(PayloadWindow<kLanes> &pw, uint32_t x, uint32_t ssym, uint32_t sf,
+                                                  uint32_t count, uint8_t *out, uint32_t &h) {
+    const bool words_ok = !(reinterpret_cast<uintptr_t>(out) & 3u);
+    uint32_t i = 0;
+    for (; i + 8 <= count; i += 8) {
+        pw.top_up();
+        uint32_t word[2] = {0, 0};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t win = pw.take32();
+            const uint32_t slot = x & (kTotal - 1u), sym = lds_u8(ssym + slot), e = lds_u32(sf + 4u * sym);
+            x = (e >> 16) * (x >> kPrec) + slot - (e & 0xffffu);
+            const uint32_t b = renorm_bits(x);
+            x = __funnelshift_l(win, x, b);
+            pw.bit += b;
+            word[k >> 2] |= sym << (8 * (k & 3));
+        }
+        h = mm3_block(mm3_block(h, word[0]), word[1]);
+        if (words_ok) {
+            reinterpret_cast<uint32_t *>(out + i)[0] = word[0];
+            reinterpret_cast<uint32_t *>(out + i)[1] = word[1];
+        } else {
+            for (int k = 0; k < 8; ++k) out[i + k] = (uint8_t)(word[k >> 2] >> (8 * (k & 3)));
+        }
+    }
+    if (i < count) {   // the last stream of a matrix or plane: fewer than 8 symbols left
+        pw.top_up();
+        uint32_t word = 0, held = 0;
+        for (; i < count; ++i) {
+            const uint32_t win = pw.take32();
+            const uint32_t slot = x & (kTotal - 1u), sym = lds_u8(ssym + slot), e = lds_u32(sf + 4u * sym);
+            x = (e >> 16) * (x >> kPrec) + slot - (e & 0xffffu);
+            const uint32_t b = renorm_bits(x);
+            x = __funnelshift_l(win, x, b);
+            pw.bit += b;
+            out[i] = (uint8_t)sym;
+            word |= sym << (8 * held);
+            if (++held == 4) { h = mm3_block(h, word); word = 0; held = 0; }
+        }
+        if (held) h ^= mm3_mix(word);   // MurmurHash3's tail: the last 1-3 bytes, mixed without a round
+    }
+    return x;
+}
 
 }  // namespace rans
 }  // namespace wexb

@@ -2,10 +2,11 @@
 //
 // wbp1_streams: a CTA serves one plane of one record. For a rANS plane it first builds the
 // slot -> symbol table of the record's CDF in shared memory (each thread 64 consecutive slots: one
-// binary search, then a walk), then every lane decodes one stream from a per-lane payload ring
-// (rans::Reader), hashing the decoded bytes as it stores them; for a raw plane every lane copies one
-// chunk and checks its MurmurHash3 word. wbp1_join writes each element's P bytes as one store,
-// rotating it right by one bit under transform 1.
+// binary search, then a walk) and the packed start | freq << 16 word of every symbol, then every lane
+// decodes one stream through its payload window with the order-0 stream decoder the WNR3 scale
+// streams use (rans_device.cuh), hashing the decoded bytes as it stores them; for a raw plane every
+// lane copies one chunk and checks its MurmurHash3 word. wbp1_join writes each element's P bytes as
+// one store, rotating it right by one bit under transform 1.
 #include "wnr3.cuh"
 #include "rans_device.cuh"
 #include "wbp1.cuh"
@@ -16,7 +17,8 @@ namespace {
 using namespace rans;
 
 constexpr uint32_t kCdfBytes = 528;   // 257 u16, padded
-constexpr size_t kStreamSmem = kTotal + kCdfBytes + (size_t)kRingWords * 4u * kWbp1Threads;
+constexpr uint32_t kSfWords = 256;
+constexpr size_t kStreamSmem = kTotal + kCdfBytes + 4u * kSfWords + (size_t)(kWinWords + 1) * 4u * kWbp1Threads;
 
 __device__ __forceinline__ uint32_t ident_hash(uint32_t owner, uint32_t g, uint32_t word) {
     uint32_t h = 0x33524e57u;
@@ -32,7 +34,8 @@ __global__ void __launch_bounds__(kWbp1Threads) wbp1_streams(const Wbp1Record *_
     extern __shared__ __align__(16) uint8_t smem[];
     uint8_t *ssym = smem;
     uint16_t *cdf = reinterpret_cast<uint16_t *>(smem + kTotal);
-    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kTotal + kCdfBytes);
+    uint32_t *sf = reinterpret_cast<uint32_t *>(smem + kTotal + kCdfBytes);
+    uint32_t *ring = reinterpret_cast<uint32_t *>(smem + kTotal + kCdfBytes + 4u * kSfWords);
     const Wbp1Task task = tasks[blockIdx.x];
     const Wbp1Record &R = recs[task.rec];
     const uint32_t p = task.plane;
@@ -49,6 +52,7 @@ __global__ void __launch_bounds__(kWbp1Threads) wbp1_streams(const Wbp1Record *_
                 ssym[base + k] = (uint8_t)lo;
             }
         }
+        for (uint32_t i = threadIdx.x; i < kSfWords; i += blockDim.x) sf[i] = cdf[i] | (uint32_t)(cdf[i + 1] - cdf[i]) << 16;
         __syncthreads();
     }
     if (threadIdx.x >= task.count) return;
@@ -73,42 +77,14 @@ __global__ void __launch_bounds__(kWbp1Threads) wbp1_streams(const Wbp1Record *_
         if (mm3_final(h, 16u + count) != rd32_bytes(R.rec + R.table_at[p] + 4ull * s)) atomicOr(R.error, kErrHash);
         return;
     }
-    Reader rd{ring + threadIdx.x, blockDim.x, reinterpret_cast<const uint32_t *>(R.rec), 0, 0, 0};
-    uint32_t x = rd.open(begin, end);
-    if (x < kRansL || x >= (kRansL << 8)) { atomicOr(R.error, kErrStruct); rd.drain(); return; }
-    const uint32_t full = count & ~15u;
-    for (uint32_t i = 0; i < full; i += 16) {
-        rd.refill();
-#pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) {
-            uint32_t word = 0;
-#pragma unroll
-            for (uint32_t k = 0; k < 4; ++k) {
-                const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), y = ssym[slot], start = cdf[y];
-                word |= y << (8u * k);
-                x = (cdf[y + 1] - start) * (x >> kPrec) + slot - start;
-                x = rd.renorm(x, two);
-            }
-            h = mm3_block(h, word);
-            *reinterpret_cast<uint32_t *>(out + i + 4u * q) = word;
-        }
-    }
-    if (full < count) {   // the stream's last partial group of 16
-        rd.refill();
-        uint32_t word = 0, held = 0;
-        for (uint32_t i = full; i < count; ++i) {
-            const uint32_t two = rd.peek(), slot = x & (kTotal - 1u), y = ssym[slot], start = cdf[y];
-            out[i] = (uint8_t)y;
-            word |= y << (8u * held);
-            x = (cdf[y + 1] - start) * (x >> kPrec) + slot - start;
-            x = rd.renorm(x, two);
-            if (++held == 4) { h = mm3_block(h, word); word = 0; held = 0; }
-        }
-        if (held) h ^= mm3_mix(word);
-    }
-    rd.drain();
-    if (rd.pos != end) atomicOr(R.error, kErrStruct);
-    else if (x != kRansL + (mm3_final(h, 16u + count) & 0x7fffffu)) atomicOr(R.error, kErrHash);
+    PayloadWindow<kWbp1Threads> pw;
+    uint32_t x = pw.open(R.rec, begin, end, smem_addr(ring + threadIdx.x));
+    uint32_t err = (x - kRansL >= 255u * kRansL) ? kErrStruct : 0u;   // a valid initial state is in [L, 256 L)
+    x = order0_stream(pw, x, smem_addr(ssym), smem_addr(sf), count, out, h);
+    pw.close();
+    if (pw.byte_pos() != end - (begin & ~3u)) err |= kErrStruct;
+    else if (x != kRansL + (mm3_final(h, 16u + count) & 0x7fffffu)) err |= kErrHash;
+    if (err) atomicOr(R.error, err);
 }
 
 // Element e of a record: byte p from plane p; under transform 1 the element (little-endian, P bytes)

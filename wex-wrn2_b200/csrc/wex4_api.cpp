@@ -8,6 +8,7 @@
 #include <sys/mman.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -353,7 +354,7 @@ struct Job {
     int pre = OK;                          // a host verdict that precedes the GPU (WEX4_E_*)
     bool nr3 = false;
     Plan plan{};
-    Nr3Tables tabs{};
+    const uint8_t *tabs = nullptr;          // device tables of its WNM2 model
     bool w4 = false;                       // a codec-8 (WNR4 kind MX) expert slab
     W4Geo geo{};
     W4Tables w4tab{};
@@ -469,18 +470,16 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     }
     std::vector<size_t> at(jobs.size()), scr(jobs.size()), offs(jobs.size());
     size_t stage_bytes = 0, out_bytes = 0, scr_bytes = 0, noffs = 0;
-    std::vector<Nr3Task> stasks, wtasks;
     std::vector<size_t> nr3_of, w4_of, bp_of;   // job index of each WNR3 / WNR4 / WBP1 descriptor
     std::vector<size_t> bp_scr(jobs.size()), bp_offs(jobs.size());
     std::vector<Wbp1Task> bptasks;
     for (size_t i = 0; i < jobs.size(); ++i) {
         Job &j = jobs[i];
         if (j.pre != OK) continue;
-        at[i] = stage_bytes; stage_bytes += align_up(j.rec.stored, 256);
+        at[i] = stage_bytes; stage_bytes += align_up(j.rec.stored + kRecordSlack, 256);
         if (j.nr3) {
             scr[i] = scr_bytes; scr_bytes += align_up(j.plan.scratch, 256);
             offs[i] = noffs; noffs += j.plan.streams() + 1;
-            plan_tasks(j.plan, (uint32_t)nr3_of.size(), weight_threads(), stasks, wtasks);
             nr3_of.push_back(i);
             out_bytes += align_up(j.rec.decoded, 256);
         }
@@ -496,6 +495,15 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     }
     const size_t kb = bp_of.size();
     const size_t n = jobs.size(), k = nr3_of.size(), k4 = w4_of.size();
+    // WNR3 records: one persistent launch per model, its records contiguous
+    std::stable_sort(nr3_of.begin(), nr3_of.end(), [&](size_t a, size_t b) { return jobs[a].tabs < jobs[b].tabs; });
+    std::vector<const Plan *> nr3_plans(k);
+    std::vector<const uint8_t *> nr3_tabs(k);
+    for (size_t q = 0; q < k; ++q) { nr3_plans[q] = &jobs[nr3_of[q]].plan; nr3_tabs[q] = jobs[nr3_of[q]].tabs; }
+    LaunchSet launches;
+    launches.plan(nr3_plans.data(), nr3_tabs.data(), (uint32_t)k, true);
+    const int sms = k ? device_sms(device) : 1;
+    if (!sms) return false;
     // codec-8 tiles, planned from the host bytes against the staged copies, grouped by model
     std::vector<W4Rec> w4info(k4);
     std::vector<W4Job> w4jobs;
@@ -526,8 +534,8 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     }
     size_t m = 0;
     auto take = [&](size_t bytes) { size_t a = m; m = align_up(m + bytes, 256); return a; };
-    const size_t o_recs = take(k * sizeof(Nr3Record)), o_st = take(stasks.size() * sizeof(Nr3Task)),
-                 o_wt = take(wtasks.size() * sizeof(Nr3Task)), o_jobs = take(k * sizeof(CommitJob)),
+    const size_t o_recs = take(k * sizeof(Nr3Record)), o_items = take(launches.items * sizeof(Nr3Item)),
+                 o_counters = take(launches.counter_words() * 4), o_jobs = take(k * sizeof(CommitJob)),
                  o_sha = take(n * sizeof(ShaMsg)), o_exp = take(n * 32), o_zero = take(n * sizeof(ZeroJob)),
                  o_err = take(n * 4), o_ver = take(n * 4), o_offs = take(noffs * 4),
                  o_w4rec = take(k4 * sizeof(W4Rec)), o_w4job = take(w4jobs.size() * sizeof(W4Job)),
@@ -558,8 +566,9 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
         Job &j = jobs[nr3_of[q]];
         const size_t i = nr3_of[q];
         plan_offsets(j.plan, reinterpret_cast<uint32_t *>(hm + o_offs) + offs[i]);
-        plan_descriptor(j.plan, j.tabs, S.stage.p + at[i], reinterpret_cast<const uint32_t *>(dm + o_offs) + offs[i],
-                        S.scratch.p + scr[i], derr + i, reinterpret_cast<Nr3Record *>(hm + o_recs) + q);
+        plan_descriptor(j.plan, S.stage.p + at[i], reinterpret_cast<const uint32_t *>(dm + o_offs) + offs[i],
+                        S.scratch.p + scr[i], derr + i, reinterpret_cast<const CommitJob *>(dm + o_jobs) + q,
+                        reinterpret_cast<Nr3Record *>(hm + o_recs) + q);
         j.out_dev = S.out.p + out_at; out_at += align_up(j.rec.decoded, 256);
         CommitJob &J = reinterpret_cast<CommitJob *>(hm + o_jobs)[q];
         for (int mm = 0; mm < 3; ++mm) {
@@ -569,8 +578,8 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
             J.dst[3 + mm] = j.out_dev + j.plan.scale_bytes + (j.plan.wout[mm] - j.plan.weight_at);
             J.bytes[3 + mm] = j.plan.dst_bytes[3 + mm];
         }
-        J.error = derr + i;
     }
+    launches.fill(nr3_plans.data(), true, sms, reinterpret_cast<Nr3Item *>(hm + o_items), reinterpret_cast<uint32_t *>(hm + o_counters));
     for (W4Job &t : w4jobs)
         if (t.tile) t.tile = S.stage.p + reinterpret_cast<uintptr_t>(t.tile);
     for (size_t q = 0; q < k4; ++q) {
@@ -592,8 +601,6 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     if (!bptasks.empty()) std::memcpy(hm + o_bptask, bptasks.data(), bptasks.size() * sizeof(Wbp1Task));
     if (k4) std::memcpy(hm + o_w4rec, w4info.data(), k4 * sizeof(W4Rec));
     if (!w4jobs.empty()) std::memcpy(hm + o_w4job, w4jobs.data(), w4jobs.size() * sizeof(W4Job));
-    std::memcpy(hm + o_st, stasks.data(), stasks.size() * sizeof(Nr3Task));
-    std::memcpy(hm + o_wt, wtasks.data(), wtasks.size() * sizeof(Nr3Task));
     cudaStream_t st = S.st;
     const size_t groups = kShaStreams, per_group = (n + groups - 1) / groups;
     bool ok = S.events(groups + kShaStreams) && cudaMemcpyAsync(dm, hm, m, cudaMemcpyHostToDevice, st) == cudaSuccess;
@@ -616,9 +623,8 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     for (uint32_t z = 0; ok && z < nzero; z += 65535)
         ok = launch_zero_check(reinterpret_cast<const ZeroJob *>(dm + o_zero) + z, std::min<uint32_t>(65535, nzero - z), st) == cudaSuccess;
     const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + o_recs);
-    ok = ok && launch_nr3_scales(drecs, reinterpret_cast<const Nr3Task *>(dm + o_st), (uint32_t)stasks.size(), st) == cudaSuccess &&
-         launch_nr3_weights(drecs, reinterpret_cast<const Nr3Task *>(dm + o_wt), (uint32_t)wtasks.size(), weight_threads(), st) == cudaSuccess &&
-         launch_commit(reinterpret_cast<const CommitJob *>(dm + o_jobs), (uint32_t)k, st) == cudaSuccess;
+    ok = ok && launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + o_items), reinterpret_cast<uint32_t *>(dm + o_counters),
+                               sms, st);
     ok = ok && launch_wbp1_streams(reinterpret_cast<const Wbp1Record *>(dm + o_bprec),
                                    reinterpret_cast<const Wbp1Task *>(dm + o_bptask), (uint32_t)bptasks.size(), st) == cudaSuccess &&
          launch_wbp1_join(reinterpret_cast<const Wbp1Record *>(dm + o_bprec), (uint32_t)kb, st) == cudaSuccess;
