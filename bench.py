@@ -1260,8 +1260,8 @@ def measure_h2d_calls(torch, views, calls, reps=3):
 
 
 def profile_value(config, key):
-    """A figure of the weight kernel's committed ncu summary (a `key: value` line), if there is one."""
-    path = os.path.join(ROOT, 'profiles', f'nr3_weights_{config}.md')
+    """A figure of the decode kernel's committed ncu summary (a `key: value` line), if there is one."""
+    path = os.path.join(ROOT, 'profiles', f'nr3_decode_{config}.md')
     if not os.path.exists(path):
         return None
     for line in open(path):
@@ -1271,7 +1271,7 @@ def profile_value(config, key):
 
 
 def profile_traffic_per_record(config):
-    """DRAM bytes per record of the weight kernel from its committed ncu summary, if there is one."""
+    """DRAM bytes per record of the decode kernel from its committed ncu summary, if there is one."""
     v = profile_value(config, 'traffic_bytes_per_record')
     return int(v) if v else None
 
@@ -1503,8 +1503,6 @@ def run_gpu(args, cfg):
     # ---- bytes ----------------------------------------------------------------------------------
     dec_bytes = sum(experts[i].raw for s in range(args.warmup, steps_total) for i in step_idx[s])
     stored = sum(len(experts[i].record) for s in range(args.warmup, steps_total) for i in step_idx[s])
-    wpay = sum(int.from_bytes(experts[i].record[12:16], 'little') for s in range(args.warmup, steps_total)
-               for i in step_idx[s])
     wbytes = sum(int.from_bytes(experts[i].entry[16:20], 'little') + int.from_bytes(experts[i].entry[12:16], 'little')
                  for s in range(args.warmup, steps_total) for i in step_idx[s])
     totals = sum_over_ranks([dec_bytes, stored, k * args.steps], world)
@@ -1512,29 +1510,33 @@ def run_gpu(args, cfg):
     value = dec_all / (value_ms / 1e3) / 1e9
     e2e = dec_all / e2e_s / 1e9
     e2e_sync = dec_all / sync_s / 1e9
-    # roofline of the dominant kernel (weights): algorithmic bytes = weight payload read + packed
-    # weights written + scales read for the contexts, per launch, over its event-timed duration
-    wk = [m[1] for m in kernel_ms if m]
-    wk_ms = statistics.mean(wk) if wk else None
-    alg = (wpay + wbytes) / args.steps
+    # roofline of the decode launch (the only kernel of a step: scale, weight and commit items), from
+    # algorithmic bytes per launch = records read (stored bytes) + decode-layout slabs written + the
+    # error-gated commit (slabs read, destinations written), over its event-timed duration
+    dk = [m[1] for m in kernel_ms if m]
+    dk_ms = statistics.mean(dk) if dk else None
+    alg = (stored + 3 * dec_bytes) / args.steps
     peaks = json.load(open(MEASURED_PEAKS)) if os.path.exists(MEASURED_PEAKS) else {}
     hbm_peak = peaks.get('hbm_gbs', 6650.0)
-    achieved = alg / (wk_ms / 1e3) / 1e9 if wk_ms else None
+    achieved = alg / (dk_ms / 1e3) / 1e9 if dk_ms else None
     traffic_rec = profile_traffic_per_record(args.config)
     # the kernel's compute roofline: warp-instructions issued (the ncu count per warp and symbol of the
-    # committed profile x the launch's weight symbols / 32) over the event-timed duration, against the
-    # issue rate of every scheduler (4 per SM, one warp-instruction a cycle) at the sampled SM clock
+    # committed profile x the launch's symbols / 32) over the event-timed duration, against the issue rate
+    # of every scheduler (4 per SM, one warp-instruction a cycle) at the sampled SM clock
     ipws = profile_value(args.config, 'warp_instructions_per_warp_symbol')
     sms = torch.cuda.get_device_properties(local).multi_processor_count
     issue = None
-    if ipws and wk_ms and clk.get('sm_mhz'):
-        winstr = 2 * wbytes / args.steps / 32 * ipws
+    symbols = 2 * sum(int.from_bytes(experts[i].entry[16:20], 'little') for s in range(args.warmup, steps_total)
+                      for i in step_idx[s])   # two weight symbols per packed byte
+    if ipws and dk_ms and clk.get('sm_mhz'):
+        winstr = symbols / args.steps / 32 * ipws
         peak_issue = sms * 4 * clk['sm_mhz'] * 1e6
-        issue = {'bound': 'warp-instruction issue', 'achieved': round(winstr / (wk_ms / 1e3) / 1e12, 4),
+        issue = {'bound': 'warp-instruction issue', 'achieved': round(winstr / (dk_ms / 1e3) / 1e12, 4),
                  'peak': round(peak_issue / 1e12, 4), 'unit': 'T warp-instructions/s',
-                 'frac': round(winstr / (wk_ms / 1e3) / peak_issue, 4),
-                 'source': f'{ipws} warp-instructions per warp-symbol (ncu, committed profile) x weight symbols '
-                           f'/ 32; {sms} SMs x 4 schedulers at the median sampled SM clock'}
+                 'frac': round(winstr / (dk_ms / 1e3) / peak_issue, 4),
+                 'source': f'{ipws} warp-instructions per weight warp-symbol (ncu, committed profile, every item of '
+                           f'the launch counted) x weight symbols / 32; {sms} SMs x 4 schedulers at the median '
+                           f'sampled SM clock'}
     h2d_per_step = stored // args.steps + 0
     # rooflines of the two paths (per GPU): the resident decode against HBM (records read, slabs written
     # by the decoder and again by the commit copy), the end-to-end path against the measured H2D link
@@ -1570,15 +1572,18 @@ def run_gpu(args, cfg):
         'value_roofline': {'bound': 'hbm', 'achieved': round(hbm_bytes / step_s / 1e9, 2), 'peak': hbm_peak, 'unit': 'GB/s',
                            'frac': round(hbm_bytes / step_s / 1e9 / hbm_peak, 4),
                            'bytes': 'records read + slabs written by the decoder and by the commit copy'},
-        'roofline': {'bound': 'hbm', 'kernel': 'nr3_weights', 'achieved': round(achieved, 2) if achieved else None,
+        'roofline': {'bound': 'hbm', 'kernel': 'nr3_decode', 'achieved': round(achieved, 2) if achieved else None,
                      'peak': hbm_peak, 'unit': 'GB/s', 'frac': round(achieved / hbm_peak, 5) if achieved else None,
                      'peak_source': 'measured' if peaks else 'fallback',
                      'traffic': int(traffic_rec * k) if traffic_rec else None,
-                     'traffic_source': 'ncu dram__bytes_read.sum + dram__bytes_write.sum per record of a 64-record '
+                     'traffic_source': 'ncu dram__bytes_read.sum + dram__bytes_write.sum per record of a smaller '
                                        'launch, scaled to this launch' if traffic_rec else None,
-                     'kernel_ms': round(wk_ms, 4) if wk_ms else None,
+                     'kernel_ms': round(dk_ms, 4) if dk_ms else None,
                      'alg_bytes_per_launch': int(alg),
-                     'step_kernel_ms': [round(statistics.mean(m[i] for m in kernel_ms if m), 4) for i in range(3)],
+                     'alg_bytes': 'records read + decode-layout slabs written + commit (slabs read, destinations '
+                                  'written): stored + 3 x decoded bytes',
+                     'step_ms': dict(zip(('metadata_upload', 'decode', 'status_readback'),
+                                         [round(statistics.mean(m[i] for m in kernel_ms if m), 4) for i in range(3)])),
                      'issue': issue},
         'gpu_launches': launches,
         'clocks': clk,

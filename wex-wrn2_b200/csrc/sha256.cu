@@ -120,7 +120,10 @@ struct Sha {
 // thread's chain is issue-bound on the integer pipe, so the work is split: warp 1 loads each 64-byte
 // block (or builds the padded last blocks) and expands its schedule into W[t] + K[t] in shared memory;
 // warp 0 runs only the 64 rounds from there. Two slots alternate, with one CTA barrier per block;
-// messages shorter than the CTA's longest keep their final state through the extra blocks.
+// messages shorter than the CTA's longest keep their final state through the extra blocks. A slot
+// holds the rounds of a lane four at a time ([group of 4 rounds][lane], 16 bytes), so the round warp
+// reads them with one 16-byte load per four rounds, issued a group ahead: its chain never waits on
+// shared memory.
 constexpr int kShaLanes = 32;
 __device__ __forceinline__ uint32_t msg_blocks(uint64_t bytes) { return (uint32_t)((bytes + 9 + 63) / 64); }
 
@@ -153,7 +156,7 @@ __device__ __forceinline__ void produce_block(const uint8_t *data, uint64_t byte
 }
 
 __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *__restrict__ msgs, uint32_t n) {
-    __shared__ uint32_t sched[2][64][kShaLanes];   // [slot][round][lane]: W[t] + K[t]
+    __shared__ uint4 sched[2][16][kShaLanes];   // [slot][rounds 4g .. 4g+3][lane]: W[t] + K[t]
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t i = blockIdx.x * kShaLanes + lane;
     const bool active = i < n;
@@ -187,7 +190,8 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *_
                 }
                 if (b + 1 < mine) load(b + 1);
                 if (64ull * (b + 8) + 64 <= m.bytes) asm volatile("prefetch.global.L2 [%0];" :: "l"(m.data + 64ull * (b + 8)));
-                uint32_t (*out)[kShaLanes] = sched[b & 1];
+                uint4 (*out)[kShaLanes] = sched[b & 1];
+                uint32_t wk[4];
 #pragma unroll
                 for (int t = 0; t < 64; ++t) {
                     uint32_t wt;
@@ -199,7 +203,8 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *_
                              (ror(w2, 17) ^ ror(w2, 19) ^ (w2 >> 10));
                         w[t & 15] = wt;
                     }
-                    out[t][lane] = wt + kSha[t];
+                    wk[t & 3] = wt + kSha[t];
+                    if ((t & 3) == 3) out[t >> 2][lane] = make_uint4(wk[0], wk[1], wk[2], wk[3]);
                 }
             }
             __syncthreads();
@@ -211,17 +216,27 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *_
     for (uint32_t b = 0; b < blocks; ++b) {
         __syncthreads();
         if (b >= mine) continue;
-        const uint32_t (*in)[kShaLanes] = sched[b & 1];
+        const uint4 (*in)[kShaLanes] = sched[b & 1];
         uint32_t a = st[0], bb = st[1], c = st[2], d = st[3], e = st[4], f = st[5], g = st[6], h = st[7];
+        // W + K of rounds 4q .. 4q+3 (cur) and of the next group (ahead, loaded a group early)
+        uint4 cur = in[0][lane], ahead = in[1][lane];
         // hk = h + W[t] + K[t], formed a round early (the next round's h is this round's g), so that the
         // new e and a are one three-input add after the round's rotations and logic functions
-        uint32_t hk = h + in[0][lane];
+        uint32_t hk = h + cur.x;
 #pragma unroll
         for (int t = 0; t < 64; ++t) {
             const uint32_t s1 = ror(e, 6) ^ ror(e, 11) ^ ror(e, 25), ch = (e & f) ^ (~e & g);
             const uint32_t s0 = ror(a, 2) ^ ror(a, 13) ^ ror(a, 22), mj = (a & bb) ^ (a & c) ^ (bb & c);
             const uint32_t dhk = d + hk, t1 = hk + s1 + ch;
-            const uint32_t next_hk = t < 63 ? g + in[t + 1][lane] : 0u;
+            uint32_t next_hk = 0;
+            if (t < 63) {
+                const int u = (t + 1) & 3;
+                if (u == 0) {   // round t + 1 opens the next group: shift, and load the one after it
+                    cur = ahead;
+                    if ((t + 1) / 4 + 1 < 16) ahead = in[(t + 1) / 4 + 1][lane];
+                }
+                next_hk = g + (u == 0 ? cur.x : u == 1 ? cur.y : u == 2 ? cur.z : cur.w);
+            }
             h = g; g = f; f = e; e = dhk + s1 + ch; d = c; c = bb; bb = a; a = t1 + (s0 + mj);
             hk = next_hk;
         }
