@@ -55,10 +55,11 @@ int wexb_resident_wait(WexbResident *r, int *status);
 /* 1: bracket each kernel of the following decodes with CUDA events on its stream; 0: stop. Returns 0
  * (a decode returns 1 when its events cannot be created). */
 int wexb_resident_profile(WexbResident *r, int on);
-/* Milliseconds of the scale, weight and commit kernels of the last waited decode (profiling on):
- * 0, or -1 when there is nothing to report. */
+/* Milliseconds of the last waited decode (profiling on), on its stream: ms3[0] the upload of its launch
+ * metadata, ms3[1] the decode launch (scale, weight and commit work of every record), ms3[2] the
+ * read-back of the error words. 0, or -1 when there is nothing to report. */
 int wexb_resident_kernel_ms(const WexbResident *r, float *ms3);
-/* Kernel launches of the last queued decode (3: scales, weights, commit). */
+/* Kernel launches of the last queued decode: one persistent launch per model among its records. */
 int wexb_resident_launches(const WexbResident *r);
 void wexb_resident_destroy(WexbResident *r);
 

@@ -280,7 +280,7 @@ def test_resident_decode(torch_cuda, tiny):
     ts, sp, wp = _dst(torch_cuda, ex[0].entry, len(order))
     assert res.decode(order, sp, wp) == 0
     bad, st = res.wait()
-    assert bad == 0 and st == [0] * 4 and res.launches() == 3
+    assert bad == 0 and st == [0] * 4 and res.launches() == 1   # one persistent launch (one model)
     for j, x in enumerate(order):
         assert _slab(ts, j) == ex[x].expected
     res.close()
@@ -306,7 +306,7 @@ def test_resident_two_decodes_queued(torch_cuda, tiny):
     assert queue(a, sa, wa) == 0 and queue(b, sb, wb) == 0
     assert L.wexb_resident_wait(res.handle, status) == 0 and list(status)[:2] == [0, 0]   # a
     ms = (ctypes.c_float * 3)()
-    assert L.wexb_resident_kernel_ms(res.handle, ms) == 0 and all(v > 0 for v in ms)
+    assert L.wexb_resident_kernel_ms(res.handle, ms) == 0 and ms[1] > 0 and all(v >= 0 for v in ms)
     assert queue(c, sc, wc) == 0                       # b and c queued
     assert queue(a, sa, wa) == 0                       # b waited for and dropped; c and a queued
     assert L.wexb_resident_wait(res.handle, status) == 0 and list(status)[:1] == [0]        # c

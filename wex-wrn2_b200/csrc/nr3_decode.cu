@@ -73,17 +73,6 @@ __device__ __forceinline__ uint32_t coded_neg_zero(const uint32_t w[4]) {
     }
     return ~nonzero & 0x88888888u;
 }
-// The ceil-form inverse of the eight nibbles of w (c/wex_neural_rans.h:446-461): magnitude a becomes
-// a + min(a, 2), i.e. 0 1 2 3 4 5 -> 0 2 4 5 6 7, read from a nibble table; signs are kept. A block
-// whose coded maximum is 5 holds magnitudes 0..5 only.
-__device__ __forceinline__ uint32_t ceil_inverse_word(uint32_t w) {
-    constexpr uint32_t kDoubled = 0x00765420u;   // nibble a: the magnitude a stands for
-    uint32_t out = w & 0x88888888u;
-#pragma unroll
-    for (int k = 0; k < 32; k += 4) out |= ((kDoubled >> (4u * ((w >> k) & 7u))) & 7u) << k;
-    return out;
-}
-
 // ---- scale streams ----------------------------------------------------------------------------
 // tables, lane_slots: shared addresses of the staged table block and of the lane's payload slot 0.
 __device__ __noinline__ uint32_t scale_stream(const Nr3Record &R, uint32_t m, uint32_t j, uint32_t tables,

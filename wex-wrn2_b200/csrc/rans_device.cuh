@@ -165,6 +165,17 @@ struct PayloadWindow {
     __device__ __forceinline__ void close() const { cp_async_wait<0>(); }
 };
 
+// The ceil-form inverse of the eight nibbles of w (c/wex_neural_rans.h:446-461, the same rule in WNR4
+// kind MX): magnitude a becomes a + min(a, 2), i.e. 0 1 2 3 4 5 -> 0 2 4 5 6 7, read from a nibble
+// table; signs are kept. A block whose coded maximum is 5 holds magnitudes 0..5 only.
+__device__ __forceinline__ uint32_t ceil_inverse_word(uint32_t w) {
+    constexpr uint32_t kDoubled = 0x00765420u;   // nibble a: the magnitude a stands for
+    uint32_t out = w & 0x88888888u;
+#pragma unroll
+    for (int k = 0; k < 32; k += 4) out |= ((kDoubled >> (4u * ((w >> k) & 7u))) & 7u) << k;
+    return out;
+}
+
 // Bits (0, 8 or 16) a state in [2^9, 2^31) shifts in until it is at least 2^23.
 __device__ __forceinline__ uint32_t renorm_bits(uint32_t x) { return ((uint32_t)__clz(x) - 1u) & 24u; }
 

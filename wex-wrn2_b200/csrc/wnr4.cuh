@@ -12,6 +12,7 @@ namespace wexb {
 constexpr uint32_t kW4L = 0x10000u;
 constexpr uint32_t kW4Classes = 7;           // MX: scale class = clamp(scale - anchor, -3, 3) + 3
 constexpr uint32_t kW4Err = 1, kW4ErrHash = 2, kW4ErrCeil = 4, kW4ErrCz = 8;
+constexpr uint32_t kW4ErrTimeout = 16;   // a bounded wait gave up (the host reports status 1)
 
 // Per model and device, per matrix: the weight rows of the reachable contexts, then the scale block.
 // A weight context (cls * 9 + pm) * 9 + mx (wnr4/wnr4.h, kind MX) only takes pm <= mx < 8 or the block

@@ -2,31 +2,29 @@
 // wnr4_decode_tile (wnr4/wnr4.h:388-478).
 //
 // One warp = one tile: its 32 lanes step in lockstep; at each step the lanes whose state fell below
-// L = 2^16 take the next words of the tile's shared u16 stream in lane order (ballot, then each lane's
-// rank = popc of the votes below it). The words come from a 64-word register window (lane l holds
-// words base + l and base + 32 + l) by shuffle; when the read position passes base + 32 the window
-// slides with one coalesced 64-byte load, consumed steps later. A CTA holds kW4Warps tiles of one
-// matrix, with that matrix's weight rows and scale CDF staged into shared memory by one TMA bulk copy.
-// A weight symbol takes two 8-byte shared loads: the row's level-1 entry gives the quartile q from
-// three packed 16-bit comparisons, the quartile's four cumulative frequencies give the rank r in it,
-// and start and end are adjacent fields taken by one funnel shift (tables in wnr4.cuh).
+// L = 2^16 take the next words of the tile's shared u16 stream in lane order (the format's rule: a
+// lane's word is the one at the stream position plus the number of needing lanes below it). The
+// stream reaches the warp through shared memory: TMA bulk copies move it in 1 KB chunks (16-byte
+// aligned spans of the record, the first one starting at or below the tile's first word) into a
+// two-chunk ring per warp, each chunk completing on its own mbarrier; the next chunk is requested as
+// soon as the warp has left the one before it, and each lane reads its word with one 2-byte shared
+// load. A CTA holds kW4Warps tiles of one matrix, with that matrix's weight rows and scale CDF staged
+// into shared memory by one TMA bulk copy. A weight symbol takes two 8-byte shared loads: the row's
+// level-1 entry gives the quartile q from three packed 16-bit comparisons, the quartile's four
+// cumulative frequencies give the rank r in it, and start and end are adjacent fields taken by one
+// funnel shift (tables in wnr4.cuh).
 #include "wnr4.cuh"
+#include "rans_device.cuh"
 
 namespace wexb {
 namespace {
 
-constexpr uint32_t kSpinLimit = 1u << 24;
-constexpr uint32_t kFull = 0xffffffffu;
+using namespace rans;
 
-__device__ __forceinline__ uint32_t rotl32(uint32_t x, int r) { return __funnelshift_l(x, x, r); }
-__device__ __forceinline__ uint32_t mm3_block(uint32_t h, uint32_t k) {
-    k *= 0xcc9e2d51u; k = rotl32(k, 15); k *= 0x1b873593u;
-    return rotl32(h ^ k, 13) * 5u + 0xe6546b64u;
-}
-__device__ __forceinline__ uint32_t mm3_final(uint32_t h, uint32_t len) {
-    h ^= len; h ^= h >> 16; h *= 0x85ebca6bu; h ^= h >> 13; h *= 0xc2b2ae35u; h ^= h >> 16;
-    return h;
-}
+constexpr uint32_t kFull = 0xffffffffu;
+constexpr uint32_t kChunkBytes = 1024, kChunkWords = kChunkBytes / 2;
+constexpr uint32_t kRingBytesPerWarp = 2 * kChunkBytes;
+
 // Number of the 16 entries of a cumulative row (a, b: 8 packed u16 pairs, all < 2^15) that are <= slot.
 __device__ __forceinline__ uint32_t row_count(const uint4 a, const uint4 b, uint32_t slot) {
     const uint32_t g = slot * 0x10001u | 0x80008000u;
@@ -35,62 +33,100 @@ __device__ __forceinline__ uint32_t row_count(const uint4 a, const uint4 b, uint
     const uint32_t m = 0x80808080u;
     return (uint32_t)__popc((p0 & m) | ((p1 & m) >> 1) | ((p2 & m) >> 2) | ((p3 & m) >> 3));
 }
-__device__ __forceinline__ uint32_t ceil_double(uint32_t w) {   // magnitudes a -> a + min(a, 2), signs kept
-    const uint32_t mag = w & 0x77777777u, two_or_more = ((mag >> 1) | (mag >> 2)) & 0x11111111u;
-    return (w & 0x88888888u) | (mag + ((two_or_more << 1) | (mag & 0x11111111u & ~two_or_more)));
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(a));
+    return v;
 }
 
-struct Window {
-    const uint16_t *words;
-    uint32_t nwords, base, lo, hi;
-    __device__ __forceinline__ uint32_t load(uint32_t i) const { return i < nwords ? (uint32_t)__ldg(words + i) : 0u; }
+// A warp's tile word stream (see the file comment). Word k of the stream is byte 2 (k + shift) of the
+// aligned span that starts at `from`; chunk c is that span's bytes [1024 c, 1024 (c + 1)), held in ring
+// half c % 2 and completed on barrier c % 2 in phase (c / 2) % 2.
+struct TileStream {
+    uint32_t ring, bars;        // shared addresses: this warp's 2 KB ring and its two mbarriers
+    const uint8_t *from;        // 16-byte aligned, at or below the first word
+    uint32_t shift;             // words from `from` to the first word (0..7)
+    uint32_t span;              // bytes from `from` to the end of the last word
+    uint32_t nwords, ptr;       // words in the tile; the next unread one
+    uint32_t ready, issued;     // chunks landed; chunks requested
+
+    // The next chunk, by lane 0 (called by the whole warp); bytes a multiple of 16. The warp barrier and
+    // the proxy fence order every lane's earlier reads of that ring half before the copy's writes.
+    __device__ __forceinline__ void request() {
+        const uint32_t c = issued++;
+        __syncwarp();
+        if ((threadIdx.x & 31u) == 0) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            const uint32_t at = c * kChunkBytes, bytes = min(kChunkBytes, (span - at + 15u) & ~15u);
+            const uint32_t bar = bars + 8u * (c & 1u);
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" :: "r"(bar), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                         :: "r"(ring + kChunkBytes * (c & 1u)), "l"(from + at), "r"(bytes), "r"(bar) : "memory");
+        }
+    }
+    __device__ __forceinline__ bool more() const { return issued * kChunkBytes < span; }
+    // Waits (bounded) for the oldest requested chunk that has not landed; false when the wait gave up.
+    __device__ __forceinline__ bool land() {
+        const uint32_t c = ready;
+        unsigned done = 0;
+        for (uint32_t i = 0; i < kWaitPolls && !done; ++i)
+            asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                         : "=r"(done) : "r"(bars + 8u * (c & 1u)), "r"((c >> 1) & 1u) : "memory");
+        if (done) ++ready;
+        return done != 0;
+    }
+    // Before the warp leaves: every requested chunk has landed, so no copy can reach shared memory
+    // that another CTA may own later (bounded like every wait).
+    __device__ __forceinline__ void drain() { while (ready < issued && land()) {} }
+    __device__ __forceinline__ uint32_t word(uint32_t k) const {
+        return lds_u16(ring + 2u * ((k + shift) % (2u * kChunkWords)));
+    }
+    // Opens the stream (the warp's barriers initialised by the caller) and requests its first two chunks.
+    __device__ __forceinline__ bool open(const uint8_t *words, uint32_t n, uint32_t ring_addr, uint32_t bar_addr) {
+        ring = ring_addr; bars = bar_addr; nwords = n; ptr = 0; ready = 0; issued = 0;
+        from = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(words) & ~(uintptr_t)15);
+        shift = (uint32_t)(words - from) / 2u;
+        span = 2u * (shift + n);
+        if (!span) return true;
+        request();
+        if (more()) request();
+        return land();
+    }
 };
 
-// The lanes with `need` take their words; false when the tile has too few words (warp-uniform).
-__device__ __forceinline__ bool renorm(uint32_t &x, bool need, uint32_t &ptr, Window &w, uint32_t lane) {
+// The lanes with `need` take the next words of the stream, in lane order. 0, or kW4Err when the tile has
+// too few words, or kW4ErrTimeout when a chunk did not land in time (both warp-uniform).
+__device__ __forceinline__ uint32_t take_words(uint32_t &x, bool need, TileStream &s, uint32_t lane) {
     const uint32_t vote = __ballot_sync(kFull, need);
-    if (!vote) return true;
+    if (!vote) return 0;
     const uint32_t total = __popc(vote);
-    if (ptr + total > w.nwords) return false;
-    const uint32_t idx = ptr - w.base + __popc(vote & ((1u << lane) - 1u));   // < 64
-    const uint32_t v0 = __shfl_sync(kFull, w.lo, idx & 31u), v1 = __shfl_sync(kFull, w.hi, idx & 31u);
-    if (need) x = x << 16 | (idx < 32u ? v0 : v1);
-    ptr += total;
-    if (ptr - w.base >= 32u) { w.lo = w.hi; w.base += 32u; w.hi = w.load(w.base + 32u + lane); }
-    return true;
-}
-
-__device__ __forceinline__ bool stage(uint64_t *bar, void *dst, const void *src, uint32_t bytes) {
-    const unsigned b = (unsigned)__cvta_generic_to_shared(bar);
-    if (threadIdx.x == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" :: "r"(b) : "memory");
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" :: "r"(b), "r"(bytes) : "memory");
-        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
-                     :: "r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src), "r"(bytes), "r"(b) : "memory");
-    }
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        uint32_t done;
-        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}\n"
-                     : "=r"(done) : "r"(b) : "memory");
-        if (done) return true;
-    }
-    return false;
+    if (s.ptr + total > s.nwords) return kW4Err;
+    if (s.shift + s.ptr + total > kChunkWords * s.ready && !s.land()) return kW4ErrTimeout;
+    if (need) x = x << 16 | s.word(s.ptr + __popc(vote & ((1u << lane) - 1u)));
+    s.ptr += total;
+    // the chunk before the current one is used up: its half of the ring takes the one after the next
+    if (s.more() && s.shift + s.ptr >= kChunkWords * (s.issued - 1u)) s.request();
+    return 0;
 }
 
 __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const W4Job *__restrict__ jobs,
                                                             const W4Rec *__restrict__ recs) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar;
+    __shared__ uint64_t stream_bars[kW4Warps][2];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t m = jobs[blockIdx.x * kW4Warps].m;   // every tile of the CTA is of this matrix
     const W4Job J = jobs[blockIdx.x * kW4Warps + warp];
-    if (!stage(&bar, smem, tab.base + (size_t)m * tab.matrix_bytes, tab.matrix_bytes)) {
-        if (J.n && lane == 0) atomicOr(recs[J.rec].error, kW4Err);
-        return;
+    if (threadIdx.x < 2 * kW4Warps) mbar_init(&stream_bars[threadIdx.x >> 1][threadIdx.x & 1u], 1);
+    {
+        void *dst[1] = {smem};
+        const void *src[1] = {tab.base + (size_t)m * tab.matrix_bytes};
+        const uint32_t bytes[1] = {tab.matrix_bytes};
+        if (!stage_tables(&bar, dst, src, bytes, 1)) {   // the table copy may still be in flight: read nothing
+            if (J.n && lane == 0) atomicOr(recs[J.rec].error, kW4ErrTimeout);
+            return;
+        }
     }
     if (!J.n) return;
     const W4Rec &R = recs[J.rec];
@@ -102,9 +138,14 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
     const uint16_t *tile16 = reinterpret_cast<const uint16_t *>(J.tile);   // 2-byte aligned only
     uint32_t x = (uint32_t)tile16[2 * lane] | (uint32_t)tile16[2 * lane + 1] << 16;
     if (__any_sync(kFull, x < kW4L)) { if (lane == 0) atomicOr(R.error, kW4Err); return; }
-    Window win{tile16 + 64, J.nwords, 0, 0, 0};
-    win.lo = win.load(lane); win.hi = win.load(32u + lane);
-    uint32_t ptr = 0, err = 0;
+    TileStream ts;
+    const uint32_t ring = smem_addr(smem + tab.matrix_bytes) + warp * kRingBytesPerWarp;
+    if (!ts.open(J.tile + 128, J.nwords, ring, smem_addr(&stream_bars[warp][0]))) {
+        ts.drain();
+        if (lane == 0) atomicOr(R.error, kW4ErrTimeout);
+        return;
+    }
+    uint32_t err = 0;
     // lane hash start: ident words {model, owner, tile, lane, kind | flags << 8 | G << 16, anchors}
     uint32_t hash = 0x34524e57u;
     hash = mm3_block(hash, R.model_id); hash = mm3_block(hash, R.owner); hash = mm3_block(hash, J.t);
@@ -126,7 +167,11 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
             so[c0 + i] = (uint8_t)y;
             hash = mm3_block(hash, y);
         }
-        if (!renorm(x, act && x < kW4L, ptr, win, lane)) { if (lane == 0) atomicOr(R.error, kW4Err); return; }
+        if (const uint32_t e = take_words(x, act && x < kW4L, ts, lane)) {
+            ts.drain();
+            if (lane == 0) atomicOr(R.error, e);
+            return;
+        }
     }
     // phase 2: rounds of 32 cells, lane l owning cell c0 + 32j + l, its 32 nibbles in order
     const bool ceil = (R.flags >> m) & 1u, cz = (R.flags & 8u) != 0;
@@ -172,13 +217,17 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
                     pair = ((top * top + top) >> 1) + mag;
                 }
                 // out of words: the structure bit alone, as the reference reports it (earlier bits dropped)
-                if (!renorm(x, act && x < kW4L, ptr, win, lane)) { if (lane == 0) atomicOr(R.error, kW4Err); return; }
+                if (const uint32_t e = take_words(x, act && x < kW4L, ts, lane)) {
+                    ts.drain();
+                    if (lane == 0) atomicOr(R.error, e);
+                    return;
+                }
             }
             w0 = w1; w1 = w2; w2 = w3; w3 = word;
         }
         uint32_t w[4] = {w0, w1, w2, w3};
         const uint32_t left = x - kW4L;
-        if (__any_sync(kFull, tail && (x < kW4L || left > 0xffffu))) { atomicOr(R.error, kW4Err | err); return; }
+        if (__any_sync(kFull, tail && (x < kW4L || left > 0xffffu))) { ts.drain(); atomicOr(R.error, kW4Err | err); return; }
         if (active) {
             if (tail) {
                 for (uint32_t q = 0; q < 4; ++q) {
@@ -194,7 +243,7 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
                 if (!scale) err |= kW4ErrCeil;
                 else {
                     so[cell] = (uint8_t)(scale - 1u);
-                    for (int q = 0; q < 4; ++q) w[q] = ceil_double(w[q]);
+                    for (int q = 0; q < 4; ++q) w[q] = ceil_inverse_word(w[q]);
                 }
             }
             wo[cell] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -205,7 +254,8 @@ __global__ void __launch_bounds__(kW4Warps * 32) wnr4_tiles(W4Tables tab, const 
     uint32_t H = mm3_final(hash, 24u + 20u * mine);
 #pragma unroll
     for (int s = 16; s; s >>= 1) H ^= __shfl_xor_sync(kFull, H, s);
-    if (ptr != J.nwords) err |= kW4Err;
+    ts.drain();
+    if (ts.ptr != J.nwords) err |= kW4Err;
     if (lane == 0 && x != kW4L + (H & 0xffffu)) err |= kW4ErrHash;
     if (lane == 1 && x != kW4L + (H >> 16)) err |= kW4ErrHash;
     if (lane >= 2 && x != kW4L) err |= kW4Err;
@@ -222,11 +272,11 @@ cudaError_t launch_wnr4(const W4Tables &tab, const W4Job *jobs, uint32_t njobs, 
     if (cudaGetDevice(&dev) != cudaSuccess) return cudaGetLastError();
     if (dev != configured_device) {
         const cudaError_t e = cudaFuncSetAttribute(wnr4_tiles, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)w4_matrix_bytes(w4_rows(5)));
+                                                   (int)(w4_matrix_bytes(w4_rows(5)) + kW4Warps * kRingBytesPerWarp));
         if (e != cudaSuccess) return e;
         configured_device = dev;
     }
-    wnr4_tiles<<<njobs / kW4Warps, kW4Warps * 32, tab.matrix_bytes, st>>>(tab, jobs, recs);
+    wnr4_tiles<<<njobs / kW4Warps, kW4Warps * 32, tab.matrix_bytes + kW4Warps * kRingBytesPerWarp, st>>>(tab, jobs, recs);
     return cudaGetLastError();
 }
 

@@ -200,7 +200,7 @@ class Resident:
         return lib().wexb_resident_profile(self.handle, 1 if on else 0)
 
     def kernel_ms(self):
-        """(scales, weights, commit) milliseconds of the last waited decode, or None."""
+        """(metadata upload, decode launch, status read-back) milliseconds of the last waited decode, or None."""
         ms = (ctypes.c_float * 3)()
         return tuple(ms) if lib().wexb_resident_kernel_ms(self.handle, ms) == 0 else None
 
