@@ -111,16 +111,58 @@ def routing_trace(cfg, steps, rank, world, layers):
     return [[trace[l][s] for l in range(layers)] for s in range(steps)]
 
 
-def build_pool(cfg, owners, threads):
-    """WNM2 model (trained on one fixed expert per layer, the same on every rank) and the records."""
+def build_pool(cfg, owners, threads, device=None):
+    """WNM2 model (trained on one fixed expert per layer, the same on every rank) and the records. With a
+    device and a lean config, the records are encoded by this library's GPU writer (wexb_encode_batch,
+    byte-identical to the CPU encoder): the host threads only make the coded slabs."""
     import synth
     sig = layer_sigmas(cfg)
     train = [(l, l % cfg['experts']) for l in range(cfg['layers'])]
     blob, _ = synth.make_experts(cfg['hidden'], cfg['ffn'], train, seed=SEED, sigma=lambda l: sig[l], cz=cfg['cz'],
                                  neg_zero=cfg['neg_zero'], train_every=1, threads=threads)
+    if device is not None and cfg.get('lean'):
+        return blob, gpu_encoded_pool(cfg, owners, threads, blob, device)
     _, experts = synth.make_experts(cfg['hidden'], cfg['ffn'], owners, seed=SEED, sigma=lambda l: sig[l], cz=cfg['cz'],
                                     neg_zero=cfg['neg_zero'], threads=threads, blob=blob, lean=cfg.get('lean', False))
     return blob, experts
+
+
+def gpu_encoded_pool(cfg, owners, threads, blob, device):
+    """Lean experts (entry, record, .raw, .expected_sha) of the owners: host threads make each group's coded
+    slabs (the same seeds as synth.make_experts) while the GPU encodes the previous group."""
+    import synth
+    import wexcuda
+    sig = layer_sigmas(cfg)
+    group = max(8, 2 * threads)
+
+    def make(o):
+        layer, idx = o
+        e = synth.Expert(cfg['hidden'], cfg['ffn'], layer, idx, SEED * 1000003 + layer * 4099 + idx, sig[layer],
+                         cfg['cz'], 0, cfg['neg_zero'])
+        e.raw = len(e.source)
+        e.expected_sha = hashlib.sha256(e.expected).digest()
+        return e
+    out = []
+    with ThreadPoolExecutor(threads) as pool, ThreadPoolExecutor(1) as ahead:
+        pending = ahead.submit(lambda g: list(pool.map(make, g)), owners[:group])
+        for at in range(0, len(owners), group):
+            ex = pending.result()
+            if at + group < len(owners):
+                pending = ahead.submit(lambda g: list(pool.map(make, g)), owners[at + group:at + 2 * group])
+            res = wexcuda.encode_batch(blob, [e.entry for e in ex], [e.coded for e in ex], [e.flags for e in ex],
+                                       [e.owner for e in ex], True, 2048, 512, device)
+            for e, (st, rec, _, _) in zip(ex, res):
+                assert st in (0, 1), f'GPU encoder status {st}'
+                if st == 0:
+                    e.record, e.codec = rec, synth.CODEC_WNR3
+                else:   # not smaller than raw: stored RAW with the source bytes (c/tools/wex_nr3_tools.c:85-103)
+                    e.record = e.source + bytes(((e.raw + 4095) & ~4095) - e.raw)
+                    e.codec = synth.CODEC_RAW
+                    e.expected_sha = hashlib.sha256(e.source).digest()
+                e.entry = synth.entry_with(e.entry, total=len(e.record), codec=e.codec)
+                e.source = e.coded = e.expected = None
+            out.extend(ex)
+    return out
 
 
 def pinned_records(experts):
@@ -1352,7 +1394,7 @@ def run_gpu(args, cfg):
     else:
         threads = max(1, (os.cpu_count() or 8) // local_world)
     t0 = time.time()
-    blob, experts = build_pool(cfg, owners, threads)
+    blob, experts = build_pool(cfg, owners, threads, device=dev)
     log(f'[rank {rank}] {len(experts)} experts generated and encoded in {time.time() - t0:.1f} s')
     assert all(e.codec == 5 for e in experts), 'every synthetic expert compresses'
     index = {(e.layer, e.index): i for i, e in enumerate(experts)}
