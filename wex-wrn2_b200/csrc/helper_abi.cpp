@@ -34,8 +34,9 @@ namespace {
 // Byte layout of a call's metadata block (host pinned, copied to the device in one piece): record
 // descriptors, the work queue, its counters, commit jobs, error words, stream offsets.
 struct MetaLayout {
-    size_t recs = 0, items = 0, counters = 0, jobs = 0, errs = 0, offs = 0, total = 0;
-    void compute(size_t k, size_t nitems, size_t ncounters, size_t njobs, size_t noffs) {
+    size_t recs = 0, items = 0, counters = 0, jobs = 0, errs = 0, offs = 0, landed = 0, total = 0;
+    // nlanded: the records' upload flags, then one word holding 1 (the source of every flag's copy)
+    void compute(size_t k, size_t nitems, size_t ncounters, size_t njobs, size_t noffs, size_t nlanded = 0) {
         size_t at = 0;
         recs = at; at = align_up(at + k * sizeof(Nr3Record), 256);
         items = at; at = align_up(at + nitems * sizeof(Nr3Item), 256);
@@ -43,6 +44,7 @@ struct MetaLayout {
         jobs = at; at = align_up(at + njobs * sizeof(CommitJob), 256);
         errs = at; at = align_up(at + k * 4, 256);
         offs = at; at = align_up(at + noffs * 4, 256);
+        landed = at; at = align_up(at + (nlanded ? nlanded + 1 : 0) * 4, 256);
         total = at;
     }
 };
@@ -124,7 +126,7 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     LaunchSet launches;
     launches.plan(plans.data(), tabs.data(), (uint32_t)k, commit);
     MetaLayout &L = c.L;
-    L.compute(k, launches.items, launches.counter_words(), commit ? k : 0, noffs);
+    L.compute(k, launches.items, launches.counter_words(), commit ? k : 0, noffs, k);
     if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total)) {
         c.settle(1); workspace_give(w, true); c.w = nullptr; return false;
     }
@@ -136,7 +138,13 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + L.recs);
     const CommitJob *djobs = reinterpret_cast<const CommitJob *>(dm + L.jobs);
     uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + L.errs);
-    launches.fill(plans.data(), commit, sms, reinterpret_cast<Nr3Item *>(hm + L.items), reinterpret_cast<uint32_t *>(hm + L.counters));
+    // records are decoded as their uploads land (one record's scale items ahead of the weight items)
+    launches.fill(plans.data(), commit, sms, 1, reinterpret_cast<Nr3Item *>(hm + L.items),
+                  reinterpret_cast<uint32_t *>(hm + L.counters));
+    uint32_t *hlanded = reinterpret_cast<uint32_t *>(hm + L.landed);
+    uint32_t *dlanded = reinterpret_cast<uint32_t *>(dm + L.landed);
+    std::memset(hlanded, 0, 4 * k);
+    hlanded[k] = 1;
     for (size_t j = 0; j < k; ++j) {
         const int i = c.pend[j];
         const Plan &p = c.plans[(size_t)i];
@@ -144,6 +152,7 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
         plan_offsets(p, hoffs + off_off[j]);
         plan_descriptor(p, w->drec.p + rec_off[j], reinterpret_cast<const uint32_t *>(dm + L.offs) + off_off[j], scr,
                         derrs + j, commit ? djobs + j : nullptr, &hrecs[j]);
+        hrecs[j].landed = dlanded + j;
         herrs[j] = 0;
         if (commit) {
             CommitJob &J = hjobs[j];
@@ -153,23 +162,33 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
             }
         }
     }
-    // enqueue: metadata and records on the upload stream; then, on the call's kernel stream, one
-    // persistent launch per model over every record of the call, and the read-back of the error words
+    // enqueue. Upload stream: the metadata, then each record followed by the copy of a 1 into its
+    // `landed` word. Kernel stream: once the metadata is there, one persistent launch per model, whose
+    // items wait for each record's flag, so the records decode as they land; then, after every upload,
+    // the read-back of the error words (`done`, recorded last, covers the whole call)
     cudaStream_t up = nullptr, st = nullptr;
     if (!device_streams(device, &up, &st)) { c.settle(1); workspace_give(w, true); c.w = nullptr; return false; }
-    bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, up) == cudaSuccess;
-    for (size_t j = 0; ok && j < k; ++j)
+    bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, up) == cudaSuccess &&
+              cudaEventRecord(w->meta_done, up) == cudaSuccess;
+    for (size_t j = 0; ok && j < k; ++j)   // the flag's copy comes from the page-locked block: a copy engine sets it
         ok = cudaMemcpyAsync(w->drec.p + rec_off[j], records[c.pend[j]], c.plans[(size_t)c.pend[j]].total,
-                             cudaMemcpyHostToDevice, up) == cudaSuccess;
-    // the kernel stream waits for every upload, so `done`, recorded on it last, covers the whole call
-    if (cudaEventRecord(w->uploads_done, up) != cudaSuccess || cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess) {
+                             cudaMemcpyHostToDevice, up) == cudaSuccess &&
+             cudaMemcpyAsync(dlanded + j, hlanded + k, 4, cudaMemcpyHostToDevice, up) == cudaSuccess;
+    const bool queued_meta = ok;
+    if (cudaEventRecord(w->uploads_done, up) != cudaSuccess) {
         (void)cudaGetLastError();
         if (wait_stream(up) == Waited::TimedOut) c.unsettled = true;
         ok = false;
     }
     if (ok)
-        ok = launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + L.items), reinterpret_cast<uint32_t *>(dm + L.counters),
+        ok = cudaStreamWaitEvent(st, w->meta_done, 0) == cudaSuccess &&
+             launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + L.items), reinterpret_cast<uint32_t *>(dm + L.counters),
                              sms, st);
+    if (queued_meta && cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess) {
+        (void)cudaGetLastError();
+        if (wait_stream(up) == Waited::TimedOut) c.unsettled = true;
+        ok = false;
+    }
     for (size_t j = 0; ok && mode == Dest::Host && j < k; ++j) {
         const int i = c.pend[j];
         const Plan &p = c.plans[(size_t)i];
@@ -557,7 +576,7 @@ WEXB_API int wexb_resident_decode(WexbResident *r, int k, const int *index, unsi
     uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + q.L.errs);
     uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + q.L.errs);
     const CommitJob *djobs = reinterpret_cast<const CommitJob *>(dm + q.L.jobs);
-    launches.fill(plans.data(), true, sms, reinterpret_cast<Nr3Item *>(hm + q.L.items),
+    launches.fill(plans.data(), true, sms, kScalesFirst, reinterpret_cast<Nr3Item *>(hm + q.L.items),
                   reinterpret_cast<uint32_t *>(hm + q.L.counters));
     for (int j = 0; j < k; ++j) {
         const int cj = order[(size_t)j];   // the caller's index of the record at launch position j

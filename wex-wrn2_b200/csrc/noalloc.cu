@@ -141,7 +141,7 @@ WEXB_API int wexb_decode_to_device_noalloc(const WexEntry *entry, const unsigned
     LaunchSet launch;
     launch.plan(plans, &tab, 1, true);
     if (launch.items > kNaMaxItems) return -2;   // not reached within the stream and slab limits above
-    launch.fill(plans, true, sms, reinterpret_cast<Nr3Item *>(g_na_host + kNaItems),
+    launch.fill(plans, true, sms, kScalesFirst, reinterpret_cast<Nr3Item *>(g_na_host + kNaItems),
                 reinterpret_cast<uint32_t *>(g_na_host + kNaCounters));
     uint32_t *derr = reinterpret_cast<uint32_t *>(base + kNaErr);
     const CommitJob *djob = reinterpret_cast<const CommitJob *>(base + kNaJob);

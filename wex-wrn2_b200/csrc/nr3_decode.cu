@@ -236,6 +236,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) nr3_decode(const Nr3Launch 
         uint32_t *done = L.done + 4u * it.rec;
         uint32_t err = 0;
         if (kind == kItemScale) {
+            if (R.landed && !warp_wait_count(R.landed, 1u)) {   // the record's bytes never arrived
+                if (lane == 0) atomicOr(R.error, kErrTimeout);
+                item_done(done + sub);
+                continue;
+            }
             const uint32_t j = first + lane;
             if (j < (R.scount[sub] + R.schunk - 1u) / R.schunk) err = scale_stream(R, sub, j, tables, lane_slots);
             if (err) atomicOr(R.error, err);

@@ -252,24 +252,31 @@ uint32_t queue_items(const Plan &p, bool commit) {
     return n;
 }
 
-uint32_t queue_fill(const Plan *const *plans, uint32_t n, bool commit, int sms, Nr3Item *items) {
+uint32_t queue_fill(const Plan *const *plans, uint32_t n, bool commit, int sms, uint32_t scale_lead, Nr3Item *items) {
     uint32_t at = 0;
-    for (uint32_t r = 0; r < n; ++r)
+    auto scales = [&](uint32_t r) {
         for (uint32_t m = 0; m < 3; ++m)
             for (uint32_t i = 0, k = warp_items(plans[r]->scount[m], plans[r]->schunk); i < k; ++i)
                 items[at++] = {r, item_what(kItemScale, m, 32u * i)};
-    // commits trail the decode by about one wave of warps (every warp of the device busy with weight items)
-    const uint32_t per_record = n ? std::max(1u, weight_items(*plans[0])) : 1u;
-    const uint32_t delay = (uint32_t)std::max(1, sms) * (kDecodeThreads / 32u) / per_record + 1u;
+    };
+    auto weights = [&](uint32_t r) {
+        for (uint32_t m = 0; m < 3; ++m)
+            for (uint32_t i = 0, k = warp_items(plans[r]->wcount[m], plans[r]->wchunk); i < k; ++i)
+                items[at++] = {r, item_what(kItemWeight, m, 32u * i)};
+    };
     auto commits = [&](uint32_t r) {
         for (uint32_t region = 0; region < 6; ++region)
             for (uint32_t c = 0, k = (plans[r]->dst_bytes[region] + kCommitChunk - 1) / kCommitChunk; c < k; ++c)
                 items[at++] = {r, item_what(kItemCommit, region, c)};
     };
+    // commits trail the decode by about one wave of warps (every warp of the device busy with weight items)
+    const uint32_t per_record = n ? std::max(1u, weight_items(*plans[0])) : 1u;
+    const uint32_t delay = (uint32_t)std::max(1, sms) * (kDecodeThreads / 32u) / per_record + 1u;
+    const uint32_t lead = std::min(std::max(scale_lead, 1u), n);
+    for (uint32_t r = 0; r < lead; ++r) scales(r);
     for (uint32_t r = 0; r < n; ++r) {
-        for (uint32_t m = 0; m < 3; ++m)
-            for (uint32_t i = 0, k = warp_items(plans[r]->wcount[m], plans[r]->wchunk); i < k; ++i)
-                items[at++] = {r, item_what(kItemWeight, m, 32u * i)};
+        if (r + lead < n) scales(r + lead);
+        weights(r);
         if (commit && r >= delay) commits(r - delay);
     }
     if (commit)
@@ -291,8 +298,9 @@ void LaunchSet::plan(const Plan *const *plans, const uint8_t *const *tables, uin
     }
 }
 
-void LaunchSet::fill(const Plan *const *plans, bool commit, int sms, Nr3Item *items_out, uint32_t *counters) const {
-    for (const Group &g : groups) queue_fill(plans + g.first_rec, g.nrecs, commit, sms, items_out + g.first_item);
+void LaunchSet::fill(const Plan *const *plans, bool commit, int sms, uint32_t scale_lead, Nr3Item *items_out,
+                     uint32_t *counters) const {
+    for (const Group &g : groups) queue_fill(plans + g.first_rec, g.nrecs, commit, sms, scale_lead, items_out + g.first_item);
     std::memset(counters, 0, 4 * counter_words());
 }
 

@@ -62,10 +62,14 @@ void plan_descriptor(const Plan &p, const uint8_t *drec, const uint32_t *doff, u
 // Items a record adds to a queue: its scale and weight items, and its commit items when `commit`.
 uint32_t queue_items(const Plan &p, bool commit);
 // Writes the queue of one launch over records 0 .. n-1 (their plans, all of one model) into items and
-// returns how many: every scale item first, record by record; then each record's weight items, with
-// the commit items of an earlier record after them (`delay` records back, about one wave of the
-// device's warps), and the commits still missing at the end.
-uint32_t queue_fill(const Plan *const *plans, uint32_t n, bool commit, int sms, Nr3Item *items);
+// returns how many. Record by record: its weight items, preceded by the scale items of the record
+// `scale_lead` places later (the first scale_lead records' scale items open the queue; scale_lead >= n
+// puts every scale item first, the order for records already in device memory, while a small lead
+// suits records still being uploaded in order) and followed by the commit items of an earlier record
+// (`delay` records back, about one wave of the device's warps); the commits still missing at the end.
+uint32_t queue_fill(const Plan *const *plans, uint32_t n, bool commit, int sms, uint32_t scale_lead, Nr3Item *items);
+// scale_lead for records already in device memory: every scale item first.
+constexpr uint32_t kScalesFirst = 0xffffffffu;
 // SMs of a device (cached), or 0 when CUDA fails.
 int device_sms(int device);
 
@@ -78,8 +82,10 @@ struct LaunchSet {
     // Groups records [0, k) by their tables (already ordered so that equal tables are contiguous).
     void plan(const Plan *const *plans, const uint8_t *const *tables, uint32_t k, bool commit);
     size_t counter_words() const { return groups.size() + 4ull * records; }
-    // Writes every group's queue (`items` entries) and zeroes the counters (counter_words()).
-    void fill(const Plan *const *plans, bool commit, int sms, Nr3Item *items_out, uint32_t *counters) const;
+    // Writes every group's queue (`items` entries; scale_lead as for queue_fill) and zeroes the counters
+    // (counter_words()).
+    void fill(const Plan *const *plans, bool commit, int sms, uint32_t scale_lead, Nr3Item *items_out,
+              uint32_t *counters) const;
     // Launches every group on st over the device copies of the records, items and counters.
     bool launch(const Nr3Record *drecs, const Nr3Item *ditems, uint32_t *dcounters, int sms, cudaStream_t st) const;
 };

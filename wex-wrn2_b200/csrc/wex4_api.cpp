@@ -579,7 +579,8 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
             J.bytes[3 + mm] = j.plan.dst_bytes[3 + mm];
         }
     }
-    launches.fill(nr3_plans.data(), true, sms, reinterpret_cast<Nr3Item *>(hm + o_items), reinterpret_cast<uint32_t *>(hm + o_counters));
+    launches.fill(nr3_plans.data(), true, sms, kScalesFirst, reinterpret_cast<Nr3Item *>(hm + o_items),
+                  reinterpret_cast<uint32_t *>(hm + o_counters));
     for (W4Job &t : w4jobs)
         if (t.tile) t.tile = S.stage.p + reinterpret_cast<uintptr_t>(t.tile);
     for (size_t q = 0; q < k4; ++q) {

@@ -64,6 +64,7 @@ struct Nr3Record {
     uint8_t *out;              // decoded slab, decode layout: scales at soff[m], weights at wout[m]
     uint32_t *error;           // error bits of this record (zero when the launch starts)
     const CommitJob *job;      // the error-gated copy to the caller's buffers, or null (none)
+    const uint32_t *landed;    // non-zero once the record's upload has landed, or null (already there)
     uint32_t scount[3], wcount[3];   // scales / 4-bit weights of matrix m
     uint32_t soff[3], wout[3];       // their offsets in out (wout 16-byte aligned)
     uint32_t schunk, wchunk;         // symbols per stream
@@ -75,7 +76,8 @@ struct Nr3Record {
 };
 
 // The launch's work queue. A warp takes the next item (one atomic on the head counter) and runs it:
-//   scale item   32 scale streams [first, first + 32) of matrix `sub`
+//   scale item   32 scale streams [first, first + 32) of matrix `sub`; a record still being uploaded
+//                is waited for (bounded) first: the upload stream sets its `landed` word after its bytes
 //   weight item  32 weight streams of matrix `sub`; it first waits until every scale item of that
 //                matrix of its record is done (the streams' contexts read the decoded scales)
 //   commit item  chunk `first` (kCommitChunk bytes) of region `sub` of the record's commit; it first

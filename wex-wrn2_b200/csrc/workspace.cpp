@@ -27,7 +27,8 @@ std::vector<Workspace *> g_parked[kMaxDevices];   // gave up waiting: back to g_
 Workspace *fresh(int device) {
     auto *w = new (std::nothrow) Workspace();
     if (!w) return nullptr;
-    if (cudaEventCreateWithFlags(&w->uploads_done, cudaEventDisableTiming) != cudaSuccess ||
+    if (cudaEventCreateWithFlags(&w->meta_done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&w->uploads_done, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&w->done, cudaEventDisableTiming) != cudaSuccess) {
         (void)cudaGetLastError();   // an event made before the failure leaks, on CUDA failure only
         delete w;

@@ -19,7 +19,7 @@ bool device_streams(int device, cudaStream_t *up, cudaStream_t *st);
 // waited for.
 struct Workspace {
     int device = -1;
-    cudaEvent_t uploads_done = nullptr, done = nullptr;
+    cudaEvent_t meta_done = nullptr, uploads_done = nullptr, done = nullptr;
     DevBuf drec, dscratch, dmeta;
     PinBuf hmeta;
 };
