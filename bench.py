@@ -55,7 +55,7 @@ CONFIGS = {
                   lean=True, trace_steps=2),
     # whole-box streaming: 1536 large experts, each rank decodes all of its shard every step
     'box': dict(hidden=7168, ffn=2048, layers=8, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
-                lean=True, all_experts=True),
+                lean=True, all_experts=True, verify=True),
     # WNR4 kind MX (draft codec 8) through the ABI 5: large experts, G = 32, one batch call per layer
     'wnr4': dict(hidden=7168, ffn=2048, layers=2, experts=8, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
                  wnr4=True),
@@ -1356,7 +1356,7 @@ def gpu_reference_rate(args, blob, call_args, steps_total, check):
 
     def step(s):
         bad = 0
-        for ep, rp, sp, wp, st in call_args[s]:
+        for ep, rp, sp, wp, st, _ in call_args[s]:
             bad += R.wex_cuda_decode_batch_to_device(len(st), ep, rp, dev, sp, wp, st)
         return bad
     for s in range(args.warmup):
@@ -1469,32 +1469,42 @@ def run_gpu(args, cfg):
     L = wexcuda.lib()
     B = cfg['batch']
     entry_store = [np.frombuffer(bytes(e.entry), np.uint8).copy() for e in experts]
+    verify = bool(cfg.get('verify'))
+    depth = args.depth or (32 if verify else 3)
+    rec_sha = None
+    if verify:   # each record's SHA-256, as a WEX4 index keeps it (c/wex4.h:673-677), computed once on the host
+        with ThreadPoolExecutor(threads) as pool:
+            rec_sha = list(pool.map(lambda e: hashlib.sha256(e.record).digest(), experts))
     call_args = []
     for s in range(steps_total):
         ids = step_idx[s]
         per = []
         for c in range(0, k, B):   # one call per B records (a layer's batch)
             sel = ids[c:c + B]
+            dg = np.frombuffer(b''.join(rec_sha[i] for i in sel), np.uint8).copy() if verify else None
             per.append((wexcuda._ptrs([entry_store[i].ctypes.data for i in sel]),
                         wexcuda._ptrs([views[i].ctypes.data for i in sel]),
                         wexcuda._ptrs(dscale[3 * c:3 * (c + B)]), wexcuda._ptrs(dweight[3 * c:3 * (c + B)]),
-                        (ctypes.c_int * B)()))
+                        (ctypes.c_int * B)(), dg))
         call_args.append(per)
     ncalls = len(call_args[0])
 
     def sync_step(s):
         bad = 0
-        for ep, rp, sp, wp, st in call_args[s]:
+        for ep, rp, sp, wp, st, _ in call_args[s]:
             bad += L.wex_cuda_decode_batch_to_device(B, ep, rp, dev, sp, wp, st)
         return bad
 
     def queued_step(s, pending):
         bad = 0
-        for ep, rp, sp, wp, st in call_args[s]:
-            t = L.wexb_batch_submit(B, ep, rp, dev, sp, wp)
+        for ep, rp, sp, wp, st, dg in call_args[s]:
+            if verify:   # the record hashes on the GPU before the decode may write the destination
+                t = L.wexb_batch_submit_verified(B, ep, rp, dg.ctypes.data, dev, sp, wp)
+            else:
+                t = L.wexb_batch_submit(B, ep, rp, dev, sp, wp)
             assert t >= 0
             pending.append((t, st))
-            if len(pending) > args.depth:
+            if len(pending) > depth:
                 t0_, st0 = pending.pop(0)
                 bad += L.wexb_batch_wait(t0_, st0)
         return bad
@@ -1516,8 +1526,9 @@ def run_gpu(args, cfg):
         barrier(world)
         return dt
 
-    for s in range(args.warmup):
-        assert sync_step(s) == 0
+    if not verify:
+        for s in range(args.warmup):
+            assert sync_step(s) == 0
     pend = []
     for s in range(args.warmup):
         assert queued_step(s, pend) == 0
@@ -1536,8 +1547,10 @@ def run_gpu(args, cfg):
     # each end-to-end form is timed three times over the same K steps (the host link is shared with
     # other work on the machine); the median is reported, with every sample
     e2e_runs = [timed(run_queued) for _ in range(3)]
-    sync_runs = [timed(run_sync) for _ in range(3)]
-    e2e_s, sync_s = statistics.median(e2e_runs), statistics.median(sync_runs)
+    # a verified call waits for its records' SHA-256 chains: one at a time is a latency figure only
+    sync_runs = [timed(run_sync) for _ in range(3)] if not verify else None
+    e2e_s = statistics.median(e2e_runs)
+    sync_s = statistics.median(sync_runs) if sync_runs else None
     clk = clocks.stop()
     got = dst[check].cpu().numpy()
     assert all(hashlib.sha256(got[i].tobytes()).digest() == experts[last[j]].expected_sha for i, j in enumerate(check))
@@ -1551,7 +1564,7 @@ def run_gpu(args, cfg):
     dec_all, stored_all, recs_all = totals
     value = dec_all / (value_ms / 1e3) / 1e9
     e2e = dec_all / e2e_s / 1e9
-    e2e_sync = dec_all / sync_s / 1e9
+    e2e_sync = dec_all / sync_s / 1e9 if sync_s else None
     # roofline of the decode launch (the only kernel of a step: scale, weight and commit items), from
     # algorithmic bytes per launch = records read (stored bytes) + decode-layout slabs written + the
     # error-gated commit (slabs read, destinations written), over its event-timed duration
@@ -1593,14 +1606,19 @@ def run_gpu(args, cfg):
         'config': config_desc(args, cfg, k),
         'e2e': {'value': round(e2e, 3), 'unit': 'GB/s', 'experts_per_s': round(recs_all / e2e_s, 1),
                 'h2d_bytes_per_step': int(h2d_per_step), 'd2h_bytes_per_step': 4 * k,
-                'api': f'wexb_batch_submit/wexb_batch_wait, {B} records per call, {ncalls} calls per step, '
-                       f'{args.depth} calls in flight',
-                'ms_per_step': round(1e3 * e2e_s / args.steps, 3), 'gpu_launches': 3 * ncalls * args.steps,
+                'api': (f'wexb_batch_submit_verified/wexb_batch_wait (every record SHA-256 checked on the GPU '
+                        f'against its digest before its decode may write)' if verify else
+                        'wexb_batch_submit/wexb_batch_wait') +
+                       f', {B} records per call, {ncalls} calls per step, {depth} calls in flight',
+                'ms_per_step': round(1e3 * e2e_s / args.steps, 3),
+                'gpu_launches': (2 if verify else 1) * ncalls * args.steps,
                 'samples_ms_per_step': [round(1e3 * t / args.steps, 3) for t in e2e_runs], 'reported': 'median of 3',
-                'sync': {'value': round(e2e_sync, 3), 'unit': 'GB/s',
-                         'api': 'wex_cuda_decode_batch_to_device (drop-in, synchronous)',
-                         'ms_per_step': round(1e3 * sync_s / args.steps, 3),
-                         'samples_ms_per_step': [round(1e3 * t / args.steps, 3) for t in sync_runs]},
+                'sync': ({'value': round(e2e_sync, 3), 'unit': 'GB/s',
+                          'api': 'wex_cuda_decode_batch_to_device (drop-in, synchronous)',
+                          'ms_per_step': round(1e3 * sync_s / args.steps, 3),
+                          'samples_ms_per_step': [round(1e3 * t / args.steps, 3) for t in sync_runs]}
+                         if sync_s else {'skipped': 'verified config: one call at a time waits for whole SHA-256 '
+                                                    'chains, a latency figure, not this workload'}),
                 'roofline': {'bound': 'h2d', 'achieved': round(h2d_per_step / e2e_step_s / 1e9, 2),
                              'peak': round(h2d_calls, 2), 'unit': 'GB/s (stored bytes per GPU)',
                              'frac': round(h2d_per_step / e2e_step_s / 1e9 / h2d_calls, 4),
@@ -1670,7 +1688,7 @@ def run_gpu(args, cfg):
                 'api': f'the reference CUDA helper (c/tools/wex_cuda_bridge.cu, compiled unchanged for sm_100a): '
                        f'wex_cuda_decode_batch_to_device, {B} records per call, {ncalls} calls per step, from the '
                        f'same pinned records into the same destinations',
-                'vs': {'e2e_sync': round(e2e_sync / (gb / g['seconds'] / 1e9), 3),
+                'vs': {'e2e_sync': round(e2e_sync / (gb / g['seconds'] / 1e9), 3) if e2e_sync else None,
                        'e2e': round(e2e / (gb / g['seconds'] / 1e9), 3)}}
             assert g['verified'], 'the reference helper decoded different bytes'
         else:
@@ -1696,7 +1714,8 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-gpu-reference', action='store_true',
                     help='skip the reference CUDA helper timed beside this library (1 GPU)')
-    ap.add_argument('--depth', type=int, default=3, help='e2e: batch calls kept in flight')
+    ap.add_argument('--depth', type=int, default=0,
+                    help='e2e: batch calls kept in flight (default 3; 32 for a verified config)')
     args = ap.parse_args()
     assert args.warmup >= 1
     cfg = CONFIGS[args.config]

@@ -26,6 +26,15 @@ unsigned int wexb_abi(void);
  * bad arguments, -3 when out of host memory. */
 int wexb_batch_submit(int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
                       unsigned char *const *dst_scale, unsigned char *const *dst_weight);
+/* wexb_batch_submit with every record's stored bytes checked on the GPU against sha256[32 i .. 32 i + 32)
+ * (the digest a WEX4 index keeps for the record, c/wex4.h:673-677) before its decode may write the
+ * destination: a record whose bytes hash to anything else gets status -1 (error bit 32) and its
+ * destination stays untouched. The hashes of a call run on their own stream once its records have
+ * landed (one SHA-256 chain per record; keep many calls in flight so that many chains run at once), its
+ * decode after them. Wait with wexb_batch_wait. Returns as wexb_batch_submit; -1 also when sha256 is NULL. */
+int wexb_batch_submit_verified(int n, const WexEntry *const *entries, const unsigned char *const *records,
+                               const unsigned char *sha256, int device, unsigned char *const *dst_scale,
+                               unsigned char *const *dst_weight);
 /* Wait for a ticket: status[i] as wex_cuda_decode_batch_to_device (0 ok, -1 invalid, 1 unavailable;
  * destinations untouched unless 0). Returns the number of non-zero statuses, -1 for an unknown or
  * already-waited ticket. status may be NULL. */
@@ -100,7 +109,8 @@ int wexb_set_wait_limit(double seconds);
 double wexb_wait_limit(void);
 
 /* Error bits of the last failed record seen by this process (1 structure, 2 stream hash, 4 ceil form
- * at scale 0, 8 canonical zero, 16 bounded wait expired); 0 if none failed. */
+ * at scale 0, 8 canonical zero, 16 bounded wait expired, 32 record SHA-256 of a verified batch); 0 if
+ * none failed. */
 unsigned int wexb_last_error_bits(void);
 
 /* Expert records read from a WEX4 container file: the step before the upload. The reference's expert

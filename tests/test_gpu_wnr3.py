@@ -362,6 +362,35 @@ def test_host_wait_gives_up_before_a_long_device_wait(torch_cuda, tiny):
     assert bad == 0 and all(_slab(ts, j) == e.expected for j, e in enumerate(ex))
 
 
+def test_verified_batches(torch_cuda, tiny):
+    """wexb_batch_submit_verified: each record's stored bytes hashed (SHA-256) on the GPU against the digest
+    given for it before its decode may write the destination. Right digests: bit-exact, as the plain
+    batch; a wrong digest: that record alone refused with bit 32, its destination untouched; a damaged
+    record whose digest matches its damaged bytes: refused by the stream hashes instead."""
+    import hashlib
+    blob, ex = tiny
+    digests = [hashlib.sha256(e.record).digest() for e in ex]
+    for _ in range(2):   # two calls in flight
+        pending = []
+        for d in (digests, [digests[0], bytes(32), digests[2]]):
+            ts, sp, wp = _dst(torch_cuda, ex[0].entry, len(ex))
+            pending.append((wexcuda.submit_batch_to_device([e.entry for e in ex], [e.record for e in ex], 0, sp, wp,
+                                                           sha256=d), ts))
+        (t0, ts0), (t1, ts1) = pending
+        assert t1.wait()[1] == [0, -1, 0] and wexcuda.lib().wexb_last_error_bits() & 32
+        assert t0.wait() == (0, [0, 0, 0])
+        for j, e in enumerate(ex):
+            assert _slab(ts0, j) == e.expected
+        assert _slab(ts1, 0) == ex[0].expected and _slab(ts1, 2) == ex[2].expected
+        assert _untouched(ts1, 1)
+    damaged = bytearray(ex[2].record)
+    damaged[7000] ^= 8
+    ts, sp, wp = _dst(torch_cuda, ex[0].entry, 1)
+    t = wexcuda.submit_batch_to_device([ex[2].entry], [bytes(damaged)], 0, sp, wp,
+                                       sha256=[hashlib.sha256(bytes(damaged)).digest()])
+    assert t.wait() == (1, [-1]) and _untouched(ts, 0)
+
+
 def test_queued_batches(torch_cuda, tiny):
     """wexb_batch_submit / wexb_batch_wait: several batches in flight, one with a damaged and an
     unavailable record; each wait gives the statuses of the synchronous call; tickets are single-use."""

@@ -22,6 +22,7 @@
 #include "container.cuh"
 #include "host_wait.h"
 #include "nr3_host.h"
+#include "sha256.cuh"
 #include "wex_cuda_helper.h"
 #include "workspace.h"
 #include "wexb200.h"
@@ -34,9 +35,11 @@ namespace {
 // Byte layout of a call's metadata block (host pinned, copied to the device in one piece): record
 // descriptors, the work queue, its counters, commit jobs, error words, stream offsets.
 struct MetaLayout {
-    size_t recs = 0, items = 0, counters = 0, jobs = 0, errs = 0, offs = 0, landed = 0, total = 0;
-    // nlanded: the records' upload flags, then one word holding 1 (the source of every flag's copy)
-    void compute(size_t k, size_t nitems, size_t ncounters, size_t njobs, size_t noffs, size_t nlanded = 0) {
+    size_t recs = 0, items = 0, counters = 0, jobs = 0, errs = 0, offs = 0, landed = 0, digests = 0, msgs = 0, total = 0;
+    // nlanded: the records' upload flags, then one word holding 1 (the source of every flag's copy);
+    // nhash: records whose SHA-256 is checked (their expected digests and hash jobs)
+    void compute(size_t k, size_t nitems, size_t ncounters, size_t njobs, size_t noffs, size_t nlanded = 0,
+                 size_t nhash = 0) {
         size_t at = 0;
         recs = at; at = align_up(at + k * sizeof(Nr3Record), 256);
         items = at; at = align_up(at + nitems * sizeof(Nr3Item), 256);
@@ -45,6 +48,8 @@ struct MetaLayout {
         errs = at; at = align_up(at + k * 4, 256);
         offs = at; at = align_up(at + noffs * 4, 256);
         landed = at; at = align_up(at + (nlanded ? nlanded + 1 : 0) * 4, 256);
+        digests = at; at = align_up(at + nhash * 32, 256);
+        msgs = at; at = align_up(at + nhash * sizeof(ShaMsg), 256);
         total = at;
     }
 };
@@ -71,9 +76,12 @@ struct Call {
 // Validates n records (host memory) and queues their pipeline: dst_scale / dst_weight (Device) or
 // dst_host (Host: copied back after the kernels; HostChecked: copied back by finish() only after a
 // clean decode). Argument and status rules of the reference batch (c/tools/wex_cuda_bridge.cu:388-487).
-// False when nothing could be queued (c.status then final).
+// expect (verified calls, device destinations): 32 bytes per record, the SHA-256 its stored bytes must
+// have; the hashes run on the GPU before the decode, and a record that differs is refused (-1) with its
+// destination untouched. False when nothing could be queued (c.status then final).
 bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
-            unsigned char *const *dst_scale, unsigned char *const *dst_weight, unsigned char *const *dst_host, Dest mode) {
+            unsigned char *const *dst_scale, unsigned char *const *dst_weight, unsigned char *const *dst_host, Dest mode,
+            const uint8_t *expect = nullptr) {
     const bool host_dst = mode != Dest::Device;
     c.n = n; c.device = device; c.mode = mode; c.dst_host = dst_host;
     c.plans.assign((size_t)n, Plan{});
@@ -126,7 +134,8 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     LaunchSet launches;
     launches.plan(plans.data(), tabs.data(), (uint32_t)k, commit);
     MetaLayout &L = c.L;
-    L.compute(k, launches.items, launches.counter_words(), commit ? k : 0, noffs, k);
+    const bool verify = expect != nullptr && commit;
+    L.compute(k, launches.items, launches.counter_words(), commit ? k : 0, noffs, k, verify ? k : 0);
     if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total)) {
         c.settle(1); workspace_give(w, true); c.w = nullptr; return false;
     }
@@ -154,6 +163,11 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
                         derrs + j, commit ? djobs + j : nullptr, &hrecs[j]);
         hrecs[j].landed = dlanded + j;
         herrs[j] = 0;
+        if (verify) {   // the record's SHA-256 against the expected digest; a difference ORs kErrRecordSha
+            std::memcpy(hm + L.digests + 32 * j, expect + 32 * (size_t)i, 32);
+            reinterpret_cast<ShaMsg *>(hm + L.msgs)[j] = {w->drec.p + rec_off[j], p.total, nullptr, dm + L.digests + 32 * j,
+                                                          derrs + j, kErrRecordSha};
+        }
         if (commit) {
             CommitJob &J = hjobs[j];
             for (int m = 0; m < 3; ++m) {
@@ -180,13 +194,24 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
         if (wait_stream(up) == Waited::TimedOut) c.unsettled = true;
         ok = false;
     }
+    // verified calls: the record hashes, on their own stream once every record has landed; the decode
+    // starts after them (its commits read the error words the hashes may have marked)
+    cudaStream_t hs = nullptr;
+    bool hash_queued = false;   // `hashed` recorded: the kernel stream waits for it whatever happens next
+    if (ok && verify) {
+        ok = hash_stream(device, &hs) && cudaStreamWaitEvent(hs, w->uploads_done, 0) == cudaSuccess &&
+             launch_sha256_messages(reinterpret_cast<const ShaMsg *>(dm + L.msgs), (uint32_t)k, hs) == cudaSuccess;
+        hash_queued = hs && cudaEventRecord(w->hashed, hs) == cudaSuccess;
+        ok = ok && hash_queued;
+    }
     if (ok)
-        ok = cudaStreamWaitEvent(st, w->meta_done, 0) == cudaSuccess &&
+        ok = cudaStreamWaitEvent(st, verify ? w->hashed : w->meta_done, 0) == cudaSuccess &&
              launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + L.items), reinterpret_cast<uint32_t *>(dm + L.counters),
                              sms, st);
-    if (queued_meta && cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess) {
+    if ((queued_meta && cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess) ||
+        (hash_queued && cudaStreamWaitEvent(st, w->hashed, 0) != cudaSuccess)) {
         (void)cudaGetLastError();
-        if (wait_stream(up) == Waited::TimedOut) c.unsettled = true;
+        if (wait_stream(up) == Waited::TimedOut || (hs && wait_stream(hs) == Waited::TimedOut)) c.unsettled = true;
         ok = false;
     }
     for (size_t j = 0; ok && mode == Dest::Host && j < k; ++j) {
@@ -380,6 +405,20 @@ WEXB_API int wexb_batch_submit(int n, const WexEntry *const *entries, const unsi
     Call *c = new (std::nothrow) Call();
     if (!c) return -3;
     (void)submit(*c, n, entries, records, device, dst_scale, dst_weight, nullptr, Dest::Device);   // statuses final if not queued
+    std::lock_guard<std::mutex> lock(g_calls_mu);
+    const int t = g_next_ticket;
+    g_next_ticket = (g_next_ticket + 1) & 0x7fffffff;
+    g_calls.emplace_back(t, c);
+    return t;
+}
+
+WEXB_API int wexb_batch_submit_verified(int n, const WexEntry *const *entries, const unsigned char *const *records,
+                                        const unsigned char *sha256, int device, unsigned char *const *dst_scale,
+                                        unsigned char *const *dst_weight) {
+    if (n <= 0 || !entries || !records || !sha256 || !dst_scale || !dst_weight) return -1;
+    Call *c = new (std::nothrow) Call();
+    if (!c) return -3;
+    (void)submit(*c, n, entries, records, device, dst_scale, dst_weight, nullptr, Dest::Device, sha256);
     std::lock_guard<std::mutex> lock(g_calls_mu);
     const int t = g_next_ticket;
     g_next_ticket = (g_next_ticket + 1) & 0x7fffffff;

@@ -249,7 +249,9 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *_
         if (m.digest) m.digest[k] = got;
         if (m.expect) differ |= got ^ m.expect[k];
     }
-    if (m.verdict) *m.verdict = m.expect ? (differ ? 1u : 0u) : 0u;
+    if (!m.verdict) return;
+    if (m.or_bits) { if (m.expect && differ) atomicOr(m.verdict, m.or_bits); }
+    else *m.verdict = m.expect ? (differ ? 1u : 0u) : 0u;
 }
 
 __global__ void sha256_segments(const ShaMsg *__restrict__ segs, uint32_t n, uint8_t *digest) {

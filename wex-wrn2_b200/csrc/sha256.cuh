@@ -12,7 +12,7 @@ struct ShaMsg {
     uint8_t *digest;          // optional: the 32-byte digest
     const uint8_t *expect;    // optional: a 32-byte digest to compare with
     uint32_t *verdict;        // optional: 0 equal (or no expect), 1 differs
-    uint32_t pad;
+    uint32_t or_bits;         // non-zero: on a difference OR these bits into *verdict, else leave it
 };
 
 // Digests and verdicts of n messages (each 16-byte aligned).

@@ -21,6 +21,7 @@ constexpr uint32_t kModelBytes = 32u + 3u * kContexts * 34u + 3u * 514u;   // 59
 
 // error word bits (the reference's c/wex_cuda.cuh:295-298, plus a bounded-wait timeout)
 constexpr uint32_t kErrStruct = 1, kErrHash = 2, kErrCeil = 4, kErrCz = 8, kErrTimeout = 16;
+constexpr uint32_t kErrRecordSha = 32;   // verified batches: the record's SHA-256 differs from the index's
 // Every wait inside a kernel (on an mbarrier, a flag or a counter) gives up after this many polls and
 // sets kErrTimeout; the self-test entry point accepts at most this many polls as well.
 constexpr uint32_t kWaitPolls = 1u << 24;

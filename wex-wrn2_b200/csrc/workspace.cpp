@@ -20,6 +20,14 @@ struct Queues {
 std::mutex g_queues_mu;
 Queues g_queues[kMaxDevices];
 
+constexpr int kHashStreams = 64;
+struct HashStreams {
+    cudaStream_t s[kHashStreams] = {};
+    unsigned next = 0;
+    bool ok = false;
+};
+HashStreams g_hash[kMaxDevices];
+
 std::mutex g_pool_mu;
 std::vector<Workspace *> g_idle[kMaxDevices];
 std::vector<Workspace *> g_parked[kMaxDevices];   // gave up waiting: back to g_idle once `done` completes
@@ -28,6 +36,7 @@ Workspace *fresh(int device) {
     auto *w = new (std::nothrow) Workspace();
     if (!w) return nullptr;
     if (cudaEventCreateWithFlags(&w->meta_done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&w->hashed, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&w->uploads_done, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&w->done, cudaEventDisableTiming) != cudaSuccess) {
         (void)cudaGetLastError();   // an event made before the failure leaks, on CUDA failure only
@@ -53,6 +62,23 @@ bool device_streams(int device, cudaStream_t *up, cudaStream_t *st) {
     *up = q.upload;
     *st = q.lane[q.next];
     q.next = (q.next + 1u) % kLanes;
+    return true;
+}
+
+bool hash_stream(int device, cudaStream_t *hs) {
+    if (device < 0 || device >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lock(g_queues_mu);
+    HashStreams &h = g_hash[device];
+    if (!h.ok) {
+        for (int i = 0; i < kHashStreams; ++i)
+            if (!h.s[i] && cudaStreamCreateWithFlags(&h.s[i], cudaStreamNonBlocking) != cudaSuccess) {
+                (void)cudaGetLastError();
+                return false;   // streams made so far are kept for the next try
+            }
+        h.ok = true;
+    }
+    *hs = h.s[h.next];
+    h.next = (h.next + 1u) % kHashStreams;
     return true;
 }
 

@@ -12,6 +12,9 @@ namespace wexb {
 // kernel streams, so the kernels of consecutive queued calls may overlap. Created once per device and
 // never destroyed (CUDA cannot be called while the process unloads). False on a CUDA failure.
 bool device_streams(int device, cudaStream_t *up, cudaStream_t *st);
+// A stream for a verified call's record hashes (the next of 64 per device): a record's SHA-256 is one
+// serial chain, so the hashes of every call in flight must run at once. False on a CUDA failure.
+bool hash_stream(int device, cudaStream_t *hs);
 
 // A call's workspace: two events and grown buffers (records, decode scratch, metadata on the device;
 // the metadata's page-locked host image). Pooled per device and never freed, like the reference
@@ -19,7 +22,7 @@ bool device_streams(int device, cudaStream_t *up, cudaStream_t *st);
 // waited for.
 struct Workspace {
     int device = -1;
-    cudaEvent_t meta_done = nullptr, uploads_done = nullptr, done = nullptr;
+    cudaEvent_t meta_done = nullptr, hashed = nullptr, uploads_done = nullptr, done = nullptr;
     DevBuf drec, dscratch, dmeta;
     PinBuf hmeta;
 };

@@ -44,6 +44,7 @@ def lib():
         L.wexb_last_error_bits.restype = U32
         L.wexb_batch_submit.argtypes = [I, P, P, I, P, P]
         L.wexb_batch_wait.argtypes = [I, P]
+        L.wexb_batch_submit_verified.argtypes = [I, P, P, P, I, P, P]
         L.wexb_resident_create.argtypes = [I, P, P, I, P, P]
         L.wexb_resident_bytes.argtypes = [P]; L.wexb_resident_bytes.restype = SZ
         L.wexb_resident_decode.argtypes = [P, I, P, P, P, P]
@@ -133,13 +134,21 @@ def decode_batch_to_host(entries, records, device, dsts):
 class Ticket:
     """A queued device batch (wexb_batch_submit); keeps its arguments alive until wait()."""
 
-    def __init__(self, entries, records, device, dst_scale, dst_weight):
+    def __init__(self, entries, records, device, dst_scale, dst_weight, sha256=None):
+        """sha256: the records' expected SHA-256 digests (32 bytes each) for a verified batch
+        (wexb_batch_submit_verified), or None."""
         self.n = len(entries)
         ep, keep_e = _entries(entries)
         bufs = [_buf(r) for r in records]
         sp, wp = _ptrs(dst_scale), _ptrs(dst_weight)
-        self._keep = (ep, keep_e, bufs, sp, wp)
-        self.ticket = lib().wexb_batch_submit(self.n, ep, _ptrs([b[0] for b in bufs]), device, sp, wp)
+        digests = None if sha256 is None else np.frombuffer(b''.join(bytes(d) for d in sha256), np.uint8).copy()
+        self._keep = (ep, keep_e, bufs, sp, wp, digests)
+        rp = _ptrs([b[0] for b in bufs])
+        if digests is None:
+            self.ticket = lib().wexb_batch_submit(self.n, ep, rp, device, sp, wp)
+        else:
+            assert len(digests) == 32 * self.n
+            self.ticket = lib().wexb_batch_submit_verified(self.n, ep, rp, digests.ctypes.data, device, sp, wp)
         if self.ticket < 0:
             raise RuntimeError(f'wexb_batch_submit: {self.ticket}')
 
@@ -151,8 +160,8 @@ class Ticket:
         return bad, list(status)[:self.n]
 
 
-def submit_batch_to_device(entries, records, device, dst_scale, dst_weight):
-    return Ticket(entries, records, device, dst_scale, dst_weight)
+def submit_batch_to_device(entries, records, device, dst_scale, dst_weight, sha256=None):
+    return Ticket(entries, records, device, dst_scale, dst_weight, sha256)
 
 
 def host_register(array):
