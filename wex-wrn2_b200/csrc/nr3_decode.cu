@@ -35,18 +35,21 @@ constexpr size_t kDecodeSmem = kTableBytes + kRingBytes;
 static_assert(kTableBytes % 16 == 0, "the table block is one TMA bulk copy");
 
 // ---- queue plumbing ---------------------------------------------------------------------------
-// Lane 0 polls `counter` until it reaches `target` (acquire loads, a short sleep between polls, at most
-// kWaitPolls polls); the whole warp then goes on (true) or gives up (false). The warp barrier orders
-// every lane's later reads after lane 0's acquire.
+// Lane 0 polls `counter` until it reaches `target` (acquire loads, at most kWaitPolls polls, with a sleep
+// between polls that doubles from 128 ns to 8 us: a waiting warp must not take issue slots from the
+// decoding warps beside it); the whole warp then goes on (true) or gives up (false). The warp barrier
+// orders every lane's later reads after lane 0's acquire.
 __device__ __forceinline__ bool warp_wait_count(const uint32_t *counter, uint32_t target) {
     uint32_t ok = 1;
     if ((threadIdx.x & 31u) == 0) {
         ok = 0;
+        uint32_t nap = 128;
         for (uint32_t n = 0; n < kWaitPolls; ++n) {
             uint32_t v;
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(counter) : "memory");
             if (v >= target) { ok = 1; break; }
-            __nanosleep(200);
+            __nanosleep(nap);
+            nap = min(2u * nap, 8192u);
         }
     }
     ok = __shfl_sync(~0u, ok, 0);

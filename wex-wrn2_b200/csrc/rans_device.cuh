@@ -108,8 +108,14 @@ __device__ __forceinline__ uint32_t lds_payload(uint32_t a) {
     return v;
 }
 
-__device__ __forceinline__ void cp_async4(uint32_t dst, const uint32_t *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" :: "r"(dst), "l"(src) : "memory");
+// One 4-byte asynchronous copy global -> shared when `go`, else nothing (the instruction is predicated,
+// so the lanes of a warp that copy and those that do not stay converged).
+__device__ __forceinline__ void cp_async4(uint32_t dst, const uint32_t *src, bool go) {
+    asm volatile("{\n"
+                 "  .reg .pred do_copy;\n"
+                 "  setp.eq.u32 do_copy, %2, 1;\n"
+                 "  @do_copy cp.async.ca.shared.global [%0], [%1], 4;\n"
+                 "}\n" :: "r"(dst), "l"(src), "r"((uint32_t)go) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
@@ -123,14 +129,15 @@ struct PayloadWindow {
     uint32_t ask;             // next word to request (a multiple of 4)
     uint32_t stop;            // words at or past this are never requested (one past the stream's last word)
 
-    __device__ __forceinline__ void request_group() {
+    // The next group when `go` (every lane runs the same predicated instructions: no divergence).
+    __device__ __forceinline__ void request_group(bool go) {
         const uint32_t s = ask % kWinWords;
         const uint32_t d = slots + s * kStride;
         const uint32_t *g = words + ask;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) cp_async4(d + k * kStride, g + k);
-        if (s == 0) cp_async4(slots + kWinWords * kStride, g);   // the mirror of slot 0
-        ask += 4;
+        for (int k = 0; k < 4; ++k) cp_async4(d + k * kStride, g + k, go);
+        cp_async4(slots + kWinWords * kStride, g, go && s == 0);   // the mirror of slot 0
+        ask += go ? 4u : 0u;
     }
     // Opens the stream of record bytes [begin, end) (length >= 4, checked on the host) and returns its
     // initial state, the big-endian word at begin. lane_slots: shared address of the lane's slot 0.
@@ -139,8 +146,7 @@ struct PayloadWindow {
         words = reinterpret_cast<const uint32_t *>(rec) + (begin >> 2);
         stop = ((end + 3u) >> 2) - (begin >> 2);
         ask = 0;
-        for (int k = 0; k < 3; ++k)
-            if (ask < stop) request_group();
+        for (int k = 0; k < 3; ++k) request_group(ask < stop);
         cp_async_commit();
         cp_async_wait<0>();
         bit = (begin & 3u) * 8u;
@@ -150,7 +156,7 @@ struct PayloadWindow {
     }
     // Before each 8 symbols: a new group when fewer than 12 words are requested ahead.
     __device__ __forceinline__ void top_up() {
-        if (ask < stop && ask - (bit >> 5) < 12u) request_group();
+        request_group(ask < stop && ask - (bit >> 5) < 12u);
         cp_async_commit();
         cp_async_wait<1>();
     }
