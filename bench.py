@@ -1,34 +1,41 @@
 #!/usr/bin/env python3
 """Decode throughput of WEX4 expert records into HBM on B200 (decoded GB/s and experts/s).
 
-Workload (default "mid"): MoE experts of hidden 2048 and expert FFN 768 (gate/up [768 x 2048], down
-[2048 x 768] in MXFP4: E2M1 nibbles packed two per byte, one E8M0 scale per 32), 48 layers x 128
-experts, per-layer sigma drawn from U(0.01, 0.04), encoded as WNR3 byte-exact records (chunks
-2048:512) under one WNM2 model. A step is one token of routed decode: for each of the 48 layers a
-batch of 8 distinct experts drawn from a Zipf(1.1) popularity over that layer's experts (seeded),
-i.e. 384 expert records and 962 MB of decoded slabs. Inputs are seeded synthetic data (no dataset is
-involved) and larger than L2 between steps.
+Workload (default "large", the largest single-GPU configuration): MoE experts of hidden 7168 and expert
+FFN 2048 (gate/up [2048 x 7168], down [7168 x 2048] in MXFP4: E2M1 nibbles packed two per byte, one E8M0
+scale per 32), 58 layers x 192 experts, per-layer sigma drawn from U(0.01, 0.04), about 3 % of the zero
+nibbles written as -0, encoded as WNR3 records in canonical-zero mode (value-exact; chunks 2048:512)
+under one WNM2 model. A step is one token of routed decode: for each of the 58 layers the top-8 of a
+Zipf(1.1) popularity over that layer's experts (seeded), i.e. 464 expert records of 23.4 MB, 10.9 GB of
+decoded slabs. The routing trace has two distinct token steps, cycled (about 800 distinct records per
+rank, so that they fit in pinned host memory). Inputs are seeded synthetic data (no dataset is involved)
+and larger than L2 between steps.
 
-  value  records resident in HBM (wexb_resident_*), the step's 384 records decoded by one queued
-         decode (3 kernel launches; the next step's decode is planned while this one runs), timed
-         with CUDA events on the launching stream; roofline: the weight kernel against HBM and, as
+  value  records resident in HBM (wexb_resident_*), the step's records decoded by one persistent launch
+         (scale, weight and commit work drained from one queue; two decodes queued, so the next step is
+         planned while this one runs), timed with CUDA events on the launching stream; roofline: that
+         launch against HBM (records read, slabs written, the error-gated commit) and, as
          roofline.issue, against the warp-instruction issue rate that binds it
   e2e    from pinned host memory through the C ABI: per layer one call of 8 records (H2D inside the
-         timed region, statuses read back), 48 calls a step, timed by the host clock (max over
-         ranks); the headline keeps --depth calls in flight (wexb_batch_submit / wexb_batch_wait),
-         e2e.sync is the synchronous drop-in wex_cuda_decode_batch_to_device
+         timed region, statuses read back), 58 calls a step, timed by the host clock (max over ranks);
+         the headline keeps --depth calls in flight (wexb_batch_submit / wexb_batch_wait), e2e.sync is
+         the synchronous drop-in wex_cuda_decode_batch_to_device; each record decodes as its upload lands
+  gpu_reference  the reference's own CUDA helper (compiled unchanged for sm_100a) on the same pinned
+         records and destinations, the synchronous call (1 GPU)
 
 N GPUs (torchrun): expert-parallel placement, rank r decodes the experts whose id = r mod N (weak
-scaling: 384 records per rank per step); the only collectives are the max-over-ranks timing and a
+scaling: 464 records per rank per step); the only collectives are the max-over-ranks timing and a
 final gather of per-rank outcome counters.
 
 --impl reference: the reference's own CPU decoder (wex_nr2_decode via its wex_nr3_decode tool,
-compiled from its sources into oracle/_ref) on all host cores, one record per core, on a bounded
-sample of the same records.
+compiled from its sources into oracle/_ref) on all host cores, one record per core, on a bounded sample
+of the same workload whose records the reference's own encoder made (nothing of this repository is
+loaded in that process).
 
-Other workloads (--config): large and box (hidden 7168, FFN 2048, canonical zero), wnr4 (draft codec
-8 through the WNR4 ABI), tiny-file and mixed (WEX4 containers checked by wex4_check), file (expert
-misses read from a container file on disk: wexb_file_decode) and encode (the GPU record writer).
+Other workloads (--config): mid (hidden 2048, FFN 768, 48 x 128, byte-exact), box (1,536 large experts
+streamed by every step, each record's SHA-256 checked on the GPU before its decode may commit), wnr4
+(draft codec 8 through the WNR4 ABI), tiny-file and mixed (WEX4 containers checked by wex4_check), file
+(expert misses read from a container file on disk: wexb_file_decode) and encode (the GPU record writer).
 """
 import argparse
 import hashlib
