@@ -98,8 +98,9 @@ __device__ __noinline__ uint32_t scale_stream(const Nr3Record &R, uint32_t m, ui
 }
 
 // ---- weight streams ---------------------------------------------------------------------------
+// active: the lanes of the warp decoding a stream of this item (every one of them calls this).
 __device__ __noinline__ uint32_t weight_stream(const Nr3Record &R, uint32_t m, uint32_t j, uint32_t tables,
-                                               uint32_t lane_slots) {
+                                               uint32_t lane_slots, uint32_t active) {
     const uint32_t g = R.wbase[m] + j, begin = R.offsets[g], end = R.offsets[g + 1];
     const uint32_t first = j * R.wchunk, blocks = min(R.wchunk, R.wcount[m] - first) / 32u;
     uint8_t *scales = R.out + R.soff[m] + first / 32u;   // coded scales; the ceil inverse edits them
@@ -113,6 +114,11 @@ __device__ __noinline__ uint32_t weight_stream(const Nr3Record &R, uint32_t m, u
     uint32_t h = nr3 ? ident_hash(R.model_id, R.owner, g, R.word24) : 0u;
     uint32_t scale = blocks ? scales[0] : 0u;
 #pragma unroll 1
+    // The lanes run in lockstep only if nothing makes them part: a rare branch (a ceil-form block)
+    // could otherwise leave the warp split in two halves for the rest of the stream, each issuing every
+    // instruction. When every active lane has the same number of blocks (all but a matrix's last item),
+    // the warp meets at the end of each block.
+    const bool lockstep = __reduce_min_sync(active, blocks) == __reduce_max_sync(active, blocks);
     for (uint32_t b = 0; b < blocks; ++b) {
         const uint32_t next_scale = b + 1 < blocks ? scales[b + 1] : 0u;
         const int d = (int)scale - anchor;
@@ -176,6 +182,7 @@ __device__ __noinline__ uint32_t weight_stream(const Nr3Record &R, uint32_t m, u
         }
         reinterpret_cast<uint4 *>(dst)[b] = make_uint4(w[0], w[1], w[2], w[3]);
         scale = next_scale;
+        if (lockstep) __syncwarp(active);
     }
     pw.close();
     const uint32_t expect = nr3 ? kRansL + (mm3_final(h, 16u + blocks * 16u) & 0x7fffffu) : kRansL;
@@ -254,7 +261,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) nr3_decode(const Nr3Launch 
                 continue;
             }
             const uint32_t j = first + lane;
-            if (j < (R.wcount[sub] + R.wchunk - 1u) / R.wchunk) err = weight_stream(R, sub, j, tables, lane_slots);
+            const bool mine = j < (R.wcount[sub] + R.wchunk - 1u) / R.wchunk;
+            const uint32_t active = __ballot_sync(~0u, mine);
+            if (mine) err = weight_stream(R, sub, j, tables, lane_slots, active);
             if (err) atomicOr(R.error, err);
             item_done(done + 3);
         } else {
