@@ -52,6 +52,9 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, 'wex-wrn2_b200'))
+# One hardware work queue per stream (read when the CUDA context is made): the library's upload, metadata,
+# kernel and hash-lane streams then never wait behind one another's long launches.
+os.environ.setdefault('CUDA_DEVICE_MAX_CONNECTIONS', '32')
 
 CONFIGS = {
     'tiny': dict(hidden=1024, ffn=512, layers=1, experts=8, batch=8, cz=False, sigma=(0.02, 0.02), neg_zero=0.0),
@@ -1477,7 +1480,7 @@ def run_gpu(args, cfg):
     B = cfg['batch']
     entry_store = [np.frombuffer(bytes(e.entry), np.uint8).copy() for e in experts]
     verify = bool(cfg.get('verify'))
-    depth = args.depth or (32 if verify else 3)
+    depth = args.depth or (64 if verify else 3)
     rec_sha = None
     if verify:   # each record's SHA-256, as a WEX4 index keeps it (c/wex4.h:673-677), computed once on the host
         with ThreadPoolExecutor(threads) as pool:
@@ -1722,7 +1725,7 @@ def main():
     ap.add_argument('--no-gpu-reference', action='store_true',
                     help='skip the reference CUDA helper timed beside this library (1 GPU)')
     ap.add_argument('--depth', type=int, default=0,
-                    help='e2e: batch calls kept in flight (default 3; 32 for a verified config)')
+                    help='e2e: batch calls kept in flight (default 3; 64 for a verified config)')
     args = ap.parse_args()
     assert args.warmup >= 1
     cfg = CONFIGS[args.config]

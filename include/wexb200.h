@@ -29,9 +29,13 @@ int wexb_batch_submit(int n, const WexEntry *const *entries, const unsigned char
 /* wexb_batch_submit with every record's stored bytes checked on the GPU against sha256[32 i .. 32 i + 32)
  * (the digest a WEX4 index keeps for the record, c/wex4.h:673-677) before its decode may write the
  * destination: a record whose bytes hash to anything else gets status -1 (error bit 32) and its
- * destination stays untouched. The hashes of a call run on their own stream once its records have
- * landed (one SHA-256 chain per record; keep many calls in flight so that many chains run at once), its
- * decode after them. Wait with wexb_batch_wait. Returns as wexb_batch_submit; -1 also when sha256 is NULL. */
+ * destination stays untouched. Verified calls of a device gather in windows of up to 64 records (or 16
+ * calls): a window's hashes are one launch on one of the device's 8 hash streams once its records have
+ * landed, and its calls' decodes follow them. A window is queued when it is full or when one of its calls
+ * is waited for, so a call may start only at the wait. One SHA-256 chain per record: keep many calls in
+ * flight (tens) so that hundreds of chains run at once, and run the process with
+ * CUDA_DEVICE_MAX_CONNECTIONS=32 so that no stream waits behind another's hash launch. Wait with
+ * wexb_batch_wait. Returns as wexb_batch_submit; -1 also when sha256 is NULL. */
 int wexb_batch_submit_verified(int n, const WexEntry *const *entries, const unsigned char *const *records,
                                const unsigned char *sha256, int device, unsigned char *const *dst_scale,
                                unsigned char *const *dst_weight);

@@ -391,6 +391,31 @@ def test_verified_batches(torch_cuda, tiny):
     assert t.wait() == (1, [-1]) and _untouched(ts, 0)
 
 
+def test_verified_windows(torch_cuda, tiny):
+    """Verified calls gather in hash windows (at most 16 calls or 64 records a window): 20 calls in flight
+    fill one window by their count and leave a partial one that the first wait queues; a wrong digest in
+    a call of either window refuses only that record; waited in reverse order, every slab is bit-exact."""
+    import hashlib
+    blob, ex = tiny
+    digests = [hashlib.sha256(e.record).digest() for e in ex]
+    pending = []
+    for c in range(20):
+        d = list(digests)
+        if c in (3, 18):
+            d[1] = bytes(32)
+        ts, sp, wp = _dst(torch_cuda, ex[0].entry, len(ex))
+        pending.append((c, wexcuda.submit_batch_to_device([e.entry for e in ex], [e.record for e in ex], 0, sp, wp,
+                                                          sha256=d), ts))
+    for c, t, ts in reversed(pending):
+        want = [0, -1, 0] if c in (3, 18) else [0, 0, 0]
+        assert t.wait()[1] == want, c
+        for j, e in enumerate(ex):
+            if want[j] == 0:
+                assert _slab(ts, j) == e.expected, (c, j)
+            else:
+                assert _untouched(ts, j), (c, j)
+
+
 def test_queued_batches(torch_cuda, tiny):
     """wexb_batch_submit / wexb_batch_wait: several batches in flight, one with a damaged and an
     unavailable record; each wait gives the statuses of the synchronous call; tickets are single-use."""

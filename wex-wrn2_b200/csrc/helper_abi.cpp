@@ -35,11 +35,9 @@ namespace {
 // Byte layout of a call's metadata block (host pinned, copied to the device in one piece): record
 // descriptors, the work queue, its counters, commit jobs, error words, stream offsets.
 struct MetaLayout {
-    size_t recs = 0, items = 0, counters = 0, jobs = 0, errs = 0, offs = 0, landed = 0, digests = 0, msgs = 0, total = 0;
-    // nlanded: the records' upload flags, then one word holding 1 (the source of every flag's copy);
+    size_t recs = 0, items = 0, counters = 0, jobs = 0, errs = 0, offs = 0, digests = 0, msgs = 0, total = 0;
     // nhash: records whose SHA-256 is checked (their expected digests and hash jobs)
-    void compute(size_t k, size_t nitems, size_t ncounters, size_t njobs, size_t noffs, size_t nlanded = 0,
-                 size_t nhash = 0) {
+    void compute(size_t k, size_t nitems, size_t ncounters, size_t njobs, size_t noffs, size_t nhash = 0) {
         size_t at = 0;
         recs = at; at = align_up(at + k * sizeof(Nr3Record), 256);
         items = at; at = align_up(at + nitems * sizeof(Nr3Item), 256);
@@ -47,7 +45,6 @@ struct MetaLayout {
         jobs = at; at = align_up(at + njobs * sizeof(CommitJob), 256);
         errs = at; at = align_up(at + k * 4, 256);
         offs = at; at = align_up(at + noffs * 4, 256);
-        landed = at; at = align_up(at + (nlanded ? nlanded + 1 : 0) * 4, 256);
         digests = at; at = align_up(at + nhash * 32, 256);
         msgs = at; at = align_up(at + nhash * sizeof(ShaMsg), 256);
         total = at;
@@ -69,9 +66,130 @@ struct Call {
     size_t k = 0, broken_at = 0;
     bool unsettled = false;   // a bounded wait during submit gave up: the workspace may still be in use
     MetaLayout L;
+    // queued after the uploads by launch_rest(): at once, or for a verified call once its window's
+    // record hashes are queued
+    LaunchSet launches;
+    cudaStream_t up = nullptr, st = nullptr, ms = nullptr;
+    int sms = 0;
+    bool ok = false, queued_meta = false, verify = false, launched = false;
     int failures() const { int bad = 0; for (int v : status) bad += v != 0; return bad; }
     void settle(int v) { for (int &s : status) if (s == kPending) s = v; }
 };
+
+// The part of a call queued after its uploads and metadata: the decode launch (behind the record
+// hashes of a verified call: `hashed`, recorded on hs after them; hash_ok: they were queued), the
+// read-back of the error words and the call's `done` event.
+void launch_rest(Call &c, cudaEvent_t hashed, cudaStream_t hs, bool hash_ok) {
+    Workspace *w = c.w;
+    const MetaLayout &L = c.L;
+    uint8_t *dm = w->dmeta.p;
+    const size_t k = c.k;
+    cudaStream_t st = c.st;
+    bool ok = c.ok && (!c.verify || hash_ok);
+    if (ok)
+        ok = cudaStreamWaitEvent(st, c.verify ? hashed : w->meta_done, 0) == cudaSuccess &&
+             c.launches.launch(reinterpret_cast<const Nr3Record *>(dm + L.recs), reinterpret_cast<const Nr3Item *>(dm + L.items),
+                               reinterpret_cast<uint32_t *>(dm + L.counters), c.sms, st, c.verify);
+    // the read-back and `done` come after every upload (records, flags, metadata) and every hash
+    if (cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess ||
+        (c.queued_meta && cudaStreamWaitEvent(st, w->meta_done, 0) != cudaSuccess) ||
+        (hashed && cudaStreamWaitEvent(st, hashed, 0) != cudaSuccess)) {
+        (void)cudaGetLastError();
+        if (wait_stream(c.up) == Waited::TimedOut || wait_stream(c.ms) == Waited::TimedOut ||
+            (hs && wait_stream(hs) == Waited::TimedOut))
+            c.unsettled = true;
+        ok = false;
+    }
+    for (size_t j = 0; ok && c.mode == Dest::Host && j < k; ++j) {
+        const int i = c.pend[j];
+        const Plan &p = c.plans[(size_t)i];
+        const uint8_t *scr = w->dscratch.p + c.scr_off[j];
+        ok = cudaMemcpyAsync(c.dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+             cudaMemcpyAsync(c.dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost,
+                             st) == cudaSuccess;
+    }
+    c.broken_at = ok ? k : 0;
+    if (!ok) (void)cudaGetLastError();
+    uint32_t *herrs = reinterpret_cast<uint32_t *>(w->hmeta.p + L.errs);
+    const uint32_t *derrs = reinterpret_cast<const uint32_t *>(dm + L.errs);
+    if (!c.queued_meta || cudaMemcpyAsync(herrs, derrs, k * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaEventRecord(w->done, st) != cudaSuccess) {
+        (void)cudaGetLastError();
+        if (cudaEventRecord(w->done, st) != cudaSuccess) {   // `done` must still cover the queued copies
+            (void)cudaGetLastError();
+            c.unsettled = true;
+        }
+        if (wait_stream(st) == Waited::TimedOut) c.unsettled = true;
+        c.broken_at = 0;
+    }
+    c.launched = true;
+}
+
+// ---- hash windows of verified calls --------------------------------------------------------------
+// A record's SHA-256 is one serial chain, so a verified stream needs hundreds of records hashing at
+// once. The verified calls of a device therefore gather in a window (up to kWindowRecords records or
+// kShaParts calls) whose hashes are one launch on the next of the device's hash lanes, behind the
+// uploads of all its calls; each call's decode then waits for that launch. A window is flushed when it
+// is full, or when one of its calls is waited for. Few long launches on few streams keep the hash
+// launches apart from the upload, metadata and kernel streams.
+constexpr uint32_t kWindowRecords = 64;
+std::mutex g_window_mu;
+struct Window { std::vector<Call *> calls; uint32_t records = 0; };
+Window g_window[kMaxDevices];
+
+// (g_window_mu held) Queues the window's hashes and the rest of each of its calls.
+void window_flush(int device) {
+    Window &win = g_window[device];
+    if (win.calls.empty()) return;
+    KeepDevice keep;
+    (void)cudaSetDevice(device);
+    ShaParts P{};
+    uint32_t total = 0;
+    for (Call *c : win.calls)
+        if (c->ok) {
+            total += (uint32_t)c->k;
+            P.part[P.nparts] = reinterpret_cast<const ShaMsg *>(c->w->dmeta.p + c->L.msgs);
+            P.end[P.nparts++] = total;
+        }
+    cudaStream_t hs = nullptr;
+    cudaEvent_t hashed = nullptr;
+    bool hash_ok = false;
+    if (P.nparts && hash_lane(device, &hs, &hashed)) {
+        bool ok = true;
+        for (Call *c : win.calls)
+            if (c->ok)
+                ok = ok && cudaStreamWaitEvent(hs, c->w->uploads_done, 0) == cudaSuccess &&
+                     cudaStreamWaitEvent(hs, c->w->meta_done, 0) == cudaSuccess;
+        ok = ok && launch_sha256_parts(P, hs) == cudaSuccess;
+        if (cudaEventRecord(hashed, hs) != cudaSuccess) {   // nothing can wait for the hashes: wait here (bounded)
+            (void)cudaGetLastError();
+            const bool gave_up = wait_stream(hs) == Waited::TimedOut;
+            for (Call *c : win.calls) c->unsettled = c->unsettled || gave_up;
+            hashed = nullptr;
+            ok = false;
+        }
+        hash_ok = ok;
+    }
+    if (!hash_ok) (void)cudaGetLastError();
+    for (Call *c : win.calls) launch_rest(*c, hashed, hs, hash_ok);
+    win.calls.clear();
+    win.records = 0;
+}
+
+void window_add(Call &c) {
+    std::lock_guard<std::mutex> lock(g_window_mu);
+    Window &win = g_window[c.device];
+    win.calls.push_back(&c);
+    win.records += (uint32_t)c.k;
+    if (win.records >= kWindowRecords || win.calls.size() >= (size_t)kShaParts) window_flush(c.device);
+}
+
+// Before a wait: a verified call still in its window is queued now.
+void ensure_launched(Call &c) {
+    if (!c.w || c.launched) return;
+    std::lock_guard<std::mutex> lock(g_window_mu);
+    if (!c.launched) window_flush(c.device);
+}
 
 // Validates n records (host memory) and queues their pipeline: dst_scale / dst_weight (Device) or
 // dst_host (Host: copied back after the kernels; HostChecked: copied back by finish() only after a
@@ -79,6 +197,10 @@ struct Call {
 // expect (verified calls, device destinations): 32 bytes per record, the SHA-256 its stored bytes must
 // have; the hashes run on the GPU before the decode, and a record that differs is refused (-1) with its
 // destination untouched. False when nothing could be queued (c.status then final).
+//
+// Each record's upload is queued as soon as that record is validated, so the copy engine starts on
+// the first record while the host still parses the others; the launch metadata (built once every
+// record is planned) goes up on the device's metadata stream, beside the record copies.
 bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char *const *records, int device,
             unsigned char *const *dst_scale, unsigned char *const *dst_weight, unsigned char *const *dst_host, Dest mode,
             const uint8_t *expect = nullptr) {
@@ -86,150 +208,140 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
     c.n = n; c.device = device; c.mode = mode; c.dst_host = dst_host;
     c.plans.assign((size_t)n, Plan{});
     c.status.assign((size_t)n, -1);
+    // argument checks only; each record is parsed just before its upload
+    std::vector<int> cand;
+    size_t rec_cap = 0, scr_cap = 0;
     for (int i = 0; i < n; ++i) {
         const WexEntry *e = entries[i];
         if (!e || !records[i]) continue;
         bool targets = host_dst ? dst_host[i] != nullptr : true;
         if (!host_dst) for (int m = 0; m < 3; ++m) if (!dst_scale[3 * i + m] || !dst_weight[3 * i + m]) targets = false;
-        if (!targets || plan_record(e, records[i], &c.plans[(size_t)i])) continue;
-        if (!model_registered(c.plans[(size_t)i].model_id)) { c.status[(size_t)i] = 1; continue; }
+        uint64_t raw, aligned;
+        if (!targets || entry_raw_sizes(e, &raw, &aligned) || e->total_bytes >= aligned) continue;   // -1 as parsed
+        cand.push_back(i);
+        rec_cap += align_up((size_t)e->total_bytes + kRecordSlack, 256);
+        scr_cap += align_up((size_t)raw + 16, 256);   // decode layout: scales, then weights 16-aligned
+    }
+    if (cand.empty()) return false;
+    // the device side: streams, a workspace, its token (every failure: valid records report 1)
+    const bool commit = mode == Dest::Device;
+    const bool verify = expect != nullptr && commit;
+    cudaStream_t up = nullptr, st = nullptr, ms = nullptr;
+    Workspace *w = nullptr;
+    int sms = 0;
+    uint32_t token = 0;
+    if (device >= 0 && device < kMaxDevices && cudaSetDevice(device) == cudaSuccess && device_streams(device, &up, &st, &ms) &&
+        (sms = device_sms(device)) > 0 && (w = workspace_take(device)) != nullptr)
+        token = w->drec.grow(rec_cap) && w->dscratch.grow(scr_cap) ? w->take_token(cand.size(), ms) : 0u;
+    if (!token) {
+        (void)cudaGetLastError();
+        if (w) workspace_give(w, true);
+        for (int i : cand) if (!plan_record(entries[i], records[i], &c.plans[(size_t)i])) c.status[(size_t)i] = 1;
+        return false;
+    }
+    c.w = w;
+    // plan and upload record by record (call order); a record's flag word follows its bytes
+    uint32_t *dflags = reinterpret_cast<uint32_t *>(w->dflags.p);
+    const uint32_t *htoken = reinterpret_cast<const uint32_t *>(w->htoken.p);
+    std::vector<const uint8_t *> tabs_of((size_t)n, nullptr);
+    std::vector<size_t> rec_off((size_t)n, 0);
+    std::vector<uint32_t> flag_of((size_t)n, 0);
+    bool ok = true;
+    size_t rec_bytes = 0;
+    uint32_t copied = 0;
+    for (int i : cand) {
+        Plan &p = c.plans[(size_t)i];
+        if (plan_record(entries[i], records[i], &p)) continue;
+        if (!model_registered(p.model_id) || model_tables(p.model_id, device, &tabs_of[(size_t)i])) {
+            c.status[(size_t)i] = 1;
+            continue;
+        }
         c.status[(size_t)i] = kPending;
         c.pend.push_back(i);
+        rec_off[(size_t)i] = rec_bytes;
+        rec_bytes += align_up(p.total + kRecordSlack, 256);
+        flag_of[(size_t)i] = copied++;
+        ok = ok && cudaMemcpyAsync(w->drec.p + rec_off[(size_t)i], records[i], p.total, cudaMemcpyHostToDevice, up) == cudaSuccess &&
+             cudaMemcpyAsync(dflags + flag_of[(size_t)i], htoken, 4, cudaMemcpyHostToDevice, up) == cudaSuccess;
     }
-    if (c.pend.empty()) return false;
-    if (device < 0 || device >= kMaxDevices || cudaSetDevice(device) != cudaSuccess) {
-        (void)cudaGetLastError(); c.settle(1); return false;
+    if (cudaEventRecord(w->uploads_done, up) != cudaSuccess) {
+        (void)cudaGetLastError();
+        if (copied && wait_stream(up) == Waited::TimedOut) c.unsettled = true;
+        ok = false;
     }
-    std::vector<const uint8_t *> tabs;   // device tables of every record's model
-    {
-        std::vector<std::pair<int, const uint8_t *>> keep;
-        for (int i : c.pend) {
-            const uint8_t *t = nullptr;
-            if (model_tables(c.plans[(size_t)i].model_id, device, &t)) { c.status[(size_t)i] = 1; continue; }
-            keep.emplace_back(i, t);
-        }
-        // one launch per model: the records of a model contiguous (call order otherwise)
-        std::stable_sort(keep.begin(), keep.end(), [](const auto &a, const auto &b) { return a.second < b.second; });
-        c.pend.clear();
-        for (const auto &e : keep) { c.pend.push_back(e.first); tabs.push_back(e.second); }
+    if (c.pend.empty()) {   // nothing was queued
+        c.w = nullptr;
+        workspace_give(w, !c.unsettled);
+        return false;
     }
+    // one launch per model: the records of a model contiguous (call order otherwise)
+    std::stable_sort(c.pend.begin(), c.pend.end(), [&](int a, int b) { return tabs_of[(size_t)a] < tabs_of[(size_t)b]; });
     const size_t k = c.k = c.pend.size();
-    if (!k) return false;
-    const int sms = device_sms(device);
-    Workspace *w = c.w = workspace_take(device);
-    if (!w || !sms) { c.settle(1); workspace_give(w, true); c.w = nullptr; return false; }
-    // layout
-    const bool commit = mode == Dest::Device;
-    std::vector<size_t> rec_off(k), off_off(k);
+    std::vector<size_t> off_off(k);
     std::vector<const Plan *> plans(k);
+    std::vector<const uint8_t *> tabs(k);
     c.scr_off.assign(k, 0);
-    size_t rec_bytes = 0, scr_bytes = 0, noffs = 0;
+    size_t scr_bytes = 0, noffs = 0;
     for (size_t j = 0; j < k; ++j) {
         const Plan &p = c.plans[(size_t)c.pend[j]];
         plans[j] = &p;
-        rec_off[j] = rec_bytes; rec_bytes += align_up(p.total + kRecordSlack, 256);
+        tabs[j] = tabs_of[(size_t)c.pend[j]];
         c.scr_off[j] = scr_bytes; scr_bytes += align_up(p.scratch, 256);
         off_off[j] = noffs; noffs += p.streams() + 1;
     }
     LaunchSet launches;
     launches.plan(plans.data(), tabs.data(), (uint32_t)k, commit);
     MetaLayout &L = c.L;
-    const bool verify = expect != nullptr && commit;
-    L.compute(k, launches.items, launches.counter_words(), commit ? k : 0, noffs, k, verify ? k : 0);
-    if (!w->drec.grow(rec_bytes) || !w->dscratch.grow(scr_bytes) || !w->dmeta.grow(L.total) || !w->hmeta.grow(L.total)) {
-        c.settle(1); workspace_give(w, true); c.w = nullptr; return false;
-    }
+    L.compute(k, launches.items, launches.counter_words(), commit ? k : 0, noffs, verify ? k : 0);
+    // (the scratch was grown for the entries' raw sizes before the uploads; a plan's scratch is that
+    // raw size rounded up to 16, so this grow does not reallocate)
+    ok = ok && w->dscratch.grow(scr_bytes) && w->dmeta.grow(L.total) && w->hmeta.grow(L.total);
     uint8_t *hm = w->hmeta.p, *dm = w->dmeta.p;
     Nr3Record *hrecs = reinterpret_cast<Nr3Record *>(hm + L.recs);
     CommitJob *hjobs = reinterpret_cast<CommitJob *>(hm + L.jobs);
     uint32_t *herrs = reinterpret_cast<uint32_t *>(hm + L.errs);
     uint32_t *hoffs = reinterpret_cast<uint32_t *>(hm + L.offs);
-    const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + L.recs);
     const CommitJob *djobs = reinterpret_cast<const CommitJob *>(dm + L.jobs);
     uint32_t *derrs = reinterpret_cast<uint32_t *>(dm + L.errs);
-    // records are decoded as their uploads land (one record's scale items ahead of the weight items)
-    launches.fill(plans.data(), commit, sms, 1, reinterpret_cast<Nr3Item *>(hm + L.items),
-                  reinterpret_cast<uint32_t *>(hm + L.counters));
-    uint32_t *hlanded = reinterpret_cast<uint32_t *>(hm + L.landed);
-    uint32_t *dlanded = reinterpret_cast<uint32_t *>(dm + L.landed);
-    std::memset(hlanded, 0, 4 * k);
-    hlanded[k] = 1;
-    for (size_t j = 0; j < k; ++j) {
-        const int i = c.pend[j];
-        const Plan &p = c.plans[(size_t)i];
-        uint8_t *scr = w->dscratch.p + c.scr_off[j];
-        plan_offsets(p, hoffs + off_off[j]);
-        plan_descriptor(p, w->drec.p + rec_off[j], reinterpret_cast<const uint32_t *>(dm + L.offs) + off_off[j], scr,
-                        derrs + j, commit ? djobs + j : nullptr, &hrecs[j]);
-        hrecs[j].landed = dlanded + j;
-        herrs[j] = 0;
-        if (verify) {   // the record's SHA-256 against the expected digest; a difference ORs kErrRecordSha
-            std::memcpy(hm + L.digests + 32 * j, expect + 32 * (size_t)i, 32);
-            reinterpret_cast<ShaMsg *>(hm + L.msgs)[j] = {w->drec.p + rec_off[j], p.total, nullptr, dm + L.digests + 32 * j,
-                                                          derrs + j, kErrRecordSha};
-        }
-        if (commit) {
-            CommitJob &J = hjobs[j];
-            for (int m = 0; m < 3; ++m) {
-                J.src[m] = scr + p.soff[m]; J.dst[m] = dst_scale[3 * i + m]; J.bytes[m] = p.dst_bytes[m];
-                J.src[3 + m] = scr + p.wout[m]; J.dst[3 + m] = dst_weight[3 * i + m]; J.bytes[3 + m] = p.dst_bytes[3 + m];
+    if (ok) {
+        // records are decoded as their uploads land (one record's scale items ahead of the weight items)
+        launches.fill(plans.data(), commit, sms, 1, reinterpret_cast<Nr3Item *>(hm + L.items),
+                      reinterpret_cast<uint32_t *>(hm + L.counters));
+        for (size_t j = 0; j < k; ++j) {
+            const int i = c.pend[j];
+            const Plan &p = c.plans[(size_t)i];
+            uint8_t *scr = w->dscratch.p + c.scr_off[j];
+            plan_offsets(p, hoffs + off_off[j]);
+            plan_descriptor(p, w->drec.p + rec_off[(size_t)i], reinterpret_cast<const uint32_t *>(dm + L.offs) + off_off[j],
+                            scr, derrs + j, commit ? djobs + j : nullptr, &hrecs[j]);
+            hrecs[j].landed = dflags + flag_of[(size_t)i];
+            hrecs[j].landed_at = token;
+            herrs[j] = 0;
+            if (verify) {   // the record's SHA-256 against the expected digest; a difference ORs kErrRecordSha
+                std::memcpy(hm + L.digests + 32 * j, expect + 32 * (size_t)i, 32);
+                reinterpret_cast<ShaMsg *>(hm + L.msgs)[j] = {w->drec.p + rec_off[(size_t)i], p.total, nullptr,
+                                                              dm + L.digests + 32 * j, derrs + j, kErrRecordSha};
+            }
+            if (commit) {
+                CommitJob &J = hjobs[j];
+                for (int m = 0; m < 3; ++m) {
+                    J.src[m] = scr + p.soff[m]; J.dst[m] = dst_scale[3 * i + m]; J.bytes[m] = p.dst_bytes[m];
+                    J.src[3 + m] = scr + p.wout[m]; J.dst[3 + m] = dst_weight[3 * i + m]; J.bytes[3 + m] = p.dst_bytes[3 + m];
+                }
             }
         }
+        // metadata stream: the whole block in one copy. Kernel stream: once it is there, one persistent
+        // launch per model, whose scale items wait for each record's flag, so the records decode as
+        // they land; then, after every upload, the read-back of the error words (`done`, recorded
+        // last, covers the whole call)
+        ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, ms) == cudaSuccess &&
+             cudaEventRecord(w->meta_done, ms) == cudaSuccess;
     }
-    // enqueue. Upload stream: the metadata, then each record followed by the copy of a 1 into its
-    // `landed` word. Kernel stream: once the metadata is there, one persistent launch per model, whose
-    // items wait for each record's flag, so the records decode as they land; then, after every upload,
-    // the read-back of the error words (`done`, recorded last, covers the whole call)
-    cudaStream_t up = nullptr, st = nullptr;
-    if (!device_streams(device, &up, &st)) { c.settle(1); workspace_give(w, true); c.w = nullptr; return false; }
-    bool ok = cudaMemcpyAsync(dm, hm, L.total, cudaMemcpyHostToDevice, up) == cudaSuccess &&
-              cudaEventRecord(w->meta_done, up) == cudaSuccess;
-    for (size_t j = 0; ok && j < k; ++j)   // the flag's copy comes from the page-locked block: a copy engine sets it
-        ok = cudaMemcpyAsync(w->drec.p + rec_off[j], records[c.pend[j]], c.plans[(size_t)c.pend[j]].total,
-                             cudaMemcpyHostToDevice, up) == cudaSuccess &&
-             cudaMemcpyAsync(dlanded + j, hlanded + k, 4, cudaMemcpyHostToDevice, up) == cudaSuccess;
-    const bool queued_meta = ok;
-    if (cudaEventRecord(w->uploads_done, up) != cudaSuccess) {
-        (void)cudaGetLastError();
-        if (wait_stream(up) == Waited::TimedOut) c.unsettled = true;
-        ok = false;
-    }
-    // verified calls: the record hashes, on their own stream once every record has landed; the decode
-    // starts after them (its commits read the error words the hashes may have marked)
-    cudaStream_t hs = nullptr;
-    bool hash_queued = false;   // `hashed` recorded: the kernel stream waits for it whatever happens next
-    if (ok && verify) {
-        ok = hash_stream(device, &hs) && cudaStreamWaitEvent(hs, w->uploads_done, 0) == cudaSuccess &&
-             launch_sha256_messages(reinterpret_cast<const ShaMsg *>(dm + L.msgs), (uint32_t)k, hs) == cudaSuccess;
-        hash_queued = hs && cudaEventRecord(w->hashed, hs) == cudaSuccess;
-        ok = ok && hash_queued;
-    }
-    if (ok)
-        ok = cudaStreamWaitEvent(st, verify ? w->hashed : w->meta_done, 0) == cudaSuccess &&
-             launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + L.items), reinterpret_cast<uint32_t *>(dm + L.counters),
-                             sms, st);
-    if ((queued_meta && cudaStreamWaitEvent(st, w->uploads_done, 0) != cudaSuccess) ||
-        (hash_queued && cudaStreamWaitEvent(st, w->hashed, 0) != cudaSuccess)) {
-        (void)cudaGetLastError();
-        if (wait_stream(up) == Waited::TimedOut || (hs && wait_stream(hs) == Waited::TimedOut)) c.unsettled = true;
-        ok = false;
-    }
-    for (size_t j = 0; ok && mode == Dest::Host && j < k; ++j) {
-        const int i = c.pend[j];
-        const Plan &p = c.plans[(size_t)i];
-        const uint8_t *scr = w->dscratch.p + c.scr_off[j];
-        ok = cudaMemcpyAsync(dst_host[i], scr, p.scale_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-             cudaMemcpyAsync(dst_host[i] + p.scale_bytes, scr + p.weight_at, p.weight_bytes, cudaMemcpyDeviceToHost,
-                             st) == cudaSuccess;
-    }
-    c.broken_at = ok ? k : 0;
-    if (!ok) (void)cudaGetLastError();
-    if (cudaMemcpyAsync(herrs, derrs, k * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaEventRecord(w->done, st) != cudaSuccess) {
-        (void)cudaGetLastError();
-        if (wait_stream(st) == Waited::TimedOut) c.unsettled = true;
-        c.broken_at = 0;
-    }
+    c.launches = std::move(launches);
+    c.up = up; c.st = st; c.ms = ms; c.sms = sms;
+    c.ok = ok; c.queued_meta = ok; c.verify = verify;
+    if (verify) window_add(c);   // its decode is queued once its window's record hashes are
+    else launch_rest(c, nullptr, nullptr, false);
     return true;
 }
 
@@ -238,6 +350,7 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
 void finish(Call &c) {
     Workspace *w = c.w;
     if (!w) { c.settle(1); return; }
+    ensure_launched(c);
     (void)cudaSetDevice(c.device);
     const Waited waited = c.unsettled ? Waited::TimedOut : wait_event(w->done);
     const bool synced = waited == Waited::Done;

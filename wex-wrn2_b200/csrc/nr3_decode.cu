@@ -30,8 +30,8 @@ namespace {
 
 using namespace rans;
 
-constexpr size_t kRingBytes = (size_t)(kWinWords + 1) * 4u * kDecodeThreads;
-constexpr size_t kDecodeSmem = kTableBytes + kRingBytes;
+// dynamic shared memory of a CTA of kThreads threads: the table block, then every lane's payload ring
+template <int kThreads> constexpr size_t decode_smem() { return kTableBytes + (size_t)(kWinWords + 1) * 4u * kThreads; }
 static_assert(kTableBytes % 16 == 0, "the table block is one TMA bulk copy");
 
 // ---- queue plumbing ---------------------------------------------------------------------------
@@ -78,13 +78,14 @@ __device__ __forceinline__ uint32_t coded_neg_zero(const uint32_t w[4]) {
 }
 // ---- scale streams ----------------------------------------------------------------------------
 // tables, lane_slots: shared addresses of the staged table block and of the lane's payload slot 0.
+template <int kThreads>
 __device__ __noinline__ uint32_t scale_stream(const Nr3Record &R, uint32_t m, uint32_t j, uint32_t tables,
                                               uint32_t lane_slots) {
     const uint32_t g = R.sbase[m] + j, begin = R.offsets[g], end = R.offsets[g + 1];
     const uint32_t first = j * R.schunk, count = min(R.schunk, R.scount[m] - first);
     const uint32_t ssym = tables + (uint32_t)kWTableBytes + m * kTotal;
     const uint32_t sf = tables + (uint32_t)(kWTableBytes + kSsymBytes) + m * kSfBytes;
-    PayloadWindow<kDecodeThreads> pw;
+    PayloadWindow<kThreads> pw;
     uint32_t x = pw.open(R.rec, begin, end, lane_slots);
     uint32_t err = (x - kRansL >= 255u * kRansL) ? kErrStruct : 0u;   // a valid initial state is in [L, 256 L)
     const bool nr3 = R.flags & 256u;
@@ -99,6 +100,7 @@ __device__ __noinline__ uint32_t scale_stream(const Nr3Record &R, uint32_t m, ui
 
 // ---- weight streams ---------------------------------------------------------------------------
 // active: the lanes of the warp decoding a stream of this item (every one of them calls this).
+template <int kThreads>
 __device__ __noinline__ uint32_t weight_stream(const Nr3Record &R, uint32_t m, uint32_t j, uint32_t tables,
                                                uint32_t lane_slots, uint32_t active) {
     const uint32_t g = R.wbase[m] + j, begin = R.offsets[g], end = R.offsets[g + 1];
@@ -108,17 +110,17 @@ __device__ __noinline__ uint32_t weight_stream(const Nr3Record &R, uint32_t m, u
     const uint32_t level1 = tables + m * kWBlockBytes, level2 = level1 + kWL1Bytes;   // rows of 8 bytes
     const bool nr3 = R.flags & 256u, cz = nr3 && (R.flags & 8u), ceil = nr3 && ((R.flags >> m) & 1u);
     const int anchor = (int)((R.word24 >> (8u * m)) & 0xffu);
-    PayloadWindow<kDecodeThreads> pw;
+    PayloadWindow<kThreads> pw;
     uint32_t x = pw.open(R.rec, begin, end, lane_slots);
     uint32_t err = (x - kRansL >= 255u * kRansL) ? kErrStruct : 0u;
     uint32_t h = nr3 ? ident_hash(R.model_id, R.owner, g, R.word24) : 0u;
     uint32_t scale = blocks ? scales[0] : 0u;
-#pragma unroll 1
     // The lanes run in lockstep only if nothing makes them part: a rare branch (a ceil-form block)
     // could otherwise leave the warp split in two halves for the rest of the stream, each issuing every
     // instruction. When every active lane has the same number of blocks (all but a matrix's last item),
     // the warp meets at the end of each block.
     const bool lockstep = __reduce_min_sync(active, blocks) == __reduce_max_sync(active, blocks);
+#pragma unroll 1
     for (uint32_t b = 0; b < blocks; ++b) {
         const uint32_t next_scale = b + 1 < blocks ? scales[b + 1] : 0u;
         const int d = (int)scale - anchor;
@@ -219,7 +221,10 @@ __device__ __noinline__ void commit_chunk(const CommitJob &J, uint32_t region, u
 }
 
 // ---- the persistent kernel --------------------------------------------------------------------
-__global__ void __launch_bounds__(kDecodeThreads, 1) nr3_decode(const Nr3Launch L) {
+// 64 registers a thread in both CTA sizes (1,024 threads: the whole register file; 832 threads: room
+// for two record-hash CTAs beside it)
+template <int kThreads>
+__global__ void __maxnreg__(64) nr3_decode(const Nr3Launch L) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bar;
     {
@@ -246,13 +251,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) nr3_decode(const Nr3Launch 
         uint32_t *done = L.done + 4u * it.rec;
         uint32_t err = 0;
         if (kind == kItemScale) {
-            if (R.landed && !warp_wait_count(R.landed, 1u)) {   // the record's bytes never arrived
+            if (R.landed && !warp_wait_count(R.landed, R.landed_at)) {   // the record's bytes never arrived
                 if (lane == 0) atomicOr(R.error, kErrTimeout);
                 item_done(done + sub);
                 continue;
             }
             const uint32_t j = first + lane;
-            if (j < (R.scount[sub] + R.schunk - 1u) / R.schunk) err = scale_stream(R, sub, j, tables, lane_slots);
+            if (j < (R.scount[sub] + R.schunk - 1u) / R.schunk) err = scale_stream<kThreads>(R, sub, j, tables, lane_slots);
             if (err) atomicOr(R.error, err);
             item_done(done + sub);
         } else if (kind == kItemWeight) {
@@ -263,7 +268,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) nr3_decode(const Nr3Launch 
             const uint32_t j = first + lane;
             const bool mine = j < (R.wcount[sub] + R.wchunk - 1u) / R.wchunk;
             const uint32_t active = __ballot_sync(~0u, mine);
-            if (mine) err = weight_stream(R, sub, j, tables, lane_slots, active);
+            if (mine) err = weight_stream<kThreads>(R, sub, j, tables, lane_slots, active);
             if (err) atomicOr(R.error, err);
             item_done(done + 3);
         } else {
@@ -279,12 +284,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) nr3_decode(const Nr3Launch 
 }  // namespace
 
 cudaError_t prepare_nr3_kernels() {
-    return cudaFuncSetAttribute(nr3_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmem);
+    const cudaError_t e = cudaFuncSetAttribute(nr3_decode<kDecodeThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)decode_smem<kDecodeThreads>());
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(nr3_decode<kBesideHashThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)decode_smem<kBesideHashThreads>());
 }
 
-cudaError_t launch_nr3(const Nr3Launch &L, int sms, cudaStream_t st) {
+cudaError_t launch_nr3(const Nr3Launch &L, int sms, cudaStream_t st, bool beside_hashes) {
     if (!L.nitems) return cudaSuccess;
-    nr3_decode<<<sms, kDecodeThreads, kDecodeSmem, st>>>(L);
+    if (beside_hashes)
+        nr3_decode<kBesideHashThreads>
+            <<<(sms + 1) / 2, kBesideHashThreads, decode_smem<kBesideHashThreads>(), st>>>(L);
+    else
+        nr3_decode<kDecodeThreads><<<sms, kDecodeThreads, decode_smem<kDecodeThreads>(), st>>>(L);
     return cudaGetLastError();
 }
 

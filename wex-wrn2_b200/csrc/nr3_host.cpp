@@ -304,13 +304,14 @@ void LaunchSet::fill(const Plan *const *plans, bool commit, int sms, uint32_t sc
     std::memset(counters, 0, 4 * counter_words());
 }
 
-bool LaunchSet::launch(const Nr3Record *drecs, const Nr3Item *ditems, uint32_t *dcounters, int sms, cudaStream_t st) const {
+bool LaunchSet::launch(const Nr3Record *drecs, const Nr3Item *ditems, uint32_t *dcounters, int sms, cudaStream_t st,
+                       bool beside_hashes) const {
     const size_t heads = groups.size();
     for (size_t i = 0; i < heads; ++i) {
         const Group &g = groups[i];
         const Nr3Launch L{drecs + g.first_rec, ditems + g.first_item, dcounters + i, dcounters + heads + 4ull * g.first_rec,
                           g.tables, g.nitems, g.nrecs};
-        if (launch_nr3(L, sms, st) != cudaSuccess) return false;
+        if (launch_nr3(L, sms, st, beside_hashes) != cudaSuccess) return false;
     }
     return true;
 }

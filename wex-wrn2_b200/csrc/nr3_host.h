@@ -86,8 +86,10 @@ struct LaunchSet {
     // (counter_words()).
     void fill(const Plan *const *plans, bool commit, int sms, uint32_t scale_lead, Nr3Item *items_out,
               uint32_t *counters) const;
-    // Launches every group on st over the device copies of the records, items and counters.
-    bool launch(const Nr3Record *drecs, const Nr3Item *ditems, uint32_t *dcounters, int sms, cudaStream_t st) const;
+    // Launches every group on st over the device copies of the records, items and counters
+    // (beside_hashes: the footprint that leaves room for record-hash CTAs, launch_nr3).
+    bool launch(const Nr3Record *drecs, const Nr3Item *ditems, uint32_t *dcounters, int sms, cudaStream_t st,
+                bool beside_hashes = false) const;
 };
 // Slack a record buffer keeps after each record: a stream's payload window may read up to 12 bytes
 // past the stream's end (rans_device.cuh).

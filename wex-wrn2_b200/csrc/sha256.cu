@@ -155,12 +155,14 @@ __device__ __forceinline__ void produce_block(const uint8_t *data, uint64_t byte
     if (last) { w[14] = (uint32_t)(bits >> 32); w[15] = (uint32_t)bits; }
 }
 
-__global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaMsg *__restrict__ msgs, uint32_t n) {
+__global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaParts P) {
     __shared__ uint4 sched[2][16][kShaLanes];   // [slot][rounds 4g .. 4g+3][lane]: W[t] + K[t]
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t i = blockIdx.x * kShaLanes + lane;
-    const bool active = i < n;
-    const ShaMsg m = active ? msgs[i] : ShaMsg{nullptr, 0, nullptr, nullptr, nullptr, 0};
+    const bool active = P.nparts && i < P.end[P.nparts - 1];
+    uint32_t part = 0;
+    while (active && i >= P.end[part]) ++part;
+    const ShaMsg m = active ? P.part[part][i - (part ? P.end[part - 1] : 0u)] : ShaMsg{nullptr, 0, nullptr, nullptr, nullptr, 0};
     const uint32_t mine = active ? msg_blocks(m.bytes) : 0u;
     const uint32_t blocks = __reduce_max_sync(0xffffffffu, mine);
     if (warp == 1) {   // producer
@@ -264,10 +266,20 @@ __global__ void sha256_segments(const ShaMsg *__restrict__ segs, uint32_t n, uin
 
 }  // namespace
 
-cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st) {
+cudaError_t launch_sha256_parts(const ShaParts &P, cudaStream_t st) {
+    const uint32_t n = P.nparts ? P.end[P.nparts - 1] : 0u;
     if (!n) return cudaSuccess;
-    sha256_messages<<<(n + kShaLanes - 1) / kShaLanes, 2 * kShaLanes, 0, st>>>(msgs, n);
+    if (P.nparts > (uint32_t)kShaParts) return cudaErrorInvalidValue;
+    sha256_messages<<<(n + kShaLanes - 1) / kShaLanes, 2 * kShaLanes, 0, st>>>(P);
     return cudaGetLastError();
+}
+
+cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st) {
+    ShaParts P{};
+    P.part[0] = msgs;
+    P.end[0] = n;
+    P.nparts = 1;
+    return launch_sha256_parts(P, st);
 }
 
 cudaError_t launch_sha256_segments(const ShaMsg *segs, uint32_t n, uint8_t *digest, cudaStream_t st) {

@@ -17,6 +17,15 @@ struct ShaMsg {
 
 // Digests and verdicts of n messages (each 16-byte aligned).
 cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st);
+// The same for up to kShaParts arrays of messages in one launch (say the records of several calls):
+// messages [end[p - 1], end[p]) of the launch are part[p][0 ..] (end[-1] = 0).
+constexpr int kShaParts = 16;
+struct ShaParts {
+    const ShaMsg *part[kShaParts];
+    uint32_t end[kShaParts];
+    uint32_t nparts;
+};
+cudaError_t launch_sha256_parts(const ShaParts &P, cudaStream_t st);
 // One thread: the digest of the concatenation of n segments (data and bytes used).
 cudaError_t launch_sha256_segments(const ShaMsg *segs, uint32_t n, uint8_t *digest, cudaStream_t st);
 

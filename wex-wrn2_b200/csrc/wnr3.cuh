@@ -65,7 +65,7 @@ struct Nr3Record {
     uint8_t *out;              // decoded slab, decode layout: scales at soff[m], weights at wout[m]
     uint32_t *error;           // error bits of this record (zero when the launch starts)
     const CommitJob *job;      // the error-gated copy to the caller's buffers, or null (none)
-    const uint32_t *landed;    // non-zero once the record's upload has landed, or null (already there)
+    const uint32_t *landed;    // reaches landed_at once the record's upload has landed, or null (already there)
     uint32_t scount[3], wcount[3];   // scales / 4-bit weights of matrix m
     uint32_t soff[3], wout[3];       // their offsets in out (wout 16-byte aligned)
     uint32_t schunk, wchunk;         // symbols per stream
@@ -74,11 +74,13 @@ struct Nr3Record {
     uint32_t flags;                  // bits 0-2 ceil mask, bit 3 canonical zero, bit 8 WNR3 (else WNR2)
     uint32_t sitems[3];              // scale items of matrix m (32 streams each)
     uint32_t witems;                 // weight items of the record (32 streams each, every matrix)
+    uint32_t landed_at;              // the value the upload stream writes into *landed (never 0)
 };
 
 // The launch's work queue. A warp takes the next item (one atomic on the head counter) and runs it:
 //   scale item   32 scale streams [first, first + 32) of matrix `sub`; a record still being uploaded
-//                is waited for (bounded) first: the upload stream sets its `landed` word after its bytes
+//                is waited for (bounded) first: after its bytes the upload stream copies the call's
+//                token (landed_at, larger than any token of an earlier call) into its `landed` word
 //   weight item  32 weight streams of matrix `sub`; it first waits until every scale item of that
 //                matrix of its record is done (the streams' contexts read the decoded scales)
 //   commit item  chunk `first` (kCommitChunk bytes) of region `sub` of the record's commit; it first
@@ -105,11 +107,16 @@ struct Nr3Launch {
     uint32_t nitems, nrecs;
 };
 
-// Threads of a decode CTA (one CTA per SM, persistent).
+// Threads of a decode CTA (one CTA per SM, persistent; 64 registers each, the whole register file).
 constexpr int kDecodeThreads = 1024;
+// Threads of a decode CTA beside record hashes: the register file then keeps room for two hash CTAs
+// (64 threads of at most 72 registers), so a launch is never held back behind hash CTAs that run for
+// the length of a whole record's SHA-256 chain.
+constexpr int kBesideHashThreads = 832;
 
-// One launch on `st`: one CTA per SM of the current device (`sms`).
-cudaError_t launch_nr3(const Nr3Launch &L, int sms, cudaStream_t st);
+// One launch on `st`: one CTA per SM of the current device (`sms`), or, beside_hashes, CTAs of
+// kBesideHashThreads threads on half of the SMs.
+cudaError_t launch_nr3(const Nr3Launch &L, int sms, cudaStream_t st, bool beside_hashes = false);
 cudaError_t prepare_nr3_kernels();   // sets the shared-memory opt-in on the current device
 
 }  // namespace wexb
