@@ -2,7 +2,7 @@
 //
 // No entry point of this library blocks on the GPU without a limit: every wait polls its event or
 // stream (cudaEventQuery / cudaStreamQuery) until the work is done, CUDA reports an error, or the
-// process-wide limit passes (WEXB_WAIT_SECONDS, default 120 s; wexb_set_wait_limit changes it). A call
+// process-wide limit passes (WEXB_WAIT_SECONDS, default 60 s; wexb_set_wait_limit changes it). A call
 // whose wait gives up returns status 1 ("unavailable, decode again"): its GPU work may still be running,
 // so the buffers that work uses are parked (never handed to another call) until it ends.
 #pragma once

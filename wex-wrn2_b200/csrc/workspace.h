@@ -14,8 +14,9 @@ namespace wexb {
 // records of the calls before it. Created once per device and never destroyed (CUDA cannot be called
 // while the process unloads). False on a CUDA failure.
 bool device_streams(int device, cudaStream_t *up, cudaStream_t *st, cudaStream_t *meta = nullptr);
-// The next of the device's 8 hash lanes (a stream and an event to record after its launch): one lane
-// per window of verified calls in flight, so that up to 8 windows hash at once. False on a CUDA failure.
+// The next of the device's 16 hash lanes (a stream and an event to record after its launch): one lane
+// per window of verified calls in flight, so that up to 16 windows (1,024 records) hash at once. False
+// on a CUDA failure.
 bool hash_lane(int device, cudaStream_t *hs, cudaEvent_t *hashed);
 
 // A call's workspace: three events and grown buffers (records, decode scratch, metadata on the device;
