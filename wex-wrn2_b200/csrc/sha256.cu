@@ -133,7 +133,7 @@ __device__ __forceinline__ void produce_block(const uint8_t *data, uint64_t byte
         const uint4 *q = reinterpret_cast<const uint4 *>(data + at);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const uint4 v = __ldg(q + k);
+            const uint4 v = __ldcg(q + k);
             w[4 * k] = bswap(v.x); w[4 * k + 1] = bswap(v.y); w[4 * k + 2] = bswap(v.z); w[4 * k + 3] = bswap(v.w);
         }
         return;
@@ -147,12 +147,38 @@ __device__ __forceinline__ void produce_block(const uint8_t *data, uint64_t byte
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint64_t pos = at + 4 * k + j;
-            const uint32_t byte = pos < bytes ? data[pos] : pos == bytes ? 0x80u : 0u;
+            const uint32_t byte = pos < bytes ? __ldcg(data + pos) : pos == bytes ? 0x80u : 0u;
             v = v << 8 | byte;
         }
         w[k] = v;
     }
     if (last) { w[14] = (uint32_t)(bits >> 32); w[15] = (uint32_t)bits; }
+}
+
+// The producer warp, before it reads block b of its lanes' messages (every lane at the same block):
+// waits (bounded, lane 0 polling with a sleep that doubles up to 8 us) until the upload pass holding
+// that block has landed. `landed`: passes known to be in place. False when the wait gave up.
+__device__ __forceinline__ bool gate_wait(const ShaParts &P, uint32_t b, uint32_t &landed) {
+    if (!P.gate) return true;
+    const uint32_t pass = (uint32_t)((64ull * b) >> P.gate_shift);
+    if (pass < landed) return true;
+    uint32_t ok = 1;
+    if ((threadIdx.x & 31u) == 0) {
+        ok = 0;
+        uint32_t nap = 64;
+        for (uint32_t n = 0; n < (1u << 24); ++n) {
+            uint32_t v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(P.gate + pass) : "memory");
+            if (v >= P.gate_token) { ok = 1; break; }
+            __nanosleep(nap);
+            nap = min(2u * nap, 8192u);
+        }
+        if (!ok) atomicExch(P.gate_fail, 1u);
+    }
+    ok = __shfl_sync(~0u, ok, 0);
+    __syncwarp();
+    if (ok) landed = pass + 1;
+    return ok != 0;
 }
 
 __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaParts P) {
@@ -168,17 +194,21 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaParts 
     if (warp == 1) {   // producer
         // a whole data block's four 16-byte loads are issued one block ahead, before the schedule work of
         // the current block, so their latency is hidden behind it
+        // (coherent L2 loads: with a gate the bytes land while the launch runs)
         uint4 v[4];
         bool ahead = false;
+        uint32_t landed = 0;   // upload passes known to be in place (gated launches)
         auto load = [&](uint32_t b) {
             ahead = 64ull * b + 64 <= m.bytes;
             if (!ahead) return;
             const uint4 *q = reinterpret_cast<const uint4 *>(m.data + 64ull * b);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = __ldg(q + k);
+            for (int k = 0; k < 4; ++k) v[k] = __ldcg(q + k);
         };
+        if (blocks) gate_wait(P, 0, landed);
         if (mine) load(0);
         for (uint32_t b = 0; b < blocks; ++b) {
+            if (b + 1 < blocks) gate_wait(P, b + 1, landed);   // the block loaded one ahead (warp-uniform)
             if (b < mine) {
                 uint32_t w[16];
                 if (ahead) {
@@ -191,7 +221,8 @@ __global__ void __launch_bounds__(2 * kShaLanes) sha256_messages(const ShaParts 
                     produce_block(m.data, m.bytes, b, w);
                 }
                 if (b + 1 < mine) load(b + 1);
-                if (64ull * (b + 8) + 64 <= m.bytes) asm volatile("prefetch.global.L2 [%0];" :: "l"(m.data + 64ull * (b + 8)));
+                if (64ull * (b + 8) + 64 <= m.bytes && (!P.gate || ((64ull * (b + 8)) >> P.gate_shift) < landed))
+                    asm volatile("prefetch.global.L2 [%0];" :: "l"(m.data + 64ull * (b + 8)));
                 uint4 (*out)[kShaLanes] = sched[b & 1];
                 uint32_t wk[4];
 #pragma unroll
@@ -275,7 +306,7 @@ cudaError_t launch_sha256_parts(const ShaParts &P, cudaStream_t st) {
 }
 
 cudaError_t launch_sha256_messages(const ShaMsg *msgs, uint32_t n, cudaStream_t st) {
-    ShaParts P{};
+    ShaParts P{};   // no gate
     P.part[0] = msgs;
     P.end[0] = n;
     P.nparts = 1;

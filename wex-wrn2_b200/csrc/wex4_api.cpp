@@ -369,10 +369,14 @@ struct Job {
 struct Space {   // the container layer's device workspace: one call at a time
     std::mutex mu;
     int device = -1;
-    cudaStream_t st = nullptr, sh[4] = {};     // uploads and decodes; record hashes, groups in turn
-    std::vector<cudaEvent_t> landed;           // one per group of uploaded records, then one per hash stream
+    cudaStream_t st = nullptr, sh[1] = {};     // uploads and decodes; the record hashes
+    std::vector<cudaEvent_t> landed;           // the metadata in place; the hashes done
     DevBuf stage, out, scratch, meta;
     PinBuf hmeta;
+    // upload passes of a hashed check: gate[q] is set to the call's token after pass q (sha256.cuh)
+    DevBuf gates;
+    PinBuf htoken;
+    uint32_t token = 0;
     bool unsettled = false;   // a bounded wait gave up: its work may still use the buffers and streams
     bool events(size_t n) {
         while (landed.size() < n) {
@@ -384,10 +388,14 @@ struct Space {   // the container layer's device workspace: one call at a time
     }
 };
 // Record hashes: one serial chain per record (a single thread hashes a large record at tens of MB/s),
-// so every record's hash must run concurrently with all the others. The records are split into
-// kShaStreams groups in record order; each group's hashes start on its own stream as soon as the
-// group's uploads have landed, beside the later uploads and the decodes.
-constexpr int kShaStreams = 4;
+// so every record's chain must run at once with all the others, and start as early as it can. The
+// records are uploaded in passes of kPassBytes of every record (pass q: bytes [q P, (q + 1) P) of each),
+// each pass followed by its gate word; one hash launch over all records starts before the uploads and
+// each chain waits only for the pass it is about to read. Every chain thus starts within the first pass
+// (about 1 GB of a 10 GB check) instead of after its record's turn in a record-by-record upload, and
+// the copies stay ahead of the chains (a record's share of the link is above a chain's speed).
+constexpr int kShaStreams = 1;
+constexpr uint32_t kPassShift = 21, kPassBytes = 1u << kPassShift;
 Space g_space;
 
 // Host verdicts of a WNR3 record before its decode (c/wex4.h:685-697): entry, model id, owner and
@@ -539,7 +547,8 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
                  o_sha = take(n * sizeof(ShaMsg)), o_exp = take(n * 32), o_zero = take(n * sizeof(ZeroJob)),
                  o_err = take(n * 4), o_ver = take(n * 4), o_offs = take(noffs * 4),
                  o_w4rec = take(k4 * sizeof(W4Rec)), o_w4job = take(w4jobs.size() * sizeof(W4Job)),
-                 o_bprec = take(kb * sizeof(Wbp1Record)), o_bptask = take(bptasks.size() * sizeof(Wbp1Task));
+                 o_bprec = take(kb * sizeof(Wbp1Record)), o_bptask = take(bptasks.size() * sizeof(Wbp1Task)),
+                 o_gfail = take(4);
     if (!S.stage.grow(stage_bytes) || !S.out.grow(out_bytes) || !S.scratch.grow(scr_bytes) || !S.meta.grow(m) ||
         !S.hmeta.grow(m)) return false;
     uint8_t *hm = S.hmeta.p, *dm = S.meta.p;
@@ -602,30 +611,50 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     if (!bptasks.empty()) std::memcpy(hm + o_bptask, bptasks.data(), bptasks.size() * sizeof(Wbp1Task));
     if (k4) std::memcpy(hm + o_w4rec, w4info.data(), k4 * sizeof(W4Rec));
     if (!w4jobs.empty()) std::memcpy(hm + o_w4job, w4jobs.data(), w4jobs.size() * sizeof(W4Job));
-    cudaStream_t st = S.st;
-    const size_t groups = kShaStreams, per_group = (n + groups - 1) / groups;
-    bool ok = S.events(groups + kShaStreams) && cudaMemcpyAsync(dm, hm, m, cudaMemcpyHostToDevice, st) == cudaSuccess;
-    // uploads in record order; each group's hashes start on sh once its records have landed
-    uint32_t sha_at = 0;
-    for (size_t g = 0; ok && g < groups; ++g) {
-        const size_t i1 = std::min(n, (g + 1) * per_group);
-        uint32_t msgs = 0;
-        for (size_t i = g * per_group; ok && i < i1; ++i) {
-            if (jobs[i].pre != OK) continue;
-            ok = cudaMemcpyAsync(S.stage.p + at[i], jobs[i].stored, jobs[i].rec.stored, cudaMemcpyHostToDevice, st) == cudaSuccess;
-            msgs += jobs[i].expect_sha != nullptr;
+    cudaStream_t st = S.st, sh = S.sh[0];
+    bool ok = S.events(2) && cudaMemcpyAsync(dm, hm, m, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    if (nsha) {   // passes of every record, gated; the hash launch first (it waits for each pass)
+        size_t passes = 0;
+        for (size_t i = 0; i < n; ++i)
+            if (jobs[i].pre == OK) passes = std::max<size_t>(passes, (jobs[i].rec.stored + kPassBytes - 1) / kPassBytes);
+        const size_t gate_bytes = 4 * (passes + 1);   // the last word covers the padding blocks past the data
+        if (ok && (gate_bytes > S.gates.cap || S.token == 0xffffffffu)) {   // new words: zero them first
+            ok = S.gates.grow(gate_bytes) && S.htoken.grow(16) &&
+                 cudaMemsetAsync(S.gates.p, 0, S.gates.cap, st) == cudaSuccess && wait_stream(st) == Waited::Done;
+            S.token = 0;
+            if (!ok) S.token = 0xffffffffu;
         }
-        cudaStream_t sh = S.sh[g];
-        if (ok && msgs)
-            ok = cudaEventRecord(S.landed[g], st) == cudaSuccess && cudaStreamWaitEvent(sh, S.landed[g], 0) == cudaSuccess &&
-                 launch_sha256_messages(reinterpret_cast<const ShaMsg *>(dm + o_sha) + sha_at, msgs, sh) == cudaSuccess;
-        sha_at += msgs;
+        const uint32_t token = ++S.token;
+        if (ok) *reinterpret_cast<uint32_t *>(S.htoken.p) = token;   // the previous check's copies have ended
+        uint32_t *gates = reinterpret_cast<uint32_t *>(S.gates.p);
+        ShaParts P{};
+        P.part[0] = reinterpret_cast<const ShaMsg *>(dm + o_sha);
+        P.end[0] = nsha;
+        P.nparts = 1;
+        P.gate = gates; P.gate_token = token; P.gate_shift = kPassShift;
+        P.gate_fail = reinterpret_cast<uint32_t *>(dm + o_gfail);
+        ok = ok && cudaEventRecord(S.landed[0], st) == cudaSuccess && cudaStreamWaitEvent(sh, S.landed[0], 0) == cudaSuccess &&
+             launch_sha256_parts(P, sh) == cudaSuccess;
+        for (size_t q = 0; ok && q < passes; ++q) {
+            const size_t from = q * kPassBytes;
+            for (size_t i = 0; ok && i < n; ++i)
+                if (jobs[i].pre == OK && jobs[i].rec.stored > from)
+                    ok = cudaMemcpyAsync(S.stage.p + at[i] + from, jobs[i].stored + from,
+                                         std::min<size_t>(kPassBytes, jobs[i].rec.stored - from), cudaMemcpyHostToDevice,
+                                         st) == cudaSuccess;
+            ok = ok && cudaMemcpyAsync(gates + q, S.htoken.p, 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+        }
+        ok = ok && cudaMemcpyAsync(gates + passes, S.htoken.p, 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    } else {
+        for (size_t i = 0; ok && i < n; ++i)
+            if (jobs[i].pre == OK)
+                ok = cudaMemcpyAsync(S.stage.p + at[i], jobs[i].stored, jobs[i].rec.stored, cudaMemcpyHostToDevice, st) == cudaSuccess;
     }
     for (uint32_t z = 0; ok && z < nzero; z += 65535)
         ok = launch_zero_check(reinterpret_cast<const ZeroJob *>(dm + o_zero) + z, std::min<uint32_t>(65535, nzero - z), st) == cudaSuccess;
     const Nr3Record *drecs = reinterpret_cast<const Nr3Record *>(dm + o_recs);
     ok = ok && launches.launch(drecs, reinterpret_cast<const Nr3Item *>(dm + o_items), reinterpret_cast<uint32_t *>(dm + o_counters),
-                               sms, st);
+                               sms, st, nsha != 0);   // beside the hash launch's CTAs
     ok = ok && launch_wbp1_streams(reinterpret_cast<const Wbp1Record *>(dm + o_bprec),
                                    reinterpret_cast<const Wbp1Task *>(dm + o_bptask), (uint32_t)bptasks.size(), st) == cudaSuccess &&
          launch_wbp1_join(reinterpret_cast<const Wbp1Record *>(dm + o_bprec), (uint32_t)kb, st) == cudaSuccess;
@@ -633,12 +662,12 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
         ok = launch_wnr4(*w4tabs[g], reinterpret_cast<const W4Job *>(dm + o_w4job) + w4runs[g].first,
                          (uint32_t)w4runs[g].second, reinterpret_cast<const W4Rec *>(dm + o_w4rec), st) == cudaSuccess;
     // the hashes rejoin the decode stream before the verdicts come back
-    for (int h = 0; ok && h < kShaStreams; ++h)
-        ok = cudaEventRecord(S.landed[groups + h], S.sh[h]) == cudaSuccess &&
-             cudaStreamWaitEvent(st, S.landed[groups + h], 0) == cudaSuccess;
+    if (nsha)
+        ok = ok && cudaEventRecord(S.landed[1], sh) == cudaSuccess && cudaStreamWaitEvent(st, S.landed[1], 0) == cudaSuccess;
     ok = ok &&
          cudaMemcpyAsync(hm + o_err, dm + o_err, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-         cudaMemcpyAsync(hm + o_ver, dm + o_ver, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+         cudaMemcpyAsync(hm + o_ver, dm + o_ver, 4 * n, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+         cudaMemcpyAsync(hm + o_gfail, dm + o_gfail, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     // bounded waits, also after a failed step: whatever was queued must end before the space is reused
     Waited waited = wait_stream(st);
     for (cudaStream_t h : S.sh) {
@@ -647,6 +676,7 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
     }
     if (waited == Waited::TimedOut) S.unsettled = true;
     if (!ok || waited != Waited::Done) { (void)cudaGetLastError(); return false; }
+    if (*reinterpret_cast<const uint32_t *>(hm + o_gfail)) return false;   // a chain gave up waiting for its bytes
     const uint32_t *herr = reinterpret_cast<const uint32_t *>(hm + o_err), *hver = reinterpret_cast<const uint32_t *>(hm + o_ver);
     for (size_t i = 0; i < n; ++i) {
         Job &j = jobs[i];
