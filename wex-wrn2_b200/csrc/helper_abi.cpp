@@ -186,8 +186,8 @@ void window_add(Call &c) {
 
 // Before a wait: a verified call still in its window is queued now.
 void ensure_launched(Call &c) {
-    if (!c.w || c.launched) return;
-    std::lock_guard<std::mutex> lock(g_window_mu);
+    if (!c.w) return;
+    std::lock_guard<std::mutex> lock(g_window_mu);   // `launched` is written under this lock
     if (!c.launched) window_flush(c.device);
 }
 
