@@ -171,23 +171,40 @@ def gpu_encoded_pool(cfg, owners, threads, blob, device):
                     e.expected_sha = hashlib.sha256(e.source).digest()
                 e.entry = synth.entry_with(e.entry, total=len(e.record), codec=e.codec)
                 e.source = e.coded = e.expected = None
+            pin_group(ex)
             out.extend(ex)
     return out
 
 
-def pinned_records(experts):
-    """All records in one page-locked host buffer; returns (buffer, views)."""
+PINNED = []   # page-locked record buffers, kept for the life of the process
+
+
+def pin_group(experts):
+    """Moves the experts' records into one new page-locked buffer (each e.record becomes a view of it), so
+    that a rank never holds a record twice in host memory."""
     import wexcuda
-    total = sum(len(e.record) for e in experts)
-    buf = np.empty(total, np.uint8)
-    views, at = [], 0
+    buf = np.empty(sum(len(e.record) for e in experts), np.uint8)
+    at = 0
     for e in experts:
         n = len(e.record)
         buf[at:at + n] = np.frombuffer(e.record, np.uint8)
-        views.append(buf[at:at + n])
+        e.record = buf[at:at + n]
         at += n
     assert wexcuda.host_register(buf) == 0
-    return buf, views
+    PINNED.append(buf)
+
+
+def pinned_records(experts):
+    """Every record in page-locked host memory (moved there unless it already is); returns (None, views)."""
+    loose = [e for e in experts if not isinstance(e.record, np.ndarray)]
+    for at in range(0, len(loose), 64):
+        pin_group(loose[at:at + 64])
+    return None, [e.record for e in experts]
+
+
+def rec_arg(record):
+    """A record (bytes or a page-locked view) as a ctypes pointer argument."""
+    return record.ctypes.data if isinstance(record, np.ndarray) else record
 
 
 # ---- clocks -------------------------------------------------------------------------------------
@@ -331,7 +348,7 @@ def reference_decode_rate(experts, blob, cores, min_seconds=10.0, max_records=No
 
     def one(i):
         e = sample[i % len(sample)]
-        st = L.wex_nr3_decode(blob, e.entry, e.record, e.layer, e.index, outs[i % cores])
+        st = L.wex_nr3_decode(blob, e.entry, rec_arg(e.record), e.layer, e.index, outs[i % cores])
         if st != 0:
             raise RuntimeError('reference decoder refused a record')
         return e.raw
@@ -1713,6 +1730,8 @@ def run_gpu(args, cfg):
         else:
             line['gpu_reference'] = g
     res.close()
+    import resource
+    log(f'[rank {rank}] peak host memory {resource.getrusage(resource.RUSAGE_SELF).ru_maxrss / 1e6:.1f} GB')
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
