@@ -143,7 +143,7 @@ def gpu_encoded_pool(cfg, owners, threads, blob, device):
     import synth
     import wexcuda
     sig = layer_sigmas(cfg)
-    group = max(8, 2 * threads)
+    group = max(8, threads)
 
     def make(o):
         layer, idx = o
@@ -151,6 +151,7 @@ def gpu_encoded_pool(cfg, owners, threads, blob, device):
                          cfg['cz'], 0, cfg['neg_zero'])
         e.raw = len(e.source)
         e.expected_sha = hashlib.sha256(e.expected).digest()
+        e.expected = None   # only its digest is kept (host memory: a rank holds its records and little else)
         return e
     out = []
     with ThreadPoolExecutor(threads) as pool, ThreadPoolExecutor(1) as ahead:
