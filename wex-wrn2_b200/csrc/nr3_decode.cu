@@ -126,18 +126,21 @@ __device__ __noinline__ uint32_t weight_stream(const Nr3Record &R, uint32_t m, u
         const int d = (int)scale - anchor;
         const uint32_t srel = (uint32_t)(min(max(d, -3), 3) + 3) * kPairs;
         const uint32_t l1 = level1 + 8u * srel, l2 = level2 + 32u * srel;
-        uint32_t idx = kPairs - 1u, top = 0, w[4] = {0, 0, 0, 0};   // the block-start context
-        // one symbol: its quartile and rank from the two 8-byte rows of context idx, the state update,
-        // then the next context (pair index top (top + 1) / 2 + mag)
+        // row1: the shared address of the context's level-1 row (8 bytes a pair index); its level-2 rows
+        // (32 bytes a pair index) sit at 4 row1 + to2. The block starts at pair index 36.
+        const uint32_t to2 = l2 - 4u * l1;   // (wraps mod 2^32; 4 row1 + to2 does not)
+        uint32_t row1 = l1 + 8u * (kPairs - 1u), top = 0, w[4] = {0, 0, 0, 0};
+        // one symbol: its quartile and rank from the two 8-byte rows of the context, the state update,
+        // then the next context (pair index top (top + 1) / 2 + mag: 4 top (top + 1) + 8 mag bytes)
         auto step = [&](uint32_t k) {
-            const uint2 c = lds_v2(l1 + 8u * idx);
+            const uint2 c = lds_v2(row1);
             const uint32_t slot = x & (kTotal - 1u), gs = slot * 0x10001u + 0x80008000u;
             // q = [cdf[4] <= slot] + [cdf[8] <= slot] + [cdf[12] <= slot]
             uint32_t d0, d1;
             asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d0) : "r"(c.x), "r"(0xffffffffu), "r"(gs));
             asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d1) : "r"(c.y), "r"(0xffffffffu), "r"(gs));
             const uint32_t q = __popc((d0 & 0x80008000u) | ((d1 >> 1) & 0x4000u));
-            const uint2 row = lds_v2(l2 + 32u * idx + 8u * q);   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
+            const uint2 row = lds_v2(4u * row1 + to2 + 8u * q);   // cdf[4q] | cdf[4q+1] << 16, cdf[4q+2] | cdf[4q+3] << 16
             // r = [cdf[4q+1] <= slot] + [cdf[4q+2] <= slot] + [cdf[4q+3] <= slot]
             uint32_t e0, e1;
             asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(e0) : "r"(row.x), "r"(0xffffffffu), "r"(gs));
@@ -154,7 +157,7 @@ __device__ __noinline__ uint32_t weight_stream(const Nr3Record &R, uint32_t m, u
             w[k / 8u] += sym << (4u * (k % 8u));
             const uint32_t mag = sym & 7u;
             top = max(top, mag);
-            idx = ((top * top + top) >> 1) + mag;
+            row1 = l1 + 4u * (top * top + top) + 8u * mag;
         };
 #pragma unroll
         for (uint32_t k = 0; k < 32; k += 2) {

@@ -108,14 +108,22 @@ __device__ __forceinline__ uint32_t lds_payload(uint32_t a) {
     return v;
 }
 
-// One 4-byte asynchronous copy global -> shared when `go`, else nothing (the instruction is predicated,
-// so the lanes of a warp that copy and those that do not stay converged).
-__device__ __forceinline__ void cp_async4(uint32_t dst, const uint32_t *src, bool go) {
+// Four 4-byte asynchronous copies global -> shared, src[k] to dst + k * stride, when `go`, and a fifth of
+// src[0] to `mirror` when `go` and `also`. The copies are predicated (one predicate for the four), so the
+// lanes of a warp that copy and those that do not stay converged.
+template <uint32_t kStrideBytes>
+__device__ __forceinline__ void cp_async4x4(uint32_t dst, const uint32_t *src, uint32_t mirror, bool go, bool also) {
     asm volatile("{\n"
-                 "  .reg .pred do_copy;\n"
-                 "  setp.eq.u32 do_copy, %2, 1;\n"
-                 "  @do_copy cp.async.ca.shared.global [%0], [%1], 4;\n"
-                 "}\n" :: "r"(dst), "l"(src), "r"((uint32_t)go) : "memory");
+                 "  .reg .pred p, q;\n"
+                 "  setp.ne.u32 p, %3, 0;\n"
+                 "  setp.ne.and.u32 q, %4, 0, p;\n"
+                 "  @p cp.async.ca.shared.global [%0], [%1], 4;\n"
+                 "  @p cp.async.ca.shared.global [%0+%5], [%1+4], 4;\n"
+                 "  @p cp.async.ca.shared.global [%0+%6], [%1+8], 4;\n"
+                 "  @p cp.async.ca.shared.global [%0+%7], [%1+12], 4;\n"
+                 "  @q cp.async.ca.shared.global [%2], [%1], 4;\n"
+                 "}\n" :: "r"(dst), "l"(src), "r"(mirror), "r"((uint32_t)go), "r"((uint32_t)also),
+                 "n"(kStrideBytes), "n"(2 * kStrideBytes), "n"(3 * kStrideBytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N) : "memory"); }
@@ -132,11 +140,8 @@ struct PayloadWindow {
     // The next group when `go` (every lane runs the same predicated instructions: no divergence).
     __device__ __forceinline__ void request_group(bool go) {
         const uint32_t s = ask % kWinWords;
-        const uint32_t d = slots + s * kStride;
-        const uint32_t *g = words + ask;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) cp_async4(d + k * kStride, g + k, go);
-        cp_async4(slots + kWinWords * kStride, g, go && s == 0);   // the mirror of slot 0
+        // the group's four words, and the mirror of slot 0 when the group starts there
+        cp_async4x4<kStride>(slots + s * kStride, words + ask, slots + kWinWords * kStride, go, s == 0);
         ask += go ? 4u : 0u;
     }
     // Opens the stream of record bytes [begin, end) (length >= 4, checked on the host) and returns its
