@@ -1,4 +1,4 @@
-"""The weight kernel's symbol lookup (nr3_weights in wnr3_kernels.cu, over the two-level rows that
+"""The weight items' symbol lookup (weight_stream in nr3_decode.cu, over the two-level rows that
 build_image in nr3_host.cpp makes from a WNM2 model), emulated on the CPU with numpy's 32-bit wrap-around
 arithmetic for every slot of every reachable context of a trained model: the quartile from the level-1
 row, the rank from the level-2 row, and start and end taken by the byte permute and the funnel shift,

@@ -1,13 +1,15 @@
 // The CUDA helper C ABI (include/wex_cuda_helper.h) and the resident-record additions
 // (include/wexb200.h), over the sm_100a WNR2/WNR3 kernels.
 //
-// One call = a pooled workspace (grown buffers, two events) on the device's shared streams: all
-// launch metadata of the call (record descriptors, CTA tasks, commit jobs, error words, stream
-// offsets) goes up in one copy and every record after it, on the upload stream in call order; the
-// call's kernels (one grid each over all its records) and the read-back of its error words follow
-// on the call's kernel stream. Queued calls therefore overlap one call's decode with the next
-// call's uploads. A record's destinations are written by the error-gated commit kernel (device
-// destinations), or copied back after the kernels (host destinations).
+// One call = a pooled workspace (grown buffers, three events, upload flags) on the device's shared
+// streams: each record is parsed and its upload queued at once (upload stream, call order, a flag word
+// after each record); the launch metadata (record descriptors, work queue, commit jobs, error words,
+// stream offsets) follows in one copy on the metadata stream; one persistent decode launch per model
+// and the read-back of the error words run on the call's kernel stream, the records decoding as their
+// flags land. Queued calls therefore overlap one call's decode with its own later uploads and the next
+// call's. A record's destinations are written by the launch's error-gated commit items (device
+// destinations), or copied back after it (host destinations). Verified calls add a hash window
+// (window_flush below).
 #include <cuda_runtime.h>
 
 #include <algorithm>

@@ -3,7 +3,8 @@
 // Host: the header page and the index are validated with the reference's rules, in the reference's
 // order, so a refused file gets the same WEX4_E_* class (c/wex4.h:185-437; each check below names
 // its rule). GPU: every record's stored bytes go up once; record SHA-256 checks, RAW padding checks,
-// WNR3 decodes (the kernels of wnr3_kernels.cu) and the content digest run there.
+// WNR3 decodes (the persistent launch of nr3_decode.cu), WBP1 and WNR4 decodes and the content digest
+// run there.
 #include <cuda_runtime.h>
 #include <sys/mman.h>
 #include <unistd.h>
