@@ -636,6 +636,7 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
         P.gate_fail = reinterpret_cast<uint32_t *>(dm + o_gfail);
         ok = ok && cudaEventRecord(S.landed[0], st) == cudaSuccess && cudaStreamWaitEvent(sh, S.landed[0], 0) == cudaSuccess &&
              launch_sha256_parts(P, sh) == cudaSuccess;
+        const bool hashing = ok;   // from here on, every gate word must be set, whatever fails
         for (size_t q = 0; ok && q < passes; ++q) {
             const size_t from = q * kPassBytes;
             for (size_t i = 0; ok && i < n; ++i)
@@ -646,6 +647,12 @@ bool run_jobs(std::vector<Job> &jobs, int device) {
             ok = ok && cudaMemcpyAsync(gates + q, S.htoken.p, 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
         }
         ok = ok && cudaMemcpyAsync(gates + passes, S.htoken.p, 4, cudaMemcpyHostToDevice, st) == cudaSuccess;
+        if (hashing && !ok) {   // an upload failed: open every gate, so the hash launch ends at once (its
+            (void)cudaGetLastError();   // verdicts are then discarded with the call) instead of at its wait limit
+            for (size_t q = 0; q <= passes; ++q)
+                (void)cudaMemcpyAsync(gates + q, S.htoken.p, 4, cudaMemcpyHostToDevice, st);
+            (void)cudaGetLastError();
+        }
     } else {
         for (size_t i = 0; ok && i < n; ++i)
             if (jobs[i].pre == OK)
