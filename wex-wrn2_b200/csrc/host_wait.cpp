@@ -28,8 +28,10 @@ inline void cpu_relax() {
 #endif
 }
 
-// Spins on `query` for the first 2 ms (a decode call of a few records finishes in well under that, so
-// the caller sees no sleep latency), then sleeps 20 us between polls until the deadline.
+// Polls `query` until the deadline: spinning for the first 100 us, then yielding the core between
+// polls up to 5 ms (no sleep latency while the core is free, and the core is shared while other
+// threads, such as the other ranks' submitting threads on a busy host, want it), then sleeping 20 us
+// between polls.
 template <class Query>
 Waited poll(Query query, double seconds) {
     using clock = std::chrono::steady_clock;
@@ -38,10 +40,11 @@ Waited poll(Query query, double seconds) {
         const cudaError_t e = query();
         if (e == cudaSuccess) return Waited::Done;
         if (e != cudaErrorNotReady) { (void)cudaGetLastError(); return Waited::Failed; }
-        if ((i & 31u) != 31u) { cpu_relax(); continue; }
+        if ((i & 7u) != 7u) { cpu_relax(); continue; }
         const double elapsed = std::chrono::duration<double>(clock::now() - start).count();
         if (elapsed > seconds) return Waited::TimedOut;
-        if (elapsed > 2e-3) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (elapsed > 5e-3) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        else if (elapsed > 1e-4) std::this_thread::yield();
     }
 }
 
