@@ -61,8 +61,9 @@ CONFIGS = {
     'mid': dict(hidden=2048, ffn=768, layers=48, experts=128, batch=8, cz=False, sigma=(0.01, 0.04), neg_zero=0.0),
     # the largest single-GPU workload (the default): a token step routes 464 experts of 23.4 MB; the routing
     # trace has `trace_steps` distinct token steps, cycled, so that the distinct records fit in host memory
+    # with eight ranks on one host (9.9 GB of page-locked records a rank; the records of a step are 80 x L2)
     'large': dict(hidden=7168, ffn=2048, layers=58, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
-                  lean=True, trace_steps=2),
+                  lean=True, trace_steps=1),
     # whole-box streaming: 1536 large experts, each rank decodes all of its shard every step
     'box': dict(hidden=7168, ffn=2048, layers=8, experts=192, batch=8, cz=True, sigma=(0.01, 0.04), neg_zero=0.03,
                 lean=True, all_experts=True, verify=True),
@@ -1355,7 +1356,8 @@ def config_desc(args, cfg, records):
                 'l2': 'inputs larger than L2 (126 MB) between steps'}
     return {'workload': f'{args.config}: routed decode of WNR3 MXFP4 experts, hidden {cfg["hidden"]}, expert FFN '
                         f'{cfg["ffn"]}, {args.layers or cfg["layers"]} layers x {cfg["experts"]} experts, top-'
-                        f'{cfg["batch"]} Zipf(1.1) per layer per step' + (', canonical zero' if cfg['cz'] else ''),
+                        f'{cfg["batch"]} Zipf(1.1) per layer per step' + (', canonical zero' if cfg['cz'] else '') +
+                        (f', {cfg["trace_steps"]} distinct routing step(s) cycled' if cfg.get('trace_steps') else ''),
             'records_per_step_per_gpu': records,
             'chunks': '2048:512', 'placement': 'expert id mod world size',
             'l2': 'inputs larger than L2 (126 MB) between steps'}
