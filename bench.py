@@ -7,9 +7,9 @@ scale per 32), 58 layers x 192 experts, per-layer sigma drawn from U(0.01, 0.04)
 nibbles written as -0, encoded as WNR3 records in canonical-zero mode (value-exact; chunks 2048:512)
 under one WNM2 model. A step is one token of routed decode: for each of the 58 layers the top-8 of a
 Zipf(1.1) popularity over that layer's experts (seeded), i.e. 464 expert records of 23.4 MB, 10.9 GB of
-decoded slabs. The routing trace has two distinct token steps, cycled (about 800 distinct records per
-rank, so that they fit in pinned host memory). Inputs are seeded synthetic data (no dataset is involved)
-and larger than L2 between steps.
+decoded slabs. The routing trace has one token step, drawn once and used by every step (464 distinct
+records, 9.9 GB of page-locked host memory a rank, so that eight ranks fit one host). Inputs are seeded
+synthetic data (no dataset is involved) and larger than L2 between steps (the step's records are 80 x L2).
 
   value  records resident in HBM (wexb_resident_*), the step's records decoded by one persistent launch
          (scale, weight and commit work drained from one queue; two decodes queued, so the next step is
