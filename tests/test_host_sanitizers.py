@@ -72,3 +72,27 @@ def test_host_parsers_under_sanitizers(tmp_path):
     by_codec = {k: int(v) for k, v in by_codec.items()}
     assert runs > 30 * len(files)
     assert by_codec['5'] > 0 and by_codec['6'] > 0 and ('mixed.wex4' not in written or by_codec['8'] > 0), r.stdout
+
+
+def test_decode_queue_waits_only_for_earlier_items(tmp_path):
+    """The decode launch's work queue (queue_fill) on 400 seeded random launches: every weight item after
+    all scale items of its matrix, every commit item after all weight items of its record, every stream
+    and commit chunk exactly once, and the descriptors' item counts equal to the queue's (the kernel's
+    items wait only for earlier items, so the queue always drains). Built with the sanitizers as above."""
+    gxx = shutil.which('g++')
+    lib = os.path.join(CUDA, 'lib64')
+    if not gxx or not os.path.exists(os.path.join(CUDA, 'include', 'cuda_runtime.h')) or \
+            not glob.glob(os.path.join(lib, 'libcudart.so*')):
+        pytest.skip('g++ or the CUDA runtime is not installed')
+    csrc = os.path.join(ROOT, 'wex-wrn2_b200', 'csrc')
+    exe = str(tmp_path / 'queue_order')
+    cmd = [gxx, '-std=c++17', '-O1', '-g', '-fsanitize=address,undefined', '-fno-sanitize-recover=all',
+           '-x', 'c++', '-I', os.path.join(CUDA, 'include'), '-I', os.path.join(ROOT, 'include'), '-I', csrc,
+           os.path.join(ROOT, 'tests', 'sanitize', 'queue_order.cpp'), os.path.join(ROOT, 'tests', 'sanitize', 'stubs.cpp'),
+           os.path.join(csrc, 'nr3_host.cpp'), os.path.join(csrc, 'host_wait.cpp'),
+           '-o', exe, '-L', lib, '-lcudart', '-lpthread']
+    subprocess.run(cmd, check=True, timeout=600)
+    env = dict(os.environ, ASAN_OPTIONS='detect_leaks=0', LD_LIBRARY_PATH=lib + ':' + os.environ.get('LD_LIBRARY_PATH', ''))
+    r = subprocess.run([exe, '5', '400'], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-4000:])
+    assert int(r.stdout.split()[0]) > 10000
