@@ -1668,6 +1668,12 @@ def run_gpu(args, cfg):
                              'frac_of_one_copy': round(h2d_per_step / e2e_step_s / 1e9 / h2d_together, 4),
                              'peak_one_gpu': round(h2d_gbs, 2),
                              'hbm_frac': round(hbm_bytes / e2e_step_s / 1e9 / hbm_peak, 4)}},
+        # the end-to-end path per GPU, for comparing runs at different N: each GPU's share of the host link
+        # (every rank copying at once) bounds it, not a collective
+        'e2e_scaling': {'gpus': world, 'decoded_gbs_per_gpu': round(e2e / world, 3),
+                        'stored_gbs_per_gpu': round(h2d_per_step / e2e_step_s / 1e9, 2),
+                        'h2d_gbs_per_gpu_all_copying': round(h2d_calls, 2),
+                        'frac_of_h2d_all_copying': round(h2d_per_step / e2e_step_s / 1e9 / h2d_calls, 4)},
         'value_roofline': {'bound': 'hbm', 'achieved': round(hbm_bytes / step_s / 1e9, 2), 'peak': hbm_peak, 'unit': 'GB/s',
                            'frac': round(hbm_bytes / step_s / 1e9 / hbm_peak, 4),
                            'bytes': 'records read + slabs written by the decoder and by the commit copy'},
