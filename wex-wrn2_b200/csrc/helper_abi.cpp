@@ -242,15 +242,27 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
         return false;
     }
     c.w = w;
-    // plan and upload record by record (call order); a record's flag word follows its bytes
+    // plan and upload record by record (call order). A flag word follows the records at least every
+    // kFlagBytes (and after the last): a 4-byte copy costs the copy engine about as much as several
+    // microseconds of record bytes, so small records share a flag (a record's flag is the first one after
+    // its bytes)
+    constexpr size_t kFlagBytes = 8u << 20;
     uint32_t *dflags = reinterpret_cast<uint32_t *>(w->dflags.p);
     const uint32_t *htoken = reinterpret_cast<const uint32_t *>(w->htoken.p);
     std::vector<const uint8_t *> tabs_of((size_t)n, nullptr);
     std::vector<size_t> rec_off((size_t)n, 0);
     std::vector<uint32_t> flag_of((size_t)n, 0);
     bool ok = true;
-    size_t rec_bytes = 0;
-    uint32_t copied = 0;
+    size_t rec_bytes = 0, since_flag = 0;
+    uint32_t flags = 0;
+    std::vector<int> unflagged;
+    auto flag_now = [&]() {
+        for (int r : unflagged) flag_of[(size_t)r] = flags;
+        ok = ok && cudaMemcpyAsync(dflags + flags, htoken, 4, cudaMemcpyHostToDevice, up) == cudaSuccess;
+        ++flags;
+        unflagged.clear();
+        since_flag = 0;
+    };
     for (int i : cand) {
         Plan &p = c.plans[(size_t)i];
         if (plan_record(entries[i], records[i], &p)) continue;
@@ -262,13 +274,15 @@ bool submit(Call &c, int n, const WexEntry *const *entries, const unsigned char 
         c.pend.push_back(i);
         rec_off[(size_t)i] = rec_bytes;
         rec_bytes += align_up(p.total + kRecordSlack, 256);
-        flag_of[(size_t)i] = copied++;
-        ok = ok && cudaMemcpyAsync(w->drec.p + rec_off[(size_t)i], records[i], p.total, cudaMemcpyHostToDevice, up) == cudaSuccess &&
-             cudaMemcpyAsync(dflags + flag_of[(size_t)i], htoken, 4, cudaMemcpyHostToDevice, up) == cudaSuccess;
+        ok = ok && cudaMemcpyAsync(w->drec.p + rec_off[(size_t)i], records[i], p.total, cudaMemcpyHostToDevice, up) == cudaSuccess;
+        unflagged.push_back(i);
+        since_flag += p.total;
+        if (since_flag >= kFlagBytes) flag_now();
     }
+    if (!unflagged.empty()) flag_now();
     if (cudaEventRecord(w->uploads_done, up) != cudaSuccess) {
         (void)cudaGetLastError();
-        if (copied && wait_stream(up) == Waited::TimedOut) c.unsettled = true;
+        if (!c.pend.empty() && wait_stream(up) == Waited::TimedOut) c.unsettled = true;
         ok = false;
     }
     if (c.pend.empty()) {   // nothing was queued
