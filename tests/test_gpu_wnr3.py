@@ -416,6 +416,37 @@ def test_verified_windows(torch_cuda, tiny):
                 assert _untouched(ts, j), (c, j)
 
 
+def test_upload_flags_shared_by_small_records(torch_cuda):
+    """A call's records share an upload flag per 8 MiB: a call of 7 mid-shape records (2.3 MB each), one
+    damaged and one refused on the host in the middle, has two flags each covering several records.
+    Queued and synchronous, in turn and twice over (the flags' tokens advance per call of a workspace):
+    every clean record bit-exact, the damaged and the refused ones -1 with their destinations
+    untouched."""
+    blob, mids = synth.make_experts(2048, 768, [(0, i) for i in range(6)], seed=77, sigma=0.02, train_every=1)
+    assert wexcuda.register_model(blob) == 0
+    damaged = bytearray(mids[3].record)
+    damaged[9000] ^= 16
+    bad_entry = bytearray(mids[4].entry)
+    bad_entry[24] ^= 1   # a scale shape that does not match its record
+    entries = [e.entry for e in mids] + [mids[0].entry]
+    records = [e.record for e in mids] + [mids[5].record]
+    records[3] = bytes(damaged)
+    entries[4] = bytes(bad_entry)
+    want = [0, 0, 0, -1, -1, 0, 0]   # the last: record 5 again, under record 0's entry (the same shape)
+    for rep in range(2):
+        for queued in (True, False):
+            ts, sp, wp = _dst(torch_cuda, mids[0].entry, len(entries))
+            if queued:
+                bad, st = wexcuda.submit_batch_to_device(entries, records, 0, sp, wp).wait()
+            else:
+                bad, st = wexcuda.decode_batch_to_device(entries, records, 0, sp, wp)
+            assert st == want and bad == 2, (rep, queued, st)
+            for j, src in ((0, 0), (1, 1), (2, 2), (5, 5), (6, 5)):
+                assert _slab(ts, j) == mids[src].expected, (rep, queued, j)
+            for j in (3, 4):
+                assert _untouched(ts, j), (rep, queued, j)
+
+
 def test_queued_batches(torch_cuda, tiny):
     """wexb_batch_submit / wexb_batch_wait: several batches in flight, one with a damaged and an
     unavailable record; each wait gives the statuses of the synchronous call; tickets are single-use."""
