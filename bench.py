@@ -1500,7 +1500,7 @@ def run_gpu(args, cfg):
     B = cfg['batch']
     entry_store = [np.frombuffer(bytes(e.entry), np.uint8).copy() for e in experts]
     verify = bool(cfg.get('verify'))
-    depth = args.depth or (112 if verify else 3)
+    depth = args.depth or (160 if verify else 3)
     rec_sha = None
     if verify:   # each record's SHA-256, as a WEX4 index keeps it (c/wex4.h:673-677), computed once on the host
         with ThreadPoolExecutor(threads) as pool:
@@ -1762,7 +1762,7 @@ def main():
     ap.add_argument('--no-gpu-reference', action='store_true',
                     help='skip the reference CUDA helper timed beside this library (1 GPU)')
     ap.add_argument('--depth', type=int, default=0,
-                    help='e2e: batch calls kept in flight (default 3; 112 for a verified config)')
+                    help='e2e: batch calls kept in flight (default 3; 160 for a verified config)')
     args = ap.parse_args()
     assert args.warmup >= 1
     cfg = CONFIGS[args.config]

@@ -30,7 +30,7 @@ int wexb_batch_submit(int n, const WexEntry *const *entries, const unsigned char
  * (the digest a WEX4 index keeps for the record, c/wex4.h:673-677) before its decode may write the
  * destination: a record whose bytes hash to anything else gets status -1 (error bit 32) and its
  * destination stays untouched. Verified calls of a device gather in windows of up to 64 records (or 16
- * calls): a window's hashes are one launch on one of the device's 16 hash streams once its records have
+ * calls): a window's hashes are one launch on one of the device's 24 hash streams once its records have
  * landed, and its calls' decodes follow them. A window is queued when it is full or when one of its calls
  * is waited for, so a call may start only at the wait. One SHA-256 chain per record: keep many calls in
  * flight (tens) so that hundreds of chains run at once, and run the process with

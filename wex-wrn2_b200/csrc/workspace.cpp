@@ -22,7 +22,7 @@ struct Queues {
 std::mutex g_queues_mu;
 Queues g_queues[kMaxDevices];
 
-constexpr int kHashLanes = 16;
+constexpr int kHashLanes = 24;
 struct HashLanes {
     cudaStream_t s[kHashLanes] = {};
     cudaEvent_t e[kHashLanes] = {};

@@ -14,8 +14,8 @@ namespace wexb {
 // records of the calls before it. Created once per device and never destroyed (CUDA cannot be called
 // while the process unloads). False on a CUDA failure.
 bool device_streams(int device, cudaStream_t *up, cudaStream_t *st, cudaStream_t *meta = nullptr);
-// The next of the device's 16 hash lanes (a stream and an event to record after its launch): one lane
-// per window of verified calls in flight, so that up to 16 windows (1,024 records) hash at once. False
+// The next of the device's 24 hash lanes (a stream and an event to record after its launch): one lane
+// per window of verified calls in flight, so that up to 24 windows (1,536 records) hash at once. False
 // on a CUDA failure.
 bool hash_lane(int device, cudaStream_t *hs, cudaEvent_t *hashed);
 
